@@ -1,0 +1,45 @@
+// strasgpt-b200 kernel-level entry points, for unit tests and for callers
+// that manage their own device buffers. All pointers are DEVICE pointers;
+// `stream` is a cudaStream_t (NULL: the legacy default stream). Each call
+// only enqueues work; it returns 0, or dies with "[StrasGPT] Error ..." on an
+// invalid shape. None of these has a counterpart in the reference API: they
+// expose the pieces of transformer_predict_chunk (source/transformer.c:
+// 1186-1602) one at a time.
+#ifndef STRASGPT_KERNELS_H
+#define STRASGPT_KERNELS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+// Epilogue selector shared by the projection entry points.
+#define STRASGPT_EPI_STORE  0  // out = W x
+#define STRASGPT_EPI_ADD    1  // out += W x (residual)
+#define STRASGPT_EPI_SWIGLU 2  // out = silu(gate) * up, rows interleaved by 16
+
+// y = W x for one token: W bf16 [rows][K] (rows of K contiguous), x fp32
+// [K]. norm_w (bf16 [K]) != NULL applies the reference RMSNorm to x first
+// (source/transformer.c:978-999). For STRASGPT_EPI_SWIGLU `rows` counts
+// outputs and W holds 2*rows rows, gate/up interleaved in groups of 16.
+int strasgpt_k_matvec(const float* x, const uint16_t* norm_w, float eps,
+                      const uint16_t* w, int k, int rows, float* out, int epi,
+                      void* stream);
+
+// C[m][n] (op)= sum_k A[m][k] W[n][k] for m < M, n < N (SIMT fp32 tiles).
+// For STRASGPT_EPI_SWIGLU, N counts weight rows and C has N/2 columns.
+int strasgpt_k_gemm_simt(const float* a, int lda, const uint16_t* w, int k,
+                         int m, int n, float* c, int ldc, int epi,
+                         void* stream);
+
+// y[t] = rmsnorm(x[t]) * w for t < T, rows of D floats.
+int strasgpt_k_rmsnorm_rows(const float* x, int t, int d, const uint16_t* w,
+                            float eps, float* y, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif // STRASGPT_KERNELS_H

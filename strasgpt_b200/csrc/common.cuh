@@ -1,0 +1,96 @@
+// Shared device helpers for the strasgpt-b200 kernels (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+
+#define SG_DIE(msg)                                                        \
+  do {                                                                     \
+    fprintf(stderr, "[StrasGPT] Error at %s:%d (%s): %s\n", __FILE__,      \
+            __LINE__, __func__, msg);                                      \
+    exit(EXIT_FAILURE);                                                    \
+  } while (0)
+
+#define SG_CUDA(call)                                                      \
+  do {                                                                     \
+    cudaError_t err_ = (call);                                             \
+    if (err_ != cudaSuccess) {                                             \
+      char m_[512];                                                        \
+      snprintf(m_, sizeof(m_), "CUDA error %s: %s", #call,                 \
+               cudaGetErrorString(err_));                                  \
+      SG_DIE(m_);                                                          \
+    }                                                                      \
+  } while (0)
+
+namespace sg {
+
+// bf16 stored as raw uint16_t everywhere: widening is a 16-bit shift
+// (the reference's util_bf16_to_f32, include/util.h:33-39).
+__device__ __forceinline__ float bf16_lo(uint32_t w) {
+  return __uint_as_float(w << 16);
+}
+__device__ __forceinline__ float bf16_hi(uint32_t w) {
+  return __uint_as_float(w & 0xFFFF0000u);
+}
+__device__ __forceinline__ float bf16_to_f32(uint16_t w) {
+  return __uint_as_float(((uint32_t)w) << 16);
+}
+
+// 128-bit streaming load that bypasses L1 (weights are read once per step).
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+    v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+  return v;
+}
+
+// Block-wide sum; every thread gets the result. `red` holds >= 32 floats.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nw = (blockDim.x + 31) >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = (lane < nw) ? red[lane] : 0.f;
+  t = warp_sum(t);
+  return t;
+}
+
+// Dot of 8 bf16 weights (one 16-byte vector) with 8 fp32 activations.
+__device__ __forceinline__ float dot8(uint4 w, float4 a, float4 b, float acc) {
+  acc = fmaf(bf16_lo(w.x), a.x, acc);
+  acc = fmaf(bf16_hi(w.x), a.y, acc);
+  acc = fmaf(bf16_lo(w.y), a.z, acc);
+  acc = fmaf(bf16_hi(w.y), a.w, acc);
+  acc = fmaf(bf16_lo(w.z), b.x, acc);
+  acc = fmaf(bf16_hi(w.z), b.y, acc);
+  acc = fmaf(bf16_lo(w.w), b.z, acc);
+  acc = fmaf(bf16_hi(w.w), b.w, acc);
+  return acc;
+}
+
+// SiLU-gated product, written as the reference does
+// (source/transformer.c:1481-1484): fc * (1 / (1 + expf(-fc))) * up.
+__device__ __forceinline__ float swiglu(float fc, float up) {
+  fc *= (1.0f / (1.0f + expf(-fc)));
+  return fc * up;
+}
+
+}  // namespace sg

@@ -1,0 +1,62 @@
+// Kernel-level C entry points (include/strasgpt_kernels.h).
+#include "common.cuh"
+#include "kernels.h"
+
+extern "C" {
+#include "strasgpt_kernels.h"
+}
+
+namespace {
+
+// cudaFuncSetAttribute is per device: configure each device once.
+void ensure_configured() {
+  static unsigned long long done = 0;
+  int dev = 0;
+  SG_CUDA(cudaGetDevice(&dev));
+  if (dev < 64 && !(done & (1ull << dev))) {
+    sg::configure_kernels();
+    done |= 1ull << dev;
+  }
+}
+
+sg::Epilogue epilogue(int epi) {
+  if (epi < 0 || epi > 2) SG_DIE("unknown epilogue");
+  return (sg::Epilogue)epi;
+}
+
+}  // namespace
+
+extern "C" {
+
+int strasgpt_k_matvec(const float* x, const uint16_t* norm_w, float eps,
+                      const uint16_t* w, int k, int rows, float* out, int epi,
+                      void* stream) {
+  ensure_configured();
+  if (k <= 0 || rows <= 0) SG_DIE("matvec: empty shape");
+  sg::matvec(x, norm_w, eps, w, k, rows, out, epilogue(epi),
+             (cudaStream_t)stream);
+  SG_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int strasgpt_k_gemm_simt(const float* a, int lda, const uint16_t* w, int k,
+                         int m, int n, float* c, int ldc, int epi,
+                         void* stream) {
+  ensure_configured();
+  if (k <= 0 || m <= 0 || n <= 0) SG_DIE("gemm: empty shape");
+  sg::gemm_simt(a, lda, w, k, m, n, c, ldc, epilogue(epi),
+                (cudaStream_t)stream);
+  SG_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int strasgpt_k_rmsnorm_rows(const float* x, int t, int d, const uint16_t* w,
+                            float eps, float* y, void* stream) {
+  ensure_configured();
+  if (t <= 0 || d <= 0) SG_DIE("rmsnorm: empty shape");
+  sg::rmsnorm_rows(x, t, d, w, eps, y, (cudaStream_t)stream);
+  SG_CUDA(cudaGetLastError());
+  return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,871 @@
+// Forward-pass kernels for sm_100a: embedding, RMSNorm, decode matvec,
+// SIMT projection tiles, q/k-norm + RoPE + KV append, decode and prefill
+// attention, greedy argmax, and the MXFP4 mixture-of-experts FFN.
+//
+// Arithmetic follows source/transformer.c of the reference: fp32
+// activations, bf16 weights widened exactly, fp32 accumulation, fp32 KV
+// cache, RMSNorm as x * (1/sqrtf(mean(x^2)+eps)) * w, scores divided by
+// sqrtf(head_dim), max-subtracted expf softmax, SwiGLU as
+// fc * (1/(1+expf(-fc))) * up. Summation order differs (parallel
+// reductions), which the parity tests bound.
+#include "common.cuh"
+#include "kernels.h"
+
+#include <math.h>
+
+namespace sg {
+
+// ---------------------------------------------------------------------------
+// Embedding gather (source/transformer.c:1247-1255)
+// ---------------------------------------------------------------------------
+__global__ void k_embed(const int* __restrict__ tok,
+                        const uint16_t* __restrict__ emb, int D,
+                        float* __restrict__ x) {
+  const int t = blockIdx.y;
+  const uint16_t* row = emb + (size_t)tok[t] * D;
+  float* xr = x + (size_t)t * D;
+  for (int e = (blockIdx.x * blockDim.x + threadIdx.x) * 8; e < D;
+       e += gridDim.x * blockDim.x * 8) {
+    uint4 w = *reinterpret_cast<const uint4*>(row + e);
+    *reinterpret_cast<float4*>(xr + e) =
+        make_float4(bf16_lo(w.x), bf16_hi(w.x), bf16_lo(w.y), bf16_hi(w.y));
+    *reinterpret_cast<float4*>(xr + e + 4) =
+        make_float4(bf16_lo(w.z), bf16_hi(w.z), bf16_lo(w.w), bf16_hi(w.w));
+  }
+}
+
+void embed(const int* tok, int T, const uint16_t* emb, int D, float* x,
+           cudaStream_t s) {
+  dim3 grid((D / 8 + 255) / 256, T);
+  k_embed<<<grid, 256, 0, s>>>(tok, emb, D, x);
+}
+
+// ---------------------------------------------------------------------------
+// Row RMSNorm (source/transformer.c:978-999)
+// ---------------------------------------------------------------------------
+__global__ void k_rmsnorm_rows(const float* __restrict__ x, int D,
+                               const uint16_t* __restrict__ w, float eps,
+                               float* __restrict__ y) {
+  __shared__ float red[32];
+  const float* xr = x + (size_t)blockIdx.x * D;
+  float* yr = y + (size_t)blockIdx.x * D;
+  float ss = 0.f;
+  for (int e = threadIdx.x; e < D; e += blockDim.x) ss += xr[e] * xr[e];
+  ss = block_sum(ss, red);
+  ss /= (float)D;
+  const float inv = 1.0f / sqrtf(ss + eps);
+  for (int e = threadIdx.x; e < D; e += blockDim.x)
+    yr[e] = (xr[e] * inv) * bf16_to_f32(w[e]);
+}
+
+void rmsnorm_rows(const float* x, int T, int D, const uint16_t* w, float eps,
+                  float* y, cudaStream_t s) {
+  k_rmsnorm_rows<<<T, 256, 0, s>>>(x, D, w, eps, y);
+}
+
+// ---------------------------------------------------------------------------
+// Decode matvec: one warp streams two weight rows with 128-bit no-L1 loads,
+// four vectors deep per row; the activation vector sits in shared memory in
+// a split layout (elements k..k+3 of every 8-group in one array, k+4..k+7
+// in another) so that each lane's two float4 reads are bank-conflict free.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int xs_split_index(int k, int K) {
+  // element k -> [half][k/8][k%4], half = (k/4)&1
+  return (((k >> 2) & 1) * (K >> 1)) + ((k >> 3) << 2) + (k & 3);
+}
+
+template <int EPI, bool NORM>
+__global__ void __launch_bounds__(256)
+    k_matvec(const float* __restrict__ x, const uint16_t* __restrict__ nw,
+             float eps, const uint16_t* __restrict__ W, int K, int items,
+             int rows, float* __restrict__ out) {
+  extern __shared__ float4 xs4[];
+  float* xs = reinterpret_cast<float*>(xs4);
+  __shared__ float red[32];
+  const int tid = threadIdx.x;
+  if (NORM) {
+    float ss = 0.f;
+    for (int k = tid; k < K; k += blockDim.x) {
+      float v = x[k];
+      ss += v * v;
+    }
+    ss = block_sum(ss, red);
+    ss /= (float)K;
+    const float inv = 1.0f / sqrtf(ss + eps);
+    for (int k = tid; k < K; k += blockDim.x)
+      xs[xs_split_index(k, K)] = (x[k] * inv) * bf16_to_f32(nw[k]);
+  } else {
+    for (int k = tid; k < K; k += blockDim.x) xs[xs_split_index(k, K)] = x[k];
+  }
+  __syncthreads();
+
+  const float4* lo4 = xs4;            // elements 8j..8j+3
+  const float4* hi4 = xs4 + (K >> 3); // elements 8j+4..8j+7
+  const int lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  constexpr int U = 4;
+  for (int item = blockIdx.x * nwarps + warp; item < items;
+       item += gridDim.x * nwarps) {
+    int r0, r1;
+    if (EPI == EPI_SWIGLU) {
+      r0 = (item / SG_GU_GROUP) * (2 * SG_GU_GROUP) + item % SG_GU_GROUP;
+      r1 = r0 + SG_GU_GROUP;
+    } else {
+      r0 = 2 * item;
+      r1 = r0 + 1;
+    }
+    const bool has1 = r1 < rows;
+    const uint16_t* w0 = W + (size_t)r0 * K;
+    const uint16_t* w1 = W + (size_t)(has1 ? r1 : r0) * K;
+    float a0 = 0.f, a1 = 0.f;
+    for (int kb = lane * 8; kb < K; kb += 256 * U) {
+      uint4 v0[U], v1[U];
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        const int k = kb + u * 256;
+        if (k < K) {
+          v0[u] = ldg_stream(w0 + k);
+          v1[u] = ldg_stream(w1 + k);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        const int k = kb + u * 256;
+        if (k < K) {
+          const float4 xa = lo4[k >> 3], xb = hi4[k >> 3];
+          a0 = dot8(v0[u], xa, xb, a0);
+          a1 = dot8(v1[u], xa, xb, a1);
+        }
+      }
+    }
+    a0 = warp_sum(a0);
+    a1 = warp_sum(a1);
+    if (lane == 0) {
+      if (EPI == EPI_SWIGLU) {
+        out[item] = swiglu(a0, a1);
+      } else if (EPI == EPI_STORE) {
+        out[r0] = a0;
+        if (has1) out[r1] = a1;
+      } else {
+        out[r0] += a0;
+        if (has1) out[r1] += a1;
+      }
+    }
+  }
+}
+
+static int g_num_sms = 0;
+static int num_sms() {
+  if (!g_num_sms) {
+    int dev;
+    SG_CUDA(cudaGetDevice(&dev));
+    SG_CUDA(cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount,
+                                   dev));
+  }
+  return g_num_sms;
+}
+
+template <int EPI, bool NORM>
+static void launch_matvec(const float* x, const uint16_t* nw, float eps,
+                          const uint16_t* W, int K, int rows, float* out,
+                          cudaStream_t s) {
+  const int items = (EPI == EPI_SWIGLU) ? rows : (rows + 1) / 2;
+  const int warps = 8;
+  int blocks = (items + warps - 1) / warps;
+  const size_t smem = (size_t)K * sizeof(float);
+  if (smem > 200 * 1024) SG_DIE("matvec: K too large for shared memory");
+  // Enough CTAs to cover every SM several times; the rest grid-stride.
+  const int cap = num_sms() * 16;
+  if (blocks > cap) blocks = cap;
+  k_matvec<EPI, NORM><<<blocks, warps * 32, smem, s>>>(x, nw, eps, W, K,
+                                                       items, rows, out);
+}
+
+void matvec(const float* x, const uint16_t* norm_w, float eps,
+            const uint16_t* W, int K, int rows, float* out, Epilogue epi,
+            cudaStream_t s) {
+  if (K % 8 != 0) SG_DIE("matvec: K must be a multiple of 8");
+  if (epi == EPI_SWIGLU && rows % SG_GU_GROUP != 0)
+    SG_DIE("matvec: swiglu outputs must be a multiple of the group");
+  if (norm_w) {
+    if (epi == EPI_STORE)
+      launch_matvec<EPI_STORE, true>(x, norm_w, eps, W, K, rows, out, s);
+    else if (epi == EPI_ADD)
+      launch_matvec<EPI_ADD, true>(x, norm_w, eps, W, K, rows, out, s);
+    else
+      launch_matvec<EPI_SWIGLU, true>(x, norm_w, eps, W, K, rows, out, s);
+  } else {
+    if (epi == EPI_STORE)
+      launch_matvec<EPI_STORE, false>(x, norm_w, eps, W, K, rows, out, s);
+    else if (epi == EPI_ADD)
+      launch_matvec<EPI_ADD, false>(x, norm_w, eps, W, K, rows, out, s);
+    else
+      launch_matvec<EPI_SWIGLU, false>(x, norm_w, eps, W, K, rows, out, s);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// SIMT projection tiles for multi-token chunks: 64 tokens x 64 weight rows
+// per CTA, 32-deep k steps, 4x4 outputs per thread, fp32 accumulation.
+// ---------------------------------------------------------------------------
+template <int EPI>
+__global__ void __launch_bounds__(256)
+    k_gemm_simt(const float* __restrict__ A, int lda,
+                const uint16_t* __restrict__ W, int K, int M, int N,
+                float* __restrict__ C, int ldc) {
+  __shared__ float smem[64 * 65];
+  float* As = smem;            // [32][65]  k-major
+  float* Ws = smem + 32 * 65;  // [32][65]
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  float acc[4][4] = {};
+  const int lr = tid >> 2, lc = (tid & 3) * 8;
+  for (int k0 = 0; k0 < K; k0 += 32) {
+    {
+      const int m = m0 + lr;
+      float4 a0 = make_float4(0, 0, 0, 0), a1 = a0;
+      if (m < M) {
+        const float* ap = A + (size_t)m * lda + k0 + lc;
+        a0 = *reinterpret_cast<const float4*>(ap);
+        a1 = *reinterpret_cast<const float4*>(ap + 4);
+      }
+      As[(lc + 0) * 65 + lr] = a0.x;
+      As[(lc + 1) * 65 + lr] = a0.y;
+      As[(lc + 2) * 65 + lr] = a0.z;
+      As[(lc + 3) * 65 + lr] = a0.w;
+      As[(lc + 4) * 65 + lr] = a1.x;
+      As[(lc + 5) * 65 + lr] = a1.y;
+      As[(lc + 6) * 65 + lr] = a1.z;
+      As[(lc + 7) * 65 + lr] = a1.w;
+      const int n = n0 + lr;
+      uint4 w = make_uint4(0, 0, 0, 0);
+      if (n < N) w = ldg_stream(W + (size_t)n * K + k0 + lc);
+      Ws[(lc + 0) * 65 + lr] = bf16_lo(w.x);
+      Ws[(lc + 1) * 65 + lr] = bf16_hi(w.x);
+      Ws[(lc + 2) * 65 + lr] = bf16_lo(w.y);
+      Ws[(lc + 3) * 65 + lr] = bf16_hi(w.y);
+      Ws[(lc + 4) * 65 + lr] = bf16_lo(w.z);
+      Ws[(lc + 5) * 65 + lr] = bf16_hi(w.z);
+      Ws[(lc + 6) * 65 + lr] = bf16_lo(w.w);
+      Ws[(lc + 7) * 65 + lr] = bf16_hi(w.w);
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int k = 0; k < 32; k++) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        a[i] = As[k * 65 + ty * 4 + i];
+        b[i] = Ws[k * 65 + tx * 4 + i];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+  if (EPI == EPI_SWIGLU) {
+    // Stage the 64x64 tile, then pair gate/up columns of each 32-group.
+    float* Cs = smem;  // [64][65]
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+      for (int j = 0; j < 4; j++) Cs[(ty * 4 + i) * 65 + tx * 4 + j] = acc[i][j];
+    __syncthreads();
+    for (int e = tid; e < 64 * 32; e += 256) {
+      const int r = e >> 5, o = e & 31;
+      const int m = m0 + r;
+      const int gcol = (o / SG_GU_GROUP) * (2 * SG_GU_GROUP) + o % SG_GU_GROUP;
+      const int out_col = n0 / 2 + o;
+      if (m < M && n0 + gcol + SG_GU_GROUP < N + 1)
+        C[(size_t)m * ldc + out_col] =
+            swiglu(Cs[r * 65 + gcol], Cs[r * 65 + gcol + SG_GU_GROUP]);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int m = m0 + ty * 4 + i;
+      if (m >= M) continue;
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int n = n0 + tx * 4 + j;
+        if (n >= N) continue;
+        float* c = C + (size_t)m * ldc + n;
+        if (EPI == EPI_STORE)
+          *c = acc[i][j];
+        else
+          *c += acc[i][j];
+      }
+    }
+  }
+}
+
+void gemm_simt(const float* A, int lda, const uint16_t* W, int K, int M,
+               int N, float* C, int ldc, Epilogue epi, cudaStream_t s) {
+  if (K % 32 != 0) SG_DIE("gemm: K must be a multiple of 32");
+  if (epi == EPI_SWIGLU && N % 64 != 0)
+    SG_DIE("gemm: swiglu weight rows must be a multiple of 64");
+  dim3 grid((N + 63) / 64, (M + 63) / 64);
+  if (epi == EPI_STORE)
+    k_gemm_simt<EPI_STORE><<<grid, 256, 0, s>>>(A, lda, W, K, M, N, C, ldc);
+  else if (epi == EPI_ADD)
+    k_gemm_simt<EPI_ADD><<<grid, 256, 0, s>>>(A, lda, W, K, M, N, C, ldc);
+  else
+    k_gemm_simt<EPI_SWIGLU><<<grid, 256, 0, s>>>(A, lda, W, K, M, N, C, ldc);
+}
+
+// ---------------------------------------------------------------------------
+// q/k per-head RMSNorm + RoPE + KV-cache append
+// (source/transformer.c:1271-1373). One CTA per (head, token), HD threads.
+// ---------------------------------------------------------------------------
+__global__ void k_qkv_post(QkvPostArgs a) {
+  __shared__ float v[256];
+  __shared__ float red[32];
+  const int head = blockIdx.x, t = blockIdx.y, i = threadIdx.x, HD = a.HD;
+  const int pos = *a.pos + t;
+  const int ld = (a.QHl + 2 * a.KHl) * HD;
+  const float* row = a.qkv + (size_t)t * ld;
+  const bool is_q = head < a.QHl;
+  const uint16_t* nw = is_q ? a.q_norm : a.k_norm;
+  float val = row[head * HD + i];
+  if (nw) {
+    float ss = block_sum(val * val, red);
+    ss /= (float)HD;
+    const float inv = 1.0f / sqrtf(ss + a.eps);
+    val = (val * inv) * bf16_to_f32(nw[i]);
+  }
+  v[i] = val;
+  __syncthreads();
+  const float* cs = a.rope + (size_t)pos * HD;
+  const int off = a.pair_offset;
+  bool first;
+  if (a.pair_stride == 1)
+    first = i < a.pair_bound;
+  else
+    first = (i & 1) == 0;
+  float o;
+  if (first) {
+    const float fr = cs[i], fi = cs[i + off];
+    o = v[i] * fr - v[i + off] * fi;
+  } else {
+    const int h = i - off;
+    const float fr = cs[h], fi = cs[h + off];
+    o = v[h] * fi + v[i] * fr;
+  }
+  if (is_q) {
+    a.q[((size_t)t * a.QHl + head) * HD + i] = o;
+  } else {
+    const int kh = head - a.QHl;
+    const size_t dst = ((size_t)kh * a.ctx + pos) * HD + i;
+    a.k_cache[dst] = o;
+    a.v_cache[dst] = row[(a.QHl + a.KHl + kh) * HD + i];
+  }
+}
+
+void qkv_post(const QkvPostArgs& a, cudaStream_t s) {
+  if (a.HD > 256 || a.HD % 32 != 0) SG_DIE("qkv_post: unsupported head_dim");
+  dim3 grid(a.QHl + a.KHl, a.T);
+  k_qkv_post<<<grid, a.HD, 0, s>>>(a);
+}
+
+// ---------------------------------------------------------------------------
+// Decode attention: grid (kv head, split). Each warp walks positions of the
+// split with an online softmax for the G query heads of the group; the CTA
+// merges its warps, writes a partial, and the last CTA of the kv head (by
+// ticket) merges the splits into att.
+// ---------------------------------------------------------------------------
+template <int HD, int G>
+__global__ void __launch_bounds__(128) k_attn_decode(AttnDecodeArgs a) {
+  constexpr int V = HD / 32;
+  constexpr int NW = 4;
+  __shared__ float qs[G * HD];
+  __shared__ float wm[NW][G], wl[NW][G];
+  __shared__ float wacc[NW][G][HD];
+  __shared__ bool is_last;
+  const int kh = blockIdx.x, sp = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int len = *a.pos + 1;
+  const int s0 = sp * a.split_len;
+  const int s1 = min(s0 + a.split_len, len);
+  for (int i = tid; i < G * HD; i += blockDim.x)
+    qs[i] = a.q[(size_t)kh * G * HD + i];
+  __syncthreads();
+
+  float m[G], l[G], acc[G][V];
+#pragma unroll
+  for (int g = 0; g < G; g++) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; i++) acc[g][i] = 0.f;
+  }
+  const float div = sqrtf((float)HD);
+  const float* kb = a.k_cache + (size_t)kh * a.ctx * HD;
+  const float* vb = a.v_cache + (size_t)kh * a.ctx * HD;
+  for (int s = s0 + warp; s < s1; s += NW) {
+    float kv[V], vv[V];
+#pragma unroll
+    for (int i = 0; i < V; i++) kv[i] = kb[(size_t)s * HD + lane * V + i];
+#pragma unroll
+    for (int i = 0; i < V; i++) vv[i] = vb[(size_t)s * HD + lane * V + i];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+      float d = 0.f;
+#pragma unroll
+      for (int i = 0; i < V; i++) d = fmaf(qs[g * HD + lane * V + i], kv[i], d);
+      d = warp_sum(d);
+      const float sc = d / div;
+      const float mn = fmaxf(m[g], sc);
+      const float corr = expf(m[g] - mn);
+      const float p = expf(sc - mn);
+      l[g] = l[g] * corr + p;
+#pragma unroll
+      for (int i = 0; i < V; i++) acc[g][i] = fmaf(p, vv[i], acc[g][i] * corr);
+      m[g] = mn;
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < G; g++) {
+    if (lane == 0) {
+      wm[warp][g] = m[g];
+      wl[warp][g] = l[g];
+    }
+#pragma unroll
+    for (int i = 0; i < V; i++) wacc[warp][g][lane * V + i] = acc[g][i];
+  }
+  __syncthreads();
+  const int nsplit = a.nsplit;
+  for (int e = tid; e < G * HD; e += blockDim.x) {
+    const int g = e / HD, d = e % HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; w++) M = fmaxf(M, wm[w][g]);
+    float L = 0.f, A = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < NW; w++) {
+        if (wm[w][g] == -INFINITY) continue;
+        const float c = expf(wm[w][g] - M);
+        L += wl[w][g] * c;
+        A += wacc[w][g][d] * c;
+      }
+    }
+    float* P = a.partial + ((size_t)(kh * G + g) * nsplit + sp) * (HD + 2);
+    if (d == 0) {
+      P[0] = M;
+      P[1] = L;
+    }
+    P[2 + d] = A;
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const int t = atomicAdd(&a.ticket[kh], 1);
+    is_last = (t == nsplit - 1);
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  for (int e = tid; e < G * HD; e += blockDim.x) {
+    const int g = e / HD, d = e % HD;
+    const float* P0 = a.partial + (size_t)(kh * G + g) * nsplit * (HD + 2);
+    float M = -INFINITY;
+    for (int j = 0; j < nsplit; j++) M = fmaxf(M, __ldcg(P0 + j * (HD + 2)));
+    float L = 0.f, A = 0.f;
+    for (int j = 0; j < nsplit; j++) {
+      const float mj = __ldcg(P0 + j * (HD + 2));
+      if (mj == -INFINITY) continue;
+      const float c = expf(mj - M);
+      L += __ldcg(P0 + j * (HD + 2) + 1) * c;
+      A += __ldcg(P0 + j * (HD + 2) + 2 + d) * c;
+    }
+    a.att[(size_t)(kh * G + g) * HD + d] = A / L;
+  }
+  if (tid == 0) a.ticket[kh] = 0;
+}
+
+template <int HD>
+static void attn_decode_hd(const AttnDecodeArgs& a, cudaStream_t s) {
+  dim3 grid(a.KHl, a.nsplit);
+  switch (a.G) {
+    case 1: k_attn_decode<HD, 1><<<grid, 128, 0, s>>>(a); break;
+    case 2: k_attn_decode<HD, 2><<<grid, 128, 0, s>>>(a); break;
+    case 4: k_attn_decode<HD, 4><<<grid, 128, 0, s>>>(a); break;
+    case 8: k_attn_decode<HD, 8><<<grid, 128, 0, s>>>(a); break;
+    default: SG_DIE("attn_decode: unsupported GQA group size");
+  }
+}
+
+void attn_decode(const AttnDecodeArgs& a, cudaStream_t s) {
+  if (a.HD == 64)
+    attn_decode_hd<64>(a, s);
+  else if (a.HD == 128)
+    attn_decode_hd<128>(a, s);
+  else if (a.HD == 32)
+    attn_decode_hd<32>(a, s);
+  else
+    SG_DIE("attn_decode: unsupported head_dim");
+}
+
+// ---------------------------------------------------------------------------
+// Prefill attention: CTA = (q head, 32-token tile); 8 warps x 4 queries.
+// K/V tiles of 32 cache rows are staged in shared memory; lane j scores key
+// j, the warp runs an online softmax and accumulates P.V.
+// ---------------------------------------------------------------------------
+template <int HD>
+__global__ void __launch_bounds__(256) k_attn_prefill(AttnPrefillArgs a) {
+  constexpr int V = HD / 32, QT = 32, KT = 32, QW = 4;
+  extern __shared__ float sm[];
+  float* qs = sm;                  // [QT][HD]
+  float* ks = qs + QT * HD;        // [KT][HD+1]
+  float* vs = ks + KT * (HD + 1);  // [KT][HD]
+  const int qh = blockIdx.x, kh = qh / a.G, QHl = a.KHl * a.G;
+  const int tq0 = blockIdx.y * QT;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tq1 = min(tq0 + QT, a.T);
+  for (int e = tid; e < QT * HD; e += blockDim.x) {
+    const int r = e / HD, d = e % HD, t = tq0 + r;
+    qs[e] = (t < a.T) ? a.q[((size_t)t * QHl + qh) * HD + d] : 0.f;
+  }
+  float m[QW], l[QW], acc[QW][V];
+#pragma unroll
+  for (int j = 0; j < QW; j++) {
+    m[j] = -INFINITY;
+    l[j] = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; i++) acc[j][i] = 0.f;
+  }
+  const float div = sqrtf((float)HD);
+  const int kmax = a.pos0 + tq1 - 1;
+  const float* kb = a.k_cache + (size_t)kh * a.ctx * HD;
+  const float* vb = a.v_cache + (size_t)kh * a.ctx * HD;
+  for (int kt0 = 0; kt0 <= kmax; kt0 += KT) {
+    __syncthreads();
+    for (int e = tid; e < KT * HD; e += blockDim.x) {
+      const int r = e / HD, d = e % HD, sidx = kt0 + r;
+      const bool ok = sidx <= kmax;
+      ks[r * (HD + 1) + d] = ok ? kb[(size_t)sidx * HD + d] : 0.f;
+      vs[r * HD + d] = ok ? vb[(size_t)sidx * HD + d] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < QW; j++) {
+      const int r = warp * QW + j, t = tq0 + r;
+      if (t >= a.T) continue;
+      const int pt = a.pos0 + t;
+      if (kt0 > pt) continue;
+      const int sidx = kt0 + lane;
+      const bool valid = sidx <= pt;
+      float sc = -INFINITY;
+      if (valid) {
+        float d = 0.f;
+#pragma unroll 16
+        for (int i = 0; i < HD; i++) d = fmaf(qs[r * HD + i], ks[lane * (HD + 1) + i], d);
+        sc = d / div;
+      }
+      const float mn = fmaxf(m[j], warp_max(sc));
+      const float corr = expf(m[j] - mn);
+      const float p = valid ? expf(sc - mn) : 0.f;
+      l[j] = l[j] * corr + warp_sum(p);
+#pragma unroll
+      for (int i = 0; i < V; i++) acc[j][i] *= corr;
+      for (int jj = 0; jj < 32; jj++) {
+        const float pj = __shfl_sync(0xFFFFFFFFu, p, jj);
+#pragma unroll
+        for (int i = 0; i < V; i++)
+          acc[j][i] = fmaf(pj, vs[jj * HD + lane + 32 * i], acc[j][i]);
+      }
+      m[j] = mn;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < QW; j++) {
+    const int t = tq0 + warp * QW + j;
+    if (t >= a.T) continue;
+#pragma unroll
+    for (int i = 0; i < V; i++)
+      a.att[((size_t)t * QHl + qh) * HD + lane + 32 * i] = acc[j][i] / l[j];
+  }
+}
+
+template <int HD>
+static void attn_prefill_hd(const AttnPrefillArgs& a, cudaStream_t s) {
+  const size_t smem = (size_t)(32 * HD + 32 * (HD + 1) + 32 * HD) * 4;
+  dim3 grid(a.KHl * a.G, (a.T + 31) / 32);
+  k_attn_prefill<HD><<<grid, 256, smem, s>>>(a);
+}
+
+void attn_prefill(const AttnPrefillArgs& a, cudaStream_t s) {
+  if (a.HD == 64)
+    attn_prefill_hd<64>(a, s);
+  else if (a.HD == 128)
+    attn_prefill_hd<128>(a, s);
+  else if (a.HD == 32)
+    attn_prefill_hd<32>(a, s);
+  else
+    SG_DIE("attn_prefill: unsupported head_dim");
+}
+
+// ---------------------------------------------------------------------------
+// Greedy argmax + position advance (device-resident decode loop).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void argmax_merge(float& v, int& i, float v2,
+                                             int i2) {
+  if (v2 > v || (v2 == v && i2 < i)) {
+    v = v2;
+    i = i2;
+  }
+}
+
+__global__ void __launch_bounds__(512)
+    k_argmax(const float* __restrict__ logits, int n, int* out_token, int* pos,
+             int* step, int* tokens_out, float* pval, int* pidx, int* ticket) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  __shared__ bool is_last;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float best = -INFINITY;
+  int bi = 0x7FFFFFFF;
+  for (int i = blockIdx.x * blockDim.x + tid; i < n; i += gridDim.x * blockDim.x) {
+    const float v = logits[i];
+    if (v > best) {  // strictly greater: first index wins within a thread
+      best = v;
+      bi = i;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const float v2 = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+    const int i2 = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+    argmax_merge(best, bi, v2, i2);
+  }
+  if (lane == 0) {
+    sv[warp] = best;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); w++) argmax_merge(best, bi, sv[w], si[w]);
+    pval[blockIdx.x] = best;
+    pidx[blockIdx.x] = bi;
+    __threadfence();
+    is_last = (atomicAdd(ticket, 1) == (int)gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!is_last || tid != 0) return;
+  __threadfence();
+  float v = __ldcg(pval);
+  int idx = __ldcg(pidx);
+  for (int b = 1; b < (int)gridDim.x; b++)
+    argmax_merge(v, idx, __ldcg(pval + b), __ldcg(pidx + b));
+  if (idx == 0x7FFFFFFF) idx = 0;  // all NaN: the reference returns 0
+  *out_token = idx;
+  if (tokens_out) tokens_out[*step] = idx;
+  *step += 1;
+  if (pos) *pos += 1;
+  *ticket = 0;
+}
+
+void argmax_advance(const float* logits, int n, int* out_token, int* pos,
+                    int* step, int* tokens_out, float* partial_val,
+                    int* partial_idx, int* ticket, cudaStream_t s) {
+  int blocks = (n + 4095) / 4096;
+  if (blocks > 64) blocks = 64;
+  if (blocks < 1) blocks = 1;
+  k_argmax<<<blocks, 512, 0, s>>>(logits, n, out_token, pos, step, tokens_out,
+                                  partial_val, partial_idx, ticket);
+}
+
+// ---------------------------------------------------------------------------
+// Mixture of experts with MXFP4 weights.
+// ---------------------------------------------------------------------------
+__global__ void k_moe_topk(const float* __restrict__ r, int E, int k,
+                           int* __restrict__ idx, float* __restrict__ w) {
+  // one warp per token; E <= 256
+  const int t = blockIdx.x, lane = threadIdx.x;
+  float v[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const int e = lane + 32 * j;
+    v[j] = (e < E) ? r[(size_t)t * E + e] : -INFINITY;
+  }
+  float sel[16];
+  int seli[16];
+  for (int s = 0; s < k; s++) {
+    float best = -INFINITY;
+    int bi = 0x7FFFFFFF;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const int e = lane + 32 * j;
+      if (e < E) argmax_merge(best, bi, v[j], e);
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      const float v2 = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+      const int i2 = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+      argmax_merge(best, bi, v2, i2);
+    }
+    sel[s] = best;
+    seli[s] = bi;
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+      if (lane + 32 * j == bi) v[j] = -INFINITY;
+  }
+  if (lane == 0) {
+    const float mx = sel[0];
+    float sum = 0.f;
+    float e[16];
+    for (int s = 0; s < k; s++) {
+      e[s] = expf(sel[s] - mx);
+      sum += e[s];
+    }
+    for (int s = 0; s < k; s++) {
+      idx[t * k + s] = seli[s];
+      w[t * k + s] = e[s] / sum;
+    }
+  }
+}
+
+void moe_topk(const float* router_logits, int T, int E, int k, int* idx,
+              float* weight, cudaStream_t s) {
+  if (E > 256 || k > 16 || k > E) SG_DIE("moe_topk: unsupported E/k");
+  k_moe_topk<<<T, 32, 0, s>>>(router_logits, E, k, idx, weight);
+}
+
+__device__ __forceinline__ float e8m0_scale(uint32_t e) {
+  return e == 0 ? __uint_as_float(0x00400000u) : __uint_as_float(e << 23);
+}
+
+// Dot of one MXFP4 block (16 bytes = 32 codes, low nibble first) with 32
+// activations at xs[0..31] (shared memory), times the block scale.
+__device__ __forceinline__ float mxfp4_block_dot(uint4 c, const float* xs,
+                                                 const float* lut) {
+  const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+  float acc = 0.f;
+#pragma unroll
+  for (int q = 0; q < 4; q++) {
+#pragma unroll
+    for (int b = 0; b < 8; b++) {
+      const uint32_t code = (w[q] >> (4 * b)) & 0xF;
+      acc = fmaf(lut[code], xs[q * 8 + b], acc);
+    }
+  }
+  return acc;
+}
+
+__constant__ float kE2M1[16] = {0.0f,  0.5f,  1.0f,  1.5f,  2.0f,  3.0f,
+                                4.0f,  6.0f,  -0.0f, -0.5f, -1.0f, -1.5f,
+                                -2.0f, -3.0f, -4.0f, -6.0f};
+
+// Activations are stored with one pad float per 32-block so that lanes
+// reading different blocks hit different banks.
+__host__ __device__ __forceinline__ int pad32(int k) { return k + (k >> 5); }
+
+__global__ void __launch_bounds__(256) k_moe_gate_up(MoeArgs a) {
+  extern __shared__ float xs[];
+  __shared__ float lut[16];
+  const int tj = blockIdx.x, t = tj / a.k;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int e = a.idx[tj];
+  const int fbeg = blockIdx.y * 64, fend = min(fbeg + 64, a.F);
+  float* h = a.h + (size_t)tj * a.F;
+  if (e < a.e_begin || e >= a.e_end) {
+    for (int f = fbeg + tid; f < fend; f += blockDim.x) h[f] = 0.f;
+    return;
+  }
+  if (tid < 16) lut[tid] = kE2M1[tid];
+  for (int kk = tid; kk < a.D; kk += blockDim.x)
+    xs[pad32(kk)] = a.xn[(size_t)t * a.D + kk];
+  __syncthreads();
+  const int nb = a.D / 32;
+  const size_t el = (size_t)(e - a.e_begin);
+  for (int f = fbeg + warp; f < fend; f += 8) {
+    const size_t row = el * a.F + f;
+    const uint8_t* gc = a.gate_codes + row * nb * 16;
+    const uint8_t* uc = a.up_codes + row * nb * 16;
+    const uint8_t* gs = a.gate_scales + row * nb;
+    const uint8_t* us = a.up_scales + row * nb;
+    float g = 0.f, u = 0.f;
+    for (int b = lane; b < nb; b += 32) {
+      const uint4 cg = ldg_stream(gc + (size_t)b * 16);
+      const uint4 cu = ldg_stream(uc + (size_t)b * 16);
+      const float* xb = xs + b * 33;
+      g = fmaf(mxfp4_block_dot(cg, xb, lut), e8m0_scale(gs[b]), g);
+      u = fmaf(mxfp4_block_dot(cu, xb, lut), e8m0_scale(us[b]), u);
+    }
+    g = warp_sum(g);
+    u = warp_sum(u);
+    if (lane == 0) h[f] = swiglu(g, u);
+  }
+}
+
+__global__ void __launch_bounds__(256) k_moe_down(MoeArgs a) {
+  extern __shared__ float hs[];  // [k][pad32(F)]
+  __shared__ float lut[16];
+  const int t = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int Fp = pad32(a.F);
+  if (tid < 16) lut[tid] = kE2M1[tid];
+  for (int e = tid; e < a.k * a.F; e += blockDim.x) {
+    const int j = e / a.F, f = e % a.F;
+    hs[j * Fp + pad32(f)] = a.h[((size_t)t * a.k + j) * a.F + f];
+  }
+  __syncthreads();
+  const int nb = a.F / 32;
+  const int rbeg = blockIdx.y * 64, rend = min(rbeg + 64, a.D);
+  for (int r = rbeg + warp; r < rend; r += 8) {
+    float y = 0.f;
+    for (int j = 0; j < a.k; j++) {
+      const int e = a.idx[t * a.k + j];
+      if (e < a.e_begin || e >= a.e_end) continue;
+      const size_t row = (size_t)(e - a.e_begin) * a.D + r;
+      const uint8_t* dc = a.down_codes + row * nb * 16;
+      const uint8_t* ds = a.down_scales + row * nb;
+      float acc = 0.f;
+      for (int b = lane; b < nb; b += 32) {
+        const uint4 c = ldg_stream(dc + (size_t)b * 16);
+        acc = fmaf(mxfp4_block_dot(c, hs + j * Fp + b * 33, lut),
+                   e8m0_scale(ds[b]), acc);
+      }
+      acc = warp_sum(acc);
+      y = fmaf(a.weight[t * a.k + j], acc, y);
+    }
+    if (lane == 0) a.out[(size_t)t * a.D + r] += y;
+  }
+}
+
+void moe_gate_up(const MoeArgs& a, cudaStream_t s) {
+  if (a.D % 32 || a.F % 32) SG_DIE("moe: dims must be multiples of 32");
+  const size_t smem = (size_t)pad32(a.D) * 4;
+  dim3 grid(a.T * a.k, (a.F + 63) / 64);
+  k_moe_gate_up<<<grid, 256, smem, s>>>(a);
+}
+
+void moe_down(const MoeArgs& a, cudaStream_t s) {
+  const size_t smem = (size_t)a.k * pad32(a.F) * 4;
+  if (smem > 200 * 1024) SG_DIE("moe_down: k * F too large");
+  dim3 grid(a.T, (a.D + 63) / 64);
+  k_moe_down<<<grid, 256, smem, s>>>(a);
+}
+
+// Raise the dynamic shared-memory limit of every kernel that needs more
+// than 48 KB. Called once per device before any launch (and before any
+// stream capture).
+void configure_kernels() {
+  const int big = 200 * 1024;
+#define SG_SMEM(fn) \
+  SG_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, big))
+  SG_SMEM((k_matvec<EPI_STORE, true>));
+  SG_SMEM((k_matvec<EPI_ADD, true>));
+  SG_SMEM((k_matvec<EPI_SWIGLU, true>));
+  SG_SMEM((k_matvec<EPI_STORE, false>));
+  SG_SMEM((k_matvec<EPI_ADD, false>));
+  SG_SMEM((k_matvec<EPI_SWIGLU, false>));
+  SG_SMEM(k_attn_prefill<32>);
+  SG_SMEM(k_attn_prefill<64>);
+  SG_SMEM(k_attn_prefill<128>);
+  SG_SMEM(k_moe_gate_up);
+  SG_SMEM(k_moe_down);
+#undef SG_SMEM
+  num_sms();
+}
+
+}  // namespace sg

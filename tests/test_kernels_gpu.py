@@ -1,0 +1,133 @@
+"""Kernel-level numerics through the C entry points of
+include/strasgpt_kernels.h, against a float64 torch reference of the same op
+(the reference's fp32 matvec/rmsnorm math, source/transformer.c:978-999,
+1038-1180). Tolerance: relative 1e-5 of the output scale (fp32 accumulation
+in a different order)."""
+import numpy as np
+import pytest
+
+from strasgpt_b200 import runtime
+
+STORE, ADD, SWIGLU = 0, 1, 2
+
+
+def bf16_from_f32(t):
+    import torch
+    return t.to(torch.bfloat16).view(torch.int16)
+
+
+def f32_from_bf16(w):
+    import torch
+    return w.view(torch.bfloat16).to(torch.float64)
+
+
+def ref_rmsnorm(x, w, eps):
+    import torch
+    x = x.to(torch.float64)
+    ss = (x * x).mean(dim=-1, keepdim=True)
+    return x / torch.sqrt(ss + eps) * f32_from_bf16(w)
+
+
+def ref_swiglu(g, u):
+    import torch
+    return g * torch.sigmoid(g) * u
+
+
+def interleave_gate_up(gate, up):
+    """[F][K] gate and up -> [2F][K] in groups of 16 rows (g, u, g, u...)."""
+    import torch
+    F, K = gate.shape
+    return torch.stack([gate.view(F // 16, 16, K), up.view(F // 16, 16, K)],
+                       dim=1).reshape(2 * F, K).contiguous()
+
+
+def close(got, want, what):
+    got = got.to(want.dtype)
+    scale = want.abs().max().item() + 1e-30
+    err = (got - want).abs().max().item()
+    assert err <= 1e-5 * scale + 1e-6, f"{what}: err {err:.3e} scale {scale:.3e}"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("rows,k", [(1, 32), (7, 256), (4096, 1024), (1024, 2048),
+                                    (130, 8200), (3, 49152)])
+@pytest.mark.parametrize("epi", [STORE, ADD])
+@pytest.mark.parametrize("norm", [False, True])
+def test_matvec(cuda, rows, k, epi, norm):
+    torch = cuda
+    g = torch.Generator(device="cuda").manual_seed(rows * 31 + k)
+    x = torch.randn(k, device="cuda", generator=g)
+    w = bf16_from_f32(torch.randn(rows, k, device="cuda", generator=g) * 0.02)
+    nw = bf16_from_f32(1 + 0.1 * torch.randn(k, device="cuda", generator=g))
+    out = torch.randn(rows, device="cuda", generator=g)
+    base = out.clone().to(torch.float64)
+    L = runtime.lib()
+    L.strasgpt_k_matvec(x.data_ptr(), nw.data_ptr() if norm else None, 1e-5,
+                        w.data_ptr(), k, rows, out.data_ptr(), epi, None)
+    torch.cuda.synchronize()
+    xin = ref_rmsnorm(x, nw, 1e-5) if norm else x.to(torch.float64)
+    want = f32_from_bf16(w) @ xin
+    if epi == ADD:
+        want = want + base
+    close(out, want, f"matvec rows={rows} k={k}")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("f,k", [(16, 64), (3072, 1024), (1792, 4096)])
+def test_matvec_swiglu(cuda, f, k):
+    torch = cuda
+    g = torch.Generator(device="cuda").manual_seed(f + k)
+    x = torch.randn(k, device="cuda", generator=g)
+    gate = torch.randn(f, k, device="cuda", generator=g) * 0.02
+    up = torch.randn(f, k, device="cuda", generator=g) * 0.02
+    w = bf16_from_f32(interleave_gate_up(gate, up))
+    out = torch.empty(f, device="cuda")
+    runtime.lib().strasgpt_k_matvec(x.data_ptr(), None, 0.0, w.data_ptr(), k, f,
+                                    out.data_ptr(), SWIGLU, None)
+    torch.cuda.synchronize()
+    gb = f32_from_bf16(bf16_from_f32(gate))
+    ub = f32_from_bf16(bf16_from_f32(up))
+    want = ref_swiglu(gb @ x.double(), ub @ x.double())
+    close(out, want, "swiglu matvec")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m,n,k", [(1, 64, 32), (5, 100, 96), (64, 64, 64),
+                                   (130, 300, 512), (512, 1024, 1024)])
+@pytest.mark.parametrize("epi", [STORE, ADD, SWIGLU])
+def test_gemm_simt(cuda, m, n, k, epi):
+    torch = cuda
+    if epi == SWIGLU and n % 64:
+        n = (n + 63) // 64 * 64
+    g = torch.Generator(device="cuda").manual_seed(m * 7 + n + k)
+    a = torch.randn(m, k, device="cuda", generator=g)
+    wf = torch.randn(n, k, device="cuda", generator=g) * 0.02
+    w = bf16_from_f32(wf)
+    ncol = n // 2 if epi == SWIGLU else n
+    c = torch.randn(m, ncol, device="cuda", generator=g)
+    base = c.clone().to(torch.float64)
+    runtime.lib().strasgpt_k_gemm_simt(a.data_ptr(), k, w.data_ptr(), k, m, n,
+                                       c.data_ptr(), ncol, epi, None)
+    torch.cuda.synchronize()
+    full = a.double() @ f32_from_bf16(w).T
+    if epi == STORE:
+        want = full
+    elif epi == ADD:
+        want = full + base
+    else:
+        v = full.view(m, n // 32, 2, 16)
+        want = ref_swiglu(v[:, :, 0, :], v[:, :, 1, :]).reshape(m, n // 2)
+    close(c, want, f"gemm {m}x{n}x{k} epi {epi}")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("t,d", [(1, 256), (3, 2048), (17, 5120)])
+def test_rmsnorm_rows(cuda, t, d):
+    torch = cuda
+    x = torch.randn(t, d, device="cuda") * 3
+    w = bf16_from_f32(1 + 0.1 * torch.randn(d, device="cuda"))
+    y = torch.empty_like(x)
+    runtime.lib().strasgpt_k_rmsnorm_rows(x.data_ptr(), t, d, w.data_ptr(), 1e-6,
+                                          y.data_ptr(), None)
+    torch.cuda.synchronize()
+    close(y, ref_rmsnorm(x, w, 1e-6), "rmsnorm")
