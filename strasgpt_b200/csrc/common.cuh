@@ -47,6 +47,25 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
   return r;
 }
 
+// Bulk prefetch of [p, p + bytes) into L2 (bytes a multiple of 16, p
+// 16-byte aligned). Only ever used on read-only weights.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes)
+               : "memory");
+}
+
+// Programmatic dependent launch. Every kernel launched through sg::launch
+// calls pdl_wait() before it reads anything an earlier kernel writes or
+// writes anything an earlier kernel reads; only read-only weights are
+// touched before it. pdl_trigger() lets the next kernel of the stream start
+// its own prologue (weight prefetch) while this one runs.
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
@@ -91,6 +110,26 @@ __device__ __forceinline__ float dot8(uint4 w, float4 a, float4 b, float acc) {
 __device__ __forceinline__ float swiglu(float fc, float up) {
   fc *= (1.0f / (1.0f + expf(-fc)));
   return fc * up;
+}
+
+// Launch with the programmatic-stream-serialization attribute (PDL), unless
+// STRASGPT_PDL=0. Launch errors are fatal.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline void launch(void (*kernel)(KArgs...), dim3 grid, dim3 block,
+                   size_t smem, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  SG_CUDA(cudaLaunchKernelEx(&cfg, kernel, ((KArgs)args)...));
 }
 
 }  // namespace sg

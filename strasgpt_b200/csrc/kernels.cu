@@ -8,12 +8,37 @@
 // sqrtf(head_dim), max-subtracted expf softmax, SwiGLU as
 // fc * (1/(1+expf(-fc))) * up. Summation order differs (parallel
 // reductions), which the parity tests bound.
+//
+// Every kernel is launched with programmatic dependent launch (sg::launch):
+// it triggers its dependents first, touches only read-only weights before
+// pdl_wait(), and only then reads activations.
 #include "common.cuh"
 #include "kernels.h"
 
 #include <math.h>
+#include <stdlib.h>
 
 namespace sg {
+
+bool pdl_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("STRASGPT_PDL");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
+static int g_num_sms = 0;
+static int num_sms() {
+  if (!g_num_sms) {
+    int dev;
+    SG_CUDA(cudaGetDevice(&dev));
+    SG_CUDA(cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount,
+                                   dev));
+  }
+  return g_num_sms;
+}
 
 // ---------------------------------------------------------------------------
 // Embedding gather (source/transformer.c:1247-1255)
@@ -21,6 +46,8 @@ namespace sg {
 __global__ void k_embed(const int* __restrict__ tok,
                         const uint16_t* __restrict__ emb, int D,
                         float* __restrict__ x) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.y;
   const uint16_t* row = emb + (size_t)tok[t] * D;
   float* xr = x + (size_t)t * D;
@@ -37,7 +64,7 @@ __global__ void k_embed(const int* __restrict__ tok,
 void embed(const int* tok, int T, const uint16_t* emb, int D, float* x,
            cudaStream_t s) {
   dim3 grid((D / 8 + 255) / 256, T);
-  k_embed<<<grid, 256, 0, s>>>(tok, emb, D, x);
+  launch(k_embed, grid, dim3(256), 0, s, tok, emb, D, x);
 }
 
 // ---------------------------------------------------------------------------
@@ -47,6 +74,8 @@ __global__ void k_rmsnorm_rows(const float* __restrict__ x, int D,
                                const uint16_t* __restrict__ w, float eps,
                                float* __restrict__ y) {
   __shared__ float red[32];
+  pdl_trigger();
+  pdl_wait();
   const float* xr = x + (size_t)blockIdx.x * D;
   float* yr = y + (size_t)blockIdx.x * D;
   float ss = 0.f;
@@ -60,29 +89,79 @@ __global__ void k_rmsnorm_rows(const float* __restrict__ x, int D,
 
 void rmsnorm_rows(const float* x, int T, int D, const uint16_t* w, float eps,
                   float* y, cudaStream_t s) {
-  k_rmsnorm_rows<<<T, 256, 0, s>>>(x, D, w, eps, y);
+  launch(k_rmsnorm_rows, dim3(T), dim3(256), 0, s, x, D, w, eps, y);
 }
 
 // ---------------------------------------------------------------------------
-// Decode matvec: one warp streams two weight rows with 128-bit no-L1 loads,
-// four vectors deep per row; the activation vector sits in shared memory in
-// a split layout (elements k..k+3 of every 8-group in one array, k+4..k+7
-// in another) so that each lane's two float4 reads are bank-conflict free.
+// Decode matvec. One warp streams two weight rows with 128-bit no-L1 loads,
+// four vectors deep per row. Before waiting on the previous kernel, each
+// warp prefetches its rows into L2 and loads its first batch into
+// registers, so the weight stream overlaps the previous kernel's tail. The
+// activation vector sits in shared memory in a split layout (elements
+// 8j..8j+3 in one array, 8j+4..8j+7 in another) so that each lane's two
+// float4 reads are bank-conflict free.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ int xs_split_index(int k, int K) {
-  // element k -> [half][k/8][k%4], half = (k/4)&1
   return (((k >> 2) & 1) * (K >> 1)) + ((k >> 3) << 2) + (k & 3);
+}
+
+template <int EPI>
+__device__ __forceinline__ void matvec_rows(int item, int rows, int& r0,
+                                            int& r1, bool& has1) {
+  if (EPI == EPI_SWIGLU) {
+    r0 = (item / SG_GU_GROUP) * (2 * SG_GU_GROUP) + item % SG_GU_GROUP;
+    r1 = r0 + SG_GU_GROUP;
+    has1 = true;  // `rows` counts outputs; the up row always exists
+  } else {
+    r0 = 2 * item;
+    r1 = r0 + 1;
+    has1 = r1 < rows;
+  }
 }
 
 template <int EPI, bool NORM>
 __global__ void __launch_bounds__(256)
     k_matvec(const float* __restrict__ x, const uint16_t* __restrict__ nw,
              float eps, const uint16_t* __restrict__ W, int K, int items,
-             int rows, float* __restrict__ out) {
+             int rows, float* __restrict__ out, int prefetch) {
   extern __shared__ float4 xs4[];
   float* xs = reinterpret_cast<float*>(xs4);
   __shared__ float red[32];
+  constexpr int U = 4;
   const int tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  const int item0 = blockIdx.x * nwarps + warp;
+  const int stride = gridDim.x * nwarps;
+
+  // Weights only: L2 prefetch of every row of this warp, then registers.
+  if (prefetch && lane < 2) {
+    for (int item = item0; item < items; item += stride) {
+      int r0, r1;
+      bool has1;
+      matvec_rows<EPI>(item, rows, r0, r1, has1);
+      if (lane == 0) prefetch_l2(W + (size_t)r0 * K, (uint32_t)K * 2);
+      if (lane == 1 && has1) prefetch_l2(W + (size_t)r1 * K, (uint32_t)K * 2);
+    }
+  }
+  uint4 p0[U], p1[U];
+  if (item0 < items) {
+    int r0, r1;
+    bool has1;
+    matvec_rows<EPI>(item0, rows, r0, r1, has1);
+    const uint16_t* w0 = W + (size_t)r0 * K;
+    const uint16_t* w1 = W + (size_t)(has1 ? r1 : r0) * K;
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int k = lane * 8 + u * 256;
+      if (k < K) {
+        p0[u] = ldg_stream(w0 + k);
+        p1[u] = ldg_stream(w1 + k);
+      }
+    }
+  }
+  pdl_trigger();
+  pdl_wait();
+
   if (NORM) {
     float ss = 0.f;
     for (int k = tid; k < K; k += blockDim.x) {
@@ -99,25 +178,29 @@ __global__ void __launch_bounds__(256)
   }
   __syncthreads();
 
-  const float4* lo4 = xs4;            // elements 8j..8j+3
-  const float4* hi4 = xs4 + (K >> 3); // elements 8j+4..8j+7
-  const int lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
-  constexpr int U = 4;
-  for (int item = blockIdx.x * nwarps + warp; item < items;
-       item += gridDim.x * nwarps) {
+  const float4* lo4 = xs4;
+  const float4* hi4 = xs4 + (K >> 3);
+  for (int item = item0; item < items; item += stride) {
     int r0, r1;
-    if (EPI == EPI_SWIGLU) {
-      r0 = (item / SG_GU_GROUP) * (2 * SG_GU_GROUP) + item % SG_GU_GROUP;
-      r1 = r0 + SG_GU_GROUP;
-    } else {
-      r0 = 2 * item;
-      r1 = r0 + 1;
-    }
-    const bool has1 = r1 < rows;
+    bool has1;
+    matvec_rows<EPI>(item, rows, r0, r1, has1);
     const uint16_t* w0 = W + (size_t)r0 * K;
     const uint16_t* w1 = W + (size_t)(has1 ? r1 : r0) * K;
     float a0 = 0.f, a1 = 0.f;
-    for (int kb = lane * 8; kb < K; kb += 256 * U) {
+    int kstart = lane * 8;
+    if (item == item0) {  // the batch loaded before the wait
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        const int k = kstart + u * 256;
+        if (k < K) {
+          const float4 xa = lo4[k >> 3], xb = hi4[k >> 3];
+          a0 = dot8(p0[u], xa, xb, a0);
+          a1 = dot8(p1[u], xa, xb, a1);
+        }
+      }
+      kstart += 256 * U;
+    }
+    for (int kb = kstart; kb < K; kb += 256 * U) {
       uint4 v0[U], v1[U];
 #pragma unroll
       for (int u = 0; u < U; u++) {
@@ -153,17 +236,6 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-static int g_num_sms = 0;
-static int num_sms() {
-  if (!g_num_sms) {
-    int dev;
-    SG_CUDA(cudaGetDevice(&dev));
-    SG_CUDA(cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount,
-                                   dev));
-  }
-  return g_num_sms;
-}
-
 template <int EPI, bool NORM>
 static void launch_matvec(const float* x, const uint16_t* nw, float eps,
                           const uint16_t* W, int K, int rows, float* out,
@@ -173,11 +245,14 @@ static void launch_matvec(const float* x, const uint16_t* nw, float eps,
   int blocks = (items + warps - 1) / warps;
   const size_t smem = (size_t)K * sizeof(float);
   if (smem > 200 * 1024) SG_DIE("matvec: K too large for shared memory");
-  // Enough CTAs to cover every SM several times; the rest grid-stride.
   const int cap = num_sms() * 16;
   if (blocks > cap) blocks = cap;
-  k_matvec<EPI, NORM><<<blocks, warps * 32, smem, s>>>(x, nw, eps, W, K,
-                                                       items, rows, out);
+  // Prefetch into L2 only what fits comfortably (the 126 MB L2 also holds
+  // the following kernels' prefetches).
+  const double bytes = (double)(EPI == EPI_SWIGLU ? 2 * rows : rows) * K * 2;
+  const int prefetch = bytes <= 32.0 * 1024 * 1024 ? 1 : 0;
+  launch(k_matvec<EPI, NORM>, dim3(blocks), dim3(warps * 32), smem, s, x, nw,
+         eps, W, K, items, rows, out, prefetch);
 }
 
 void matvec(const float* x, const uint16_t* norm_w, float eps,
@@ -215,6 +290,8 @@ __global__ void __launch_bounds__(256)
   __shared__ float smem[64 * 65];
   float* As = smem;            // [32][65]  k-major
   float* Ws = smem + 32 * 65;  // [32][65]
+  pdl_trigger();
+  pdl_wait();
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
   float acc[4][4] = {};
@@ -307,11 +384,11 @@ void gemm_simt(const float* A, int lda, const uint16_t* W, int K, int M,
     SG_DIE("gemm: swiglu weight rows must be a multiple of 64");
   dim3 grid((N + 63) / 64, (M + 63) / 64);
   if (epi == EPI_STORE)
-    k_gemm_simt<EPI_STORE><<<grid, 256, 0, s>>>(A, lda, W, K, M, N, C, ldc);
+    launch(k_gemm_simt<EPI_STORE>, grid, dim3(256), 0, s, A, lda, W, K, M, N, C, ldc);
   else if (epi == EPI_ADD)
-    k_gemm_simt<EPI_ADD><<<grid, 256, 0, s>>>(A, lda, W, K, M, N, C, ldc);
+    launch(k_gemm_simt<EPI_ADD>, grid, dim3(256), 0, s, A, lda, W, K, M, N, C, ldc);
   else
-    k_gemm_simt<EPI_SWIGLU><<<grid, 256, 0, s>>>(A, lda, W, K, M, N, C, ldc);
+    launch(k_gemm_simt<EPI_SWIGLU>, grid, dim3(256), 0, s, A, lda, W, K, M, N, C, ldc);
 }
 
 // ---------------------------------------------------------------------------
@@ -321,6 +398,8 @@ void gemm_simt(const float* A, int lda, const uint16_t* W, int K, int M,
 __global__ void k_qkv_post(QkvPostArgs a) {
   __shared__ float v[256];
   __shared__ float red[32];
+  pdl_trigger();
+  pdl_wait();
   const int head = blockIdx.x, t = blockIdx.y, i = threadIdx.x, HD = a.HD;
   const int pos = *a.pos + t;
   const int ld = (a.QHl + 2 * a.KHl) * HD;
@@ -365,28 +444,58 @@ __global__ void k_qkv_post(QkvPostArgs a) {
 void qkv_post(const QkvPostArgs& a, cudaStream_t s) {
   if (a.HD > 256 || a.HD % 32 != 0) SG_DIE("qkv_post: unsupported head_dim");
   dim3 grid(a.QHl + a.KHl, a.T);
-  k_qkv_post<<<grid, a.HD, 0, s>>>(a);
+  launch(k_qkv_post, grid, dim3(a.HD), 0, s, a);
 }
 
 // ---------------------------------------------------------------------------
-// Decode attention: grid (kv head, split). Each warp walks positions of the
-// split with an online softmax for the G query heads of the group; the CTA
-// merges its warps, writes a partial, and the last CTA of the kv head (by
-// ticket) merges the splits into att.
+// Decode attention. Grid (kv head, split); 8 warps per CTA. A warp takes 8
+// cache positions at a time with 4 lanes per position (each lane a quarter
+// of the row, all its float4 loads in flight at once), reduces the G dot
+// products over the 4 lanes, runs an online softmax over the 8 positions,
+// and accumulates P.V with lanes spanning the head dimension. Warps, then
+// splits, are merged with the usual max-rescaling; the last CTA of a kv
+// head (ticket) does the split merge, one warp per query head.
 // ---------------------------------------------------------------------------
+constexpr int kAttnWarps = 8;
+constexpr int kAttnMaxSplits = 64;
+
+// Aligned vector load of N consecutive floats (N = 1, 2 or 4).
+template <int N>
+__device__ __forceinline__ void load_vec(const float* p, float* out) {
+  if (N == 4) {
+    const float4 t = *reinterpret_cast<const float4*>(p);
+    out[0] = t.x;
+    out[1] = t.y;
+    out[2] = t.z;
+    out[3] = t.w;
+  } else if (N == 2) {
+    const float2 t = *reinterpret_cast<const float2*>(p);
+    out[0] = t.x;
+    out[1] = t.y;
+  } else {
+    out[0] = *p;
+  }
+}
+
 template <int HD, int G>
-__global__ void __launch_bounds__(128) k_attn_decode(AttnDecodeArgs a) {
-  constexpr int V = HD / 32;
-  constexpr int NW = 4;
-  __shared__ float qs[G * HD];
+__global__ void __launch_bounds__(kAttnWarps * 32)
+    k_attn_decode(AttnDecodeArgs a) {
+  constexpr int NW = kAttnWarps;
+  constexpr int QF = HD / 16;  // float4 per lane for a score
+  constexpr int V = HD / 32;   // floats per lane for P.V
+  __shared__ __align__(16) float qs[G * HD];
   __shared__ float wm[NW][G], wl[NW][G];
-  __shared__ float wacc[NW][G][HD];
+  __shared__ __align__(16) float wacc[NW][G][HD];
+  __shared__ float cw[G][kAttnMaxSplits];
+  __shared__ float Ls[G];
   __shared__ bool is_last;
+  pdl_trigger();
+  pdl_wait();
   const int kh = blockIdx.x, sp = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int len = *a.pos + 1;
-  const int s0 = sp * a.split_len;
-  const int s1 = min(s0 + a.split_len, len);
+  const int s_begin = sp * a.split_len;
+  const int s_end = min(s_begin + a.split_len, len);
   for (int i = tid; i < G * HD; i += blockDim.x)
     qs[i] = a.q[(size_t)kh * G * HD + i];
   __syncthreads();
@@ -397,30 +506,75 @@ __global__ void __launch_bounds__(128) k_attn_decode(AttnDecodeArgs a) {
     m[g] = -INFINITY;
     l[g] = 0.f;
 #pragma unroll
-    for (int i = 0; i < V; i++) acc[g][i] = 0.f;
+    for (int v = 0; v < V; v++) acc[g][v] = 0.f;
   }
-  const float div = sqrtf((float)HD);
+  const int j = lane >> 2, qd = lane & 3;
   const float* kb = a.k_cache + (size_t)kh * a.ctx * HD;
   const float* vb = a.v_cache + (size_t)kh * a.ctx * HD;
-  for (int s = s0 + warp; s < s1; s += NW) {
-    float kv[V], vv[V];
+  const float div = sqrtf((float)HD);
+  for (int base = s_begin + warp * 8; base < s_end; base += NW * 8) {
+    const int s = base + j;
+    const bool valid = s < s_end;
+    float d[G];
 #pragma unroll
-    for (int i = 0; i < V; i++) kv[i] = kb[(size_t)s * HD + lane * V + i];
+    for (int g = 0; g < G; g++) d[g] = 0.f;
+    float4 kv[QF];
+    if (valid) {
+      const float4* kr = reinterpret_cast<const float4*>(kb + (size_t)s * HD);
 #pragma unroll
-    for (int i = 0; i < V; i++) vv[i] = vb[(size_t)s * HD + lane * V + i];
+      for (int i = 0; i < QF; i++) kv[i] = kr[qd + 4 * i];
+    }
+    float vv[8][V];
+#pragma unroll
+    for (int jj = 0; jj < 8; jj++) {
+      const int sj = base + jj;
+      if (sj < s_end) {
+        load_vec<V>(vb + (size_t)sj * HD + lane * V, vv[jj]);
+      } else {
+#pragma unroll
+        for (int v = 0; v < V; v++) vv[jj][v] = 0.f;
+      }
+    }
+    if (valid) {
+#pragma unroll
+      for (int i = 0; i < QF; i++) {
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+          const float4 q4 =
+              *reinterpret_cast<const float4*>(&qs[g * HD + (qd + 4 * i) * 4]);
+          d[g] = fmaf(q4.x, kv[i].x, d[g]);
+          d[g] = fmaf(q4.y, kv[i].y, d[g]);
+          d[g] = fmaf(q4.z, kv[i].z, d[g]);
+          d[g] = fmaf(q4.w, kv[i].w, d[g]);
+        }
+      }
+    }
 #pragma unroll
     for (int g = 0; g < G; g++) {
-      float d = 0.f;
-#pragma unroll
-      for (int i = 0; i < V; i++) d = fmaf(qs[g * HD + lane * V + i], kv[i], d);
-      d = warp_sum(d);
-      const float sc = d / div;
-      const float mn = fmaxf(m[g], sc);
+      float dd = d[g];
+      dd += __shfl_xor_sync(0xFFFFFFFFu, dd, 1);
+      dd += __shfl_xor_sync(0xFFFFFFFFu, dd, 2);
+      const float sc = valid ? dd / div : -INFINITY;
+      float mx = sc;
+      mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 4));
+      mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 8));
+      mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 16));
+      const float mn = fmaxf(m[g], mx);  // finite: position `base` is valid
       const float corr = expf(m[g] - mn);
-      const float p = expf(sc - mn);
-      l[g] = l[g] * corr + p;
+      const float p = valid ? expf(sc - mn) : 0.f;
+      float ps = (qd == 0) ? p : 0.f;
+      ps += __shfl_xor_sync(0xFFFFFFFFu, ps, 4);
+      ps += __shfl_xor_sync(0xFFFFFFFFu, ps, 8);
+      ps += __shfl_xor_sync(0xFFFFFFFFu, ps, 16);
+      l[g] = l[g] * corr + ps;
 #pragma unroll
-      for (int i = 0; i < V; i++) acc[g][i] = fmaf(p, vv[i], acc[g][i] * corr);
+      for (int v = 0; v < V; v++) acc[g][v] *= corr;
+#pragma unroll
+      for (int jj = 0; jj < 8; jj++) {
+        const float pj = __shfl_sync(0xFFFFFFFFu, p, jj * 4);
+#pragma unroll
+        for (int v = 0; v < V; v++) acc[g][v] = fmaf(pj, vv[jj][v], acc[g][v]);
+      }
       m[g] = mn;
     }
   }
@@ -431,12 +585,12 @@ __global__ void __launch_bounds__(128) k_attn_decode(AttnDecodeArgs a) {
       wl[warp][g] = l[g];
     }
 #pragma unroll
-    for (int i = 0; i < V; i++) wacc[warp][g][lane * V + i] = acc[g][i];
+    for (int v = 0; v < V; v++) wacc[warp][g][lane * V + v] = acc[g][v];
   }
   __syncthreads();
   const int nsplit = a.nsplit;
   for (int e = tid; e < G * HD; e += blockDim.x) {
-    const int g = e / HD, d = e % HD;
+    const int g = e / HD, dd = e % HD;
     float M = -INFINITY;
 #pragma unroll
     for (int w = 0; w < NW; w++) M = fmaxf(M, wm[w][g]);
@@ -447,15 +601,15 @@ __global__ void __launch_bounds__(128) k_attn_decode(AttnDecodeArgs a) {
         if (wm[w][g] == -INFINITY) continue;
         const float c = expf(wm[w][g] - M);
         L += wl[w][g] * c;
-        A += wacc[w][g][d] * c;
+        A += wacc[w][g][dd] * c;
       }
     }
     float* P = a.partial + ((size_t)(kh * G + g) * nsplit + sp) * (HD + 2);
-    if (d == 0) {
+    if (dd == 0) {
       P[0] = M;
       P[1] = L;
     }
-    P[2 + d] = A;
+    P[2 + dd] = A;
   }
   __threadfence();
   __syncthreads();
@@ -466,37 +620,62 @@ __global__ void __launch_bounds__(128) k_attn_decode(AttnDecodeArgs a) {
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  for (int e = tid; e < G * HD; e += blockDim.x) {
-    const int g = e / HD, d = e % HD;
+  for (int g = warp; g < G; g += NW) {
     const float* P0 = a.partial + (size_t)(kh * G + g) * nsplit * (HD + 2);
-    float M = -INFINITY;
-    for (int j = 0; j < nsplit; j++) M = fmaxf(M, __ldcg(P0 + j * (HD + 2)));
-    float L = 0.f, A = 0.f;
-    for (int j = 0; j < nsplit; j++) {
-      const float mj = __ldcg(P0 + j * (HD + 2));
-      if (mj == -INFINITY) continue;
-      const float c = expf(mj - M);
-      L += __ldcg(P0 + j * (HD + 2) + 1) * c;
-      A += __ldcg(P0 + j * (HD + 2) + 2 + d) * c;
+    float mloc = -INFINITY;
+    for (int jx = lane; jx < nsplit; jx += 32)
+      mloc = fmaxf(mloc, __ldcg(P0 + (size_t)jx * (HD + 2)));
+    const float M = warp_max(mloc);
+    float lsum = 0.f;
+    for (int jx = lane; jx < nsplit; jx += 32) {
+      const float mj = __ldcg(P0 + (size_t)jx * (HD + 2));
+      const float c = (mj == -INFINITY) ? 0.f : expf(mj - M);
+      cw[g][jx] = c;
+      lsum += c * __ldcg(P0 + (size_t)jx * (HD + 2) + 1);
     }
-    a.att[(size_t)(kh * G + g) * HD + d] = A / L;
+    lsum = warp_sum(lsum);
+    if (lane == 0) Ls[g] = lsum;
+  }
+  __syncthreads();
+  for (int e = tid; e < G * HD; e += blockDim.x) {
+    const int g = e / HD, dd = e % HD;
+    const float* P0 = a.partial + (size_t)(kh * G + g) * nsplit * (HD + 2) + 2 + dd;
+    float A = 0.f;
+#pragma unroll 4
+    for (int jx = 0; jx < nsplit; jx++)
+      A = fmaf(cw[g][jx], __ldcg(P0 + (size_t)jx * (HD + 2)), A);
+    a.att[(size_t)(kh * G + g) * HD + dd] = A / Ls[g];
   }
   if (tid == 0) a.ticket[kh] = 0;
 }
 
 template <int HD>
 static void attn_decode_hd(const AttnDecodeArgs& a, cudaStream_t s) {
-  dim3 grid(a.KHl, a.nsplit);
+  dim3 grid(a.KHl, a.nsplit), block(kAttnWarps * 32);
   switch (a.G) {
-    case 1: k_attn_decode<HD, 1><<<grid, 128, 0, s>>>(a); break;
-    case 2: k_attn_decode<HD, 2><<<grid, 128, 0, s>>>(a); break;
-    case 4: k_attn_decode<HD, 4><<<grid, 128, 0, s>>>(a); break;
-    case 8: k_attn_decode<HD, 8><<<grid, 128, 0, s>>>(a); break;
+    case 1: launch(k_attn_decode<HD, 1>, grid, block, 0, s, a); break;
+    case 2: launch(k_attn_decode<HD, 2>, grid, block, 0, s, a); break;
+    case 4: launch(k_attn_decode<HD, 4>, grid, block, 0, s, a); break;
+    case 8: launch(k_attn_decode<HD, 8>, grid, block, 0, s, a); break;
     default: SG_DIE("attn_decode: unsupported GQA group size");
   }
 }
 
+void attn_decode_split(int ctx, int KHl, int* nsplit, int* split_len) {
+  // Enough CTAs to cover the SMs about twice, at most kAttnMaxSplits splits,
+  // splits a multiple of the CTA's 64 positions per pass.
+  int target = (2 * num_sms() + KHl - 1) / KHl;
+  if (target > kAttnMaxSplits) target = kAttnMaxSplits;
+  if (target < 1) target = 1;
+  const int per = kAttnWarps * 8;
+  int len = (ctx + target - 1) / target;
+  len = (len + per - 1) / per * per;
+  *split_len = len;
+  *nsplit = (ctx + len - 1) / len;
+}
+
 void attn_decode(const AttnDecodeArgs& a, cudaStream_t s) {
+  if (a.nsplit > kAttnMaxSplits) SG_DIE("attn_decode: too many splits");
   if (a.HD == 64)
     attn_decode_hd<64>(a, s);
   else if (a.HD == 128)
@@ -519,6 +698,8 @@ __global__ void __launch_bounds__(256) k_attn_prefill(AttnPrefillArgs a) {
   float* qs = sm;                  // [QT][HD]
   float* ks = qs + QT * HD;        // [KT][HD+1]
   float* vs = ks + KT * (HD + 1);  // [KT][HD]
+  pdl_trigger();
+  pdl_wait();
   const int qh = blockIdx.x, kh = qh / a.G, QHl = a.KHl * a.G;
   const int tq0 = blockIdx.y * QT;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -592,7 +773,7 @@ template <int HD>
 static void attn_prefill_hd(const AttnPrefillArgs& a, cudaStream_t s) {
   const size_t smem = (size_t)(32 * HD + 32 * (HD + 1) + 32 * HD) * 4;
   dim3 grid(a.KHl * a.G, (a.T + 31) / 32);
-  k_attn_prefill<HD><<<grid, 256, smem, s>>>(a);
+  launch(k_attn_prefill<HD>, grid, dim3(256), smem, s, a);
 }
 
 void attn_prefill(const AttnPrefillArgs& a, cudaStream_t s) {
@@ -623,6 +804,8 @@ __global__ void __launch_bounds__(512)
   __shared__ float sv[32];
   __shared__ int si[32];
   __shared__ bool is_last;
+  pdl_trigger();
+  pdl_wait();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   float best = -INFINITY;
   int bi = 0x7FFFFFFF;
@@ -671,8 +854,8 @@ void argmax_advance(const float* logits, int n, int* out_token, int* pos,
   int blocks = (n + 4095) / 4096;
   if (blocks > 64) blocks = 64;
   if (blocks < 1) blocks = 1;
-  k_argmax<<<blocks, 512, 0, s>>>(logits, n, out_token, pos, step, tokens_out,
-                                  partial_val, partial_idx, ticket);
+  launch(k_argmax, dim3(blocks), dim3(512), 0, s, logits, n, out_token, pos,
+         step, tokens_out, partial_val, partial_idx, ticket);
 }
 
 // ---------------------------------------------------------------------------
@@ -681,6 +864,8 @@ void argmax_advance(const float* logits, int n, int* out_token, int* pos,
 __global__ void k_moe_topk(const float* __restrict__ r, int E, int k,
                            int* __restrict__ idx, float* __restrict__ w) {
   // one warp per token; E <= 256
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x, lane = threadIdx.x;
   float v[8];
 #pragma unroll
@@ -727,7 +912,7 @@ __global__ void k_moe_topk(const float* __restrict__ r, int E, int k,
 void moe_topk(const float* router_logits, int T, int E, int k, int* idx,
               float* weight, cudaStream_t s) {
   if (E > 256 || k > 16 || k > E) SG_DIE("moe_topk: unsupported E/k");
-  k_moe_topk<<<T, 32, 0, s>>>(router_logits, E, k, idx, weight);
+  launch(k_moe_topk, dim3(T), dim3(32), 0, s, router_logits, E, k, idx, weight);
 }
 
 __device__ __forceinline__ float e8m0_scale(uint32_t e) {
@@ -735,7 +920,7 @@ __device__ __forceinline__ float e8m0_scale(uint32_t e) {
 }
 
 // Dot of one MXFP4 block (16 bytes = 32 codes, low nibble first) with 32
-// activations at xs[0..31] (shared memory), times the block scale.
+// activations at xs[0..31] (shared memory).
 __device__ __forceinline__ float mxfp4_block_dot(uint4 c, const float* xs,
                                                  const float* lut) {
   const uint32_t w[4] = {c.x, c.y, c.z, c.w};
@@ -762,6 +947,8 @@ __host__ __device__ __forceinline__ int pad32(int k) { return k + (k >> 5); }
 __global__ void __launch_bounds__(256) k_moe_gate_up(MoeArgs a) {
   extern __shared__ float xs[];
   __shared__ float lut[16];
+  pdl_trigger();
+  pdl_wait();
   const int tj = blockIdx.x, t = tj / a.k;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int e = a.idx[tj];
@@ -800,6 +987,8 @@ __global__ void __launch_bounds__(256) k_moe_gate_up(MoeArgs a) {
 __global__ void __launch_bounds__(256) k_moe_down(MoeArgs a) {
   extern __shared__ float hs[];  // [k][pad32(F)]
   __shared__ float lut[16];
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int Fp = pad32(a.F);
@@ -836,14 +1025,27 @@ void moe_gate_up(const MoeArgs& a, cudaStream_t s) {
   if (a.D % 32 || a.F % 32) SG_DIE("moe: dims must be multiples of 32");
   const size_t smem = (size_t)pad32(a.D) * 4;
   dim3 grid(a.T * a.k, (a.F + 63) / 64);
-  k_moe_gate_up<<<grid, 256, smem, s>>>(a);
+  launch(k_moe_gate_up, grid, dim3(256), smem, s, a);
 }
 
 void moe_down(const MoeArgs& a, cudaStream_t s) {
   const size_t smem = (size_t)a.k * pad32(a.F) * 4;
   if (smem > 200 * 1024) SG_DIE("moe_down: k * F too large");
   dim3 grid(a.T, (a.D + 63) / 64);
-  k_moe_down<<<grid, 256, smem, s>>>(a);
+  launch(k_moe_down, grid, dim3(256), smem, s, a);
+}
+
+// Busy-wait for a bounded number of SM cycles (always terminates). Used by
+// the profiling pass so the host can enqueue a whole step before the GPU
+// starts on it.
+__global__ void k_sleep_cycles(long long cycles) {
+  const long long t0 = clock64();
+  while (clock64() - t0 < cycles) __nanosleep(1000);
+}
+
+void gpu_sleep_cycles(long long cycles, cudaStream_t s) {
+  k_sleep_cycles<<<1, 1, 0, s>>>(cycles);
+  SG_CUDA(cudaGetLastError());
 }
 
 // Raise the dynamic shared-memory limit of every kernel that needs more

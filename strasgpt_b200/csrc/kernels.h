@@ -69,6 +69,9 @@ struct AttnDecodeArgs {
   float* att;               // [QHl][HD]
 };
 void attn_decode(const AttnDecodeArgs& a, cudaStream_t s);
+// Split of a `ctx`-row cache for attn_decode (<= 64 splits, each a multiple
+// of 64 positions, about two CTAs per SM).
+void attn_decode_split(int ctx, int KHl, int* nsplit, int* split_len);
 
 // Causal prefill attention for T tokens at positions pos..pos+T-1 over
 // cache rows [0, pos+t]. q [T][QHl][HD] -> att [T][QHl][HD].
@@ -117,4 +120,6 @@ namespace sg {
 // Raise shared-memory limits of the kernels above; once per device, before
 // the first launch or stream capture.
 void configure_kernels();
+// One-thread kernel that spins for `cycles` SM clocks (bounded).
+void gpu_sleep_cycles(long long cycles, cudaStream_t s);
 }  // namespace sg

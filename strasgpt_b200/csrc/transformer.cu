@@ -509,15 +509,7 @@ void alloc_state(const W_t* w, const transformer_configuration_t* c, S_t* s) {
   s->pos = I32(1);
   s->step = I32(1);
   s->gen = I32((size_t)s->ctx + 1);
-  // Decode attention split: enough CTAs to cover the SMs twice.
-  int sms = 148;
-  SG_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, w->device));
-  int ns = (2 * sms + w->KHl - 1) / w->KHl;
-  const int max_ns = (s->ctx + 31) / 32;
-  if (ns > max_ns) ns = max_ns;
-  if (ns < 1) ns = 1;
-  s->split_len = (s->ctx + ns - 1) / ns;
-  s->nsplit = (s->ctx + s->split_len - 1) / s->split_len;
+  sg::attn_decode_split(s->ctx, w->KHl, &s->nsplit, &s->split_len);
   s->attn_partial = F32((size_t)w->QHl * s->nsplit * (HD + 2));
   s->attn_ticket = I32(w->KHl);
   SG_CUDA(cudaMemset(s->attn_ticket, 0, w->KHl * 4));
@@ -553,14 +545,15 @@ struct Runner {
       fn();
       return;
     }
-    cudaEvent_t a, b;
-    SG_CUDA(cudaEventCreate(&a));
-    SG_CUDA(cudaEventCreate(&b));
-    SG_CUDA(cudaEventRecord(a, st));
+    const size_t n = s->prof_fam.size();
+    while (s->prof_ev.size() < 2 * n + 2) {
+      cudaEvent_t e;
+      SG_CUDA(cudaEventCreate(&e));
+      s->prof_ev.push_back(e);
+    }
+    SG_CUDA(cudaEventRecord(s->prof_ev[2 * n], st));
     fn();
-    SG_CUDA(cudaEventRecord(b, st));
-    s->prof_ev.push_back(a);
-    s->prof_ev.push_back(b);
+    SG_CUDA(cudaEventRecord(s->prof_ev[2 * n + 1], st));
     s->prof_fam.push_back(fam);
     s->prof_bytes.push_back(bytes);
   }
@@ -902,6 +895,7 @@ void transformer_free(transformer_t* t) {
     for (auto e : s->ev)
       if (e) cudaEventDestroy(e);
     if (s->h_logits) cudaFreeHost(s->h_logits);
+    for (auto e : s->prof_ev) cudaEventDestroy(e);
     if (s->stream) cudaStreamDestroy(s->stream);
     for (void* p : s->allocs) cudaFree(p);
     delete s;
@@ -1048,6 +1042,9 @@ int strasgpt_profile_decode(transformer_t* t, int first_token, size_t steps,
   const int zero = 0;
   SG_CUDA(cudaMemcpyAsync(st->step, &zero, 4, cudaMemcpyHostToDevice, st->stream));
   for (size_t i = 0; i < steps; i++) {
+    // Hold the GPU ~2 ms so the host enqueues the whole step first: the
+    // event pairs then time the kernels, not the host's launch rate.
+    sg::gpu_sleep_cycles(4000000LL, st->stream);
     st->prof = prof;
     r.decode_layers();
     r.argmax(1);
@@ -1064,8 +1061,6 @@ int strasgpt_profile_decode(transformer_t* t, int first_token, size_t steps,
     // attention bytes: K and V rows [0, pos] of every layer
     const double pos = (double)(st->cached_count + i);
     prof->bytes[FAM_ATTN] += 2.0 * w->L * w->KHl * (pos + 1) * w->HD * 4;
-    for (auto e : st->prof_ev) cudaEventDestroy(e);
-    st->prof_ev.clear();
     st->prof_fam.clear();
     st->prof_bytes.clear();
   }
