@@ -18,12 +18,12 @@ extern "C" {
 // Epilogue selector shared by the projection entry points.
 #define STRASGPT_EPI_STORE  0  // out = W x
 #define STRASGPT_EPI_ADD    1  // out += W x (residual)
-#define STRASGPT_EPI_SWIGLU 2  // out = silu(gate) * up, rows interleaved by 16
+#define STRASGPT_EPI_SWIGLU 2  // out = silu(gate) * up, gate/up rows interleaved
 
 // y = W x for one token: W bf16 [rows][K] (rows of K contiguous), x fp32
 // [K]. norm_w (bf16 [K]) != NULL applies the reference RMSNorm to x first
 // (source/transformer.c:978-999). For STRASGPT_EPI_SWIGLU `rows` counts
-// outputs and W holds 2*rows rows, gate/up interleaved in groups of 16.
+// outputs and W holds 2*rows rows: gate row f at 2f, up row f at 2f+1.
 int strasgpt_k_matvec(const float* x, const uint16_t* norm_w, float eps,
                       const uint16_t* w, int k, int rows, float* out, int epi,
                       void* stream);

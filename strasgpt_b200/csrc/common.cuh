@@ -105,6 +105,19 @@ __device__ __forceinline__ float dot8(uint4 w, float4 a, float4 b, float acc) {
   return acc;
 }
 
+// s[i] += w_i * x_i for the 8 bf16 weights of a 16-byte vector: eight
+// independent accumulators (no FMA chain between the elements).
+__device__ __forceinline__ void acc8(uint4 w, float4 a, float4 b, float* s) {
+  s[0] = fmaf(bf16_lo(w.x), a.x, s[0]);
+  s[1] = fmaf(bf16_hi(w.x), a.y, s[1]);
+  s[2] = fmaf(bf16_lo(w.y), a.z, s[2]);
+  s[3] = fmaf(bf16_hi(w.y), a.w, s[3]);
+  s[4] = fmaf(bf16_lo(w.z), b.x, s[4]);
+  s[5] = fmaf(bf16_hi(w.z), b.y, s[5]);
+  s[6] = fmaf(bf16_lo(w.w), b.z, s[6]);
+  s[7] = fmaf(bf16_hi(w.w), b.w, s[7]);
+}
+
 // SiLU-gated product, written as the reference does
 // (source/transformer.c:1481-1484): fc * (1 / (1 + expf(-fc))) * up.
 __device__ __forceinline__ float swiglu(float fc, float up) {

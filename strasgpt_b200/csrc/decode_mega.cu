@@ -1,0 +1,1087 @@
+// Persistent decode megakernel for dense models (see mega.h).
+//
+// One CTA per SM (cooperative launch, so all CTAs are co-resident), 8
+// warps. A decode step is a fixed sequence of phases; each phase splits its
+// work over the CTAs and ends at a grid barrier:
+//   per layer  QKV     x -> RMSNorm -> Wqkv rows            -> qkv
+//              ATTN    per (kv head, split): q/k RMSNorm + RoPE, K/V append
+//                      at `pos`, scores / softmax / P.V      -> split partials
+//              O       merge the splits -> Wo rows, residual add -> x
+//              GU      x -> RMSNorm -> gate/up row pairs, SwiGLU -> h
+//              DOWN    h -> Wd rows, residual add              -> x
+//   LM head    x -> RMSNorm -> vocab rows (+ per-CTA argmax)
+//   argmax     every CTA reduces the per-CTA partials -> next token
+//
+// Weight streaming. Each weight phase gives CTA c a contiguous slice of row
+// pairs, so a CTA's weights for the whole launch form a fixed list of
+// contiguous byte ranges ("chunks", at most one shared-memory buffer each).
+// kRing buffers per CTA: thread 0 issues the cp.async.bulk copy of chunk
+// g+kRing as soon as chunk g has been consumed, with completion on the
+// buffer's mbarrier. Weights never depend on activations, so copies run ahead across
+// phase and layer boundaries while the grid waits at barriers. Attention
+// CTAs also prefetch their K/V cache rows into L2 during the QKV phase.
+//
+// Activations are read with ld.global.cg (L2), never from a possibly stale
+// L1 line. Every wait is bounded (2 s): a timeout sets *err, later waits
+// return at once, the kernel runs to its end and the host reports the error.
+// All issued copies are consumed (waited on) before the kernel ends.
+//
+// Math per element is the same as the multi-kernel path (kernels.cu) and
+// the reference (source/transformer.c:1186-1602).
+#include "common.cuh"
+#include "kernels.h"
+#include "mega.h"
+
+namespace sg {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kPosPerPass = kWarps * 8;  // cache rows per CTA pass
+constexpr int kMaxSplits = 64;
+constexpr unsigned long long kTimeoutNs = 2000000000ULL;
+constexpr size_t kSmemBudget = 220 * 1024;  // dynamic shared memory per CTA
+
+// ---------------------------------------------------------------------------
+// PTX helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long now_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n .reg .pred p;\n"
+      " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Global -> this CTA's shared memory, completion counted on `bar`.
+__device__ __forceinline__ void bulk_copy(void* dst, const void* src, unsigned bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// Trace record per (barrier, CTA): [arrive, release, staged, first chunk
+// ready, phase consumed] (%globaltimer ns; thread 0 writes them).
+constexpr int kTraceWidth = kMegaTraceWidth;
+enum { MARK_STAGED = 2, MARK_READY = 3, MARK_CONSUMED = 4, MARK_COMPUTED = 5, MARK_ISSUED = 6 };
+
+__device__ __forceinline__ void trace_mark(const MegaArgs& a, int nbar, int slot) {
+  if (a.trace && nbar < a.trace_barriers && threadIdx.x == 0)
+    a.trace[((size_t)nbar * gridDim.x + blockIdx.x) * kTraceWidth + slot] = now_ns();
+}
+
+// ---------------------------------------------------------------------------
+// Grid barrier: a monotonic arrival counter (zeroed by the host before each
+// launch); barrier n completes when the counter reaches (n+1) * gridDim.x.
+// ---------------------------------------------------------------------------
+__device__ void grid_barrier(const MegaArgs& a, int& nbar) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const bool tr = a.trace && nbar < a.trace_barriers;
+    unsigned long long* slot =
+        tr ? a.trace + ((size_t)nbar * gridDim.x + blockIdx.x) * kTraceWidth : nullptr;
+    if (tr) slot[0] = now_ns();
+    const unsigned target = (unsigned)(nbar + 1) * gridDim.x;
+    __threadfence();
+    red_release_add(&a.bar[0], 1u);
+    if (!*(volatile int*)a.err) {
+      const unsigned long long t0 = now_ns();
+      unsigned spins = 0;
+      while ((int)(ld_acquire_u32(&a.bar[0]) - target) < 0) {
+        // The timer and the error flag are checked every 64 polls only.
+        if ((++spins & 63) == 0) {
+          if (*(volatile int*)a.err) break;
+          if (now_ns() - t0 > kTimeoutNs) {
+            atomicExch(a.err, 1);
+            break;
+          }
+        }
+      }
+    }
+    if (tr) slot[1] = now_ns();
+  }
+  nbar++;
+  __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
+// Weight phases and the per-CTA chunk schedule
+// ---------------------------------------------------------------------------
+enum WKind { W_QKV = 0, W_O = 1, W_GU = 2, W_DOWN = 3, W_LM = 4 };
+
+struct Phase {
+  const uint16_t* W;
+  int K;       // row length (elements)
+  int pairs;   // total row pairs of the phase
+  int kind;
+};
+
+// Per-layer weight pointers, copied to shared memory at kernel start so that
+// no global load sits on the phase-to-phase critical path.
+constexpr int kMaxLayers = 96;
+__shared__ MegaLayer s_layers[kMaxLayers];
+
+// Weight phase `wp` of a step: 4 per layer (QKV, O, GU, DOWN), then LM.
+__device__ __forceinline__ Phase weight_phase(const MegaArgs& a, int wp) {
+  Phase p;
+  if (wp == 4 * a.L) {
+    p.W = a.out_w;
+    p.K = a.D;
+    p.pairs = a.Vl / 2;
+    p.kind = W_LM;
+    return p;
+  }
+  const MegaLayer& ly = s_layers[wp >> 2];
+  p.kind = wp & 3;
+  switch (p.kind) {
+    case W_QKV:
+      p.W = ly.wqkv;
+      p.K = a.D;
+      p.pairs = a.QKVl / 2;
+      break;
+    case W_O:
+      p.W = ly.wo;
+      p.K = a.QHl * a.HD;
+      p.pairs = a.D / 2;
+      break;
+    case W_GU:
+      p.W = ly.wgu;
+      p.K = a.D;
+      p.pairs = a.Fl;
+      break;
+    default:
+      p.W = ly.wd;
+      p.K = a.Fl;
+      p.pairs = a.D / 2;
+      break;
+  }
+  return p;
+}
+
+// One chunk: row pairs [p0, p1) over columns [k0, k1) (either whole rows,
+// several pairs; or one pair and a column segment when a pair does not fit a
+// buffer).
+struct Chunk {
+  int p0, p1, k0, k1;
+  bool last_seg;  // the chunk completes its pair(s)
+};
+
+struct Slice {
+  int pb, pe;     // pairs [pb, pe) of this CTA
+  int ppc;        // pairs per chunk (whole rows), 0 when rows are split
+  int kseg;       // columns per segment when rows are split
+  int spp;        // segments per pair
+  int nchunks;
+};
+
+__device__ __forceinline__ Slice cta_slice(const Phase& ph, int buf_bytes) {
+  Slice s;
+  const long long np = ph.pairs;
+  s.pb = (int)(np * blockIdx.x / gridDim.x);
+  s.pe = (int)(np * (blockIdx.x + 1) / gridDim.x);
+  const int n = s.pe - s.pb;
+  const int pair_bytes = 4 * ph.K;
+  if (pair_bytes <= buf_bytes) {
+    s.ppc = buf_bytes / pair_bytes;
+    s.kseg = ph.K;
+    s.spp = 1;
+    s.nchunks = (n + s.ppc - 1) / s.ppc;
+  } else {
+    s.ppc = 0;
+    s.kseg = (buf_bytes / 4) / 256 * 256;
+    s.spp = (ph.K + s.kseg - 1) / s.kseg;
+    s.nchunks = n * s.spp;
+  }
+  return s;
+}
+
+__device__ __forceinline__ Chunk slice_chunk(const Slice& s, const Phase& ph, int ci) {
+  Chunk c;
+  if (s.ppc) {
+    c.p0 = s.pb + ci * s.ppc;
+    c.p1 = min(c.p0 + s.ppc, s.pe);
+    c.k0 = 0;
+    c.k1 = ph.K;
+    c.last_seg = true;
+  } else {
+    const int pair = s.pb + ci / s.spp, seg = ci % s.spp;
+    c.p0 = pair;
+    c.p1 = pair + 1;
+    c.k0 = seg * s.kseg;
+    c.k1 = min(c.k0 + s.kseg, ph.K);
+    c.last_seg = (seg == s.spp - 1);
+  }
+  return c;
+}
+
+// Copy-issue cursor (thread 0 only): walks the same chunk sequence as the
+// consumers, two chunks ahead.
+struct Cursor {
+  int step, wp, ci;
+};
+
+__device__ __forceinline__ bool cursor_valid(const MegaArgs& a, const Cursor& c) {
+  return c.step < a.steps;
+}
+
+// This CTA's slice of each weight-phase kind (QKV, O, GU, DOWN, LM); every
+// layer has the same shapes, so they are computed once per launch.
+__shared__ Slice s_slices[5];
+
+__device__ void cursor_skip_empty(const MegaArgs& a, Cursor& c) {
+  while (c.step < a.steps) {
+    const int kind = (c.wp == 4 * a.L) ? W_LM : (c.wp & 3);
+    if (c.ci < s_slices[kind].nchunks) return;
+    c.ci = 0;
+    if (++c.wp > 4 * a.L) {
+      c.wp = 0;
+      c.step++;
+    }
+  }
+}
+
+__device__ void cursor_issue(const MegaArgs& a, Cursor& c, char* buf, uint64_t* bar) {
+  cursor_skip_empty(a, c);
+  if (!cursor_valid(a, c)) return;
+  const Phase ph = weight_phase(a, c.wp);
+  const Slice& s = s_slices[ph.kind];
+  const Chunk ch = slice_chunk(s, ph, c.ci);
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  if (s.ppc) {
+    const unsigned bytes = (unsigned)(ch.p1 - ch.p0) * 4u * (unsigned)ph.K;
+    mbar_expect_tx(bar, bytes);
+    bulk_copy(buf, ph.W + (size_t)2 * ch.p0 * ph.K, bytes, bar);
+  } else {
+    const unsigned seg = (unsigned)(ch.k1 - ch.k0) * 2u;
+    mbar_expect_tx(bar, 2 * seg);
+    const uint16_t* r0 = ph.W + (size_t)2 * ch.p0 * ph.K + ch.k0;
+    bulk_copy(buf, r0, seg, bar);
+    bulk_copy(buf + seg, r0 + ph.K, seg, bar);
+  }
+  c.ci++;
+}
+
+// Bounded wait on a buffer's mbarrier phase.
+__device__ void wait_buffer(const MegaArgs& a, uint64_t* bar, unsigned parity) {
+  if (mbar_try_wait(bar, parity)) return;
+  const unsigned long long t0 = now_ns();
+  unsigned spins = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if ((++spins & 63) == 0) {
+      if (*(volatile int*)a.err) return;
+      if (now_ns() - t0 > kTimeoutNs) {
+        atomicExch(a.err, 2);
+        return;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Activation staging
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int split_index(int k, int K) {
+  return (((k >> 2) & 1) * (K >> 1)) + ((k >> 3) << 2) + (k & 3);
+}
+
+// Largest K an RMSNorm staging keeps in registers (K = embedding_dim).
+constexpr int kNormRegs = 32;
+constexpr int kNormMaxK = kNormRegs * kThreads;
+
+// xs (split layout) = rmsnorm(xin) * nw, or xin when nw is null. One round
+// trip to global memory: every thread loads its x values and gains at once,
+// keeps them in registers across the block-wide sum of squares, and writes
+// the normalised products.
+__device__ void stage_x(const float* xin, const uint16_t* nw, float eps, int K, float* xs,
+                        float* red) {
+  const int tid = threadIdx.x;
+  constexpr int B = 8;  // loads in flight per thread
+  if (nw) {
+    float v[kNormRegs], g[kNormRegs];
+    float ss = 0.f;
+#pragma unroll
+    for (int u = 0; u < kNormRegs; u++) {
+      const int k = tid + u * kThreads;
+      v[u] = (k < K) ? __ldcg(xin + k) : 0.f;
+      g[u] = (k < K) ? bf16_to_f32(__ldg(nw + k)) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < kNormRegs; u++) ss += v[u] * v[u];
+    ss = block_sum(ss, red);
+    ss /= (float)K;
+    const float inv = 1.0f / sqrtf(ss + eps);
+#pragma unroll
+    for (int u = 0; u < kNormRegs; u++) {
+      const int k = tid + u * kThreads;
+      if (k < K) xs[split_index(k, K)] = (v[u] * inv) * g[u];
+    }
+  } else {
+    for (int base = tid; base < K; base += B * kThreads) {
+      float v[B];
+#pragma unroll
+      for (int u = 0; u < B; u++) {
+        const int k = base + u * kThreads;
+        v[u] = (k < K) ? __ldcg(xin + k) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < B; u++) {
+        const int k = base + u * kThreads;
+        if (k < K) xs[split_index(k, K)] = v[u];
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// Attention output for the O phase, merged from the per-split partial
+// records [m, l, -, -, acc[HD]] of every query head:
+// att = sum_j c_j acc_j / sum_j c_j l_j with c_j = exp(m_j - max_j m_j);
+// splits without positions have m = -inf. Pass 1: a warp per head (two
+// heads per pass, loads together) computes the split weights c_j and the
+// denominator into shared memory (`cw`: QHl*nsplit + QHl floats). Pass 2:
+// every thread owns float4 slots of the output.
+template <int HD>
+__device__ void stage_attention(const MegaArgs& a, float* xs, float* cw) {
+  constexpr int PS = HD + 4;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int ns = a.nsplit, QD = a.QHl * HD;
+  float* Lh = cw + a.QHl * ns;
+  for (int h0 = warp; h0 < a.QHl; h0 += 2 * kWarps) {
+    const int hs[2] = {h0, h0 + kWarps};
+    float c0[2], c1[2], L[2];
+#pragma unroll
+    for (int t = 0; t < 2; t++) {
+      float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+      if (hs[t] < a.QHl) {
+        const float* P0 = a.attn_partial + (size_t)hs[t] * ns * PS;
+        if (lane < ns) {
+          m0 = __ldcg(P0 + (size_t)lane * PS);
+          l0 = __ldcg(P0 + (size_t)lane * PS + 1);
+        }
+        if (lane + 32 < ns) {
+          m1 = __ldcg(P0 + (size_t)(lane + 32) * PS);
+          l1 = __ldcg(P0 + (size_t)(lane + 32) * PS + 1);
+        }
+      }
+      const float M = warp_max(fmaxf(m0, m1));
+      c0[t] = (m0 == -INFINITY) ? 0.f : expf(m0 - M);
+      c1[t] = (m1 == -INFINITY) ? 0.f : expf(m1 - M);
+      L[t] = warp_sum(c0[t] * l0 + c1[t] * l1);
+    }
+#pragma unroll
+    for (int t = 0; t < 2; t++) {
+      if (hs[t] >= a.QHl) continue;
+      if (lane < ns) cw[hs[t] * ns + lane] = c0[t];
+      if (lane + 32 < ns) cw[hs[t] * ns + lane + 32] = c1[t];
+      if (lane == 0) Lh[hs[t]] = L[t];
+    }
+  }
+  __syncthreads();
+  // Pass 2: each thread owns float4 slots of the QD outputs and sums them
+  // over the splits, kJB splits' loads in flight per batch.
+  constexpr int kSlots = 4;  // QD <= 4 * 4 * kThreads
+  constexpr int kJB = 6;
+  const int nslot = QD / 4;
+  float4 acc[kSlots];
+#pragma unroll
+  for (int s = 0; s < kSlots; s++) acc[s] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int jb = 0; jb < ns; jb += kJB) {
+    float4 v[kSlots][kJB];
+#pragma unroll
+    for (int s = 0; s < kSlots; s++) {
+      const int slot = threadIdx.x + s * kThreads;
+      const int h = (slot * 4) / HD, d = (slot * 4) % HD;
+#pragma unroll
+      for (int jj = 0; jj < kJB; jj++) {
+        const int j = jb + jj;
+        v[s][jj] = (slot < nslot && j < ns)
+                       ? __ldcg(reinterpret_cast<const float4*>(
+                             a.attn_partial + ((size_t)h * ns + j) * PS + 4 + d))
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int s = 0; s < kSlots; s++) {
+      const int slot = threadIdx.x + s * kThreads;
+      if (slot >= nslot) continue;
+      const int h = (slot * 4) / HD;
+#pragma unroll
+      for (int jj = 0; jj < kJB; jj++) {
+        const int j = jb + jj;
+        if (j >= ns) continue;
+        const float c = cw[h * ns + j];
+        acc[s].x = fmaf(c, v[s][jj].x, acc[s].x);
+        acc[s].y = fmaf(c, v[s][jj].y, acc[s].y);
+        acc[s].z = fmaf(c, v[s][jj].z, acc[s].z);
+        acc[s].w = fmaf(c, v[s][jj].w, acc[s].w);
+      }
+    }
+  }
+#pragma unroll
+  for (int s = 0; s < kSlots; s++) {
+    const int slot = threadIdx.x + s * kThreads;
+    if (slot >= nslot) continue;
+    const int k = slot * 4, h = k / HD;
+    const float L = Lh[h];
+    xs[split_index(k, QD)] = acc[s].x / L;
+    xs[split_index(k + 1, QD)] = acc[s].y / L;
+    xs[split_index(k + 2, QD)] = acc[s].z / L;
+    xs[split_index(k + 3, QD)] = acc[s].w / L;
+  }
+  __syncthreads();
+}
+
+// Layer-0 input: the embedding row of `token`; CTA 0 also writes x.
+__device__ void stage_embedding(const MegaArgs& a, int token, const uint16_t* nw, float* xs,
+                                float* red) {
+  const int tid = threadIdx.x, K = a.D;
+  const uint16_t* row = a.emb + (size_t)token * K;
+  float v[kNormRegs], g[kNormRegs];
+  float ss = 0.f;
+#pragma unroll
+  for (int u = 0; u < kNormRegs; u++) {
+    const int k = tid + u * kThreads;
+    v[u] = (k < K) ? bf16_to_f32(__ldg(row + k)) : 0.f;
+    g[u] = (k < K) ? bf16_to_f32(__ldg(nw + k)) : 0.f;
+  }
+#pragma unroll
+  for (int u = 0; u < kNormRegs; u++) {
+    const int k = tid + u * kThreads;
+    ss += v[u] * v[u];
+    if (blockIdx.x == 0 && k < K) a.x[k] = v[u];
+  }
+  ss = block_sum(ss, red);
+  ss /= (float)K;
+  const float inv = 1.0f / sqrtf(ss + a.eps);
+#pragma unroll
+  for (int u = 0; u < kNormRegs; u++) {
+    const int k = tid + u * kThreads;
+    if (k < K) xs[split_index(k, K)] = (v[u] * inv) * g[u];
+  }
+  __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
+// Consuming one weight phase
+// ---------------------------------------------------------------------------
+constexpr int kRing = 4;  // weight buffers per CTA
+
+struct Ring {
+  char* buf[kRing];
+  uint64_t* bar;   // [kRing] in shared memory
+  int buf_bytes;
+  unsigned g;      // chunks consumed so far
+  Cursor cur;      // thread 0: next chunk to issue
+};
+
+__device__ __forceinline__ void pair_epilogue(const MegaArgs& a, int kind, int pair, float y0,
+                                              float y1, float& bv, int& bi) {
+  const int r0 = 2 * pair;
+  switch (kind) {
+    case W_QKV:
+      a.qkv[r0] = y0;
+      a.qkv[r0 + 1] = y1;
+      break;
+    case W_O:
+    case W_DOWN:
+      a.x[r0] = __ldcg(a.x + r0) + y0;
+      a.x[r0 + 1] = __ldcg(a.x + r0 + 1) + y1;
+      break;
+    case W_GU:
+      a.h[pair] = swiglu(y0, y1);
+      break;
+    default:
+      if (a.write_logits) {
+        a.logits[r0] = y0;
+        a.logits[r0 + 1] = y1;
+      }
+      if (y0 > bv || (y0 == bv && r0 < bi)) {
+        bv = y0;
+        bi = r0;
+      }
+      if (y1 > bv || (y1 == bv && r0 + 1 < bi)) {
+        bv = y1;
+        bi = r0 + 1;
+      }
+      break;
+  }
+}
+
+// Consumes every chunk of weight phase `wp` with activations in xs (split
+// layout, K floats). For the LM head, (bv, bi) track the warp's argmax.
+__device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const float* xs,
+                              float* red, float& bv, int& bi, int nbar) {
+  trace_mark(a, nbar, MARK_STAGED);
+  const Phase ph = weight_phase(a, wp);
+  const Slice s = s_slices[ph.kind];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int K = ph.K;
+  const float4* lo4 = reinterpret_cast<const float4*>(xs);
+  const float4* hi4 = lo4 + (K >> 3);
+  float acc0 = 0.f, acc1 = 0.f;  // split rows: running sums (thread 0)
+  for (int ci = 0; ci < s.nchunks; ci++) {
+    const int b = r.g % kRing;
+    wait_buffer(a, r.bar + b, (r.g / kRing) & 1);
+    if (ci == 0) trace_mark(a, nbar, MARK_READY);
+    const Chunk c = slice_chunk(s, ph, ci);
+    const uint16_t* wb = reinterpret_cast<const uint16_t*>(r.buf[b]);
+    if (s.ppc) {
+      for (int p = c.p0 + warp; p < c.p1; p += kWarps) {
+        const uint16_t* w0 = wb + (size_t)(p - c.p0) * 2 * K;
+        const uint16_t* w1 = w0 + K;
+        // One accumulator per element slot: no FMA dependency chain longer
+        // than K / 256.
+        float s0[8], s1[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) s0[i] = s1[i] = 0.f;
+#pragma unroll 4
+        for (int k = lane * 8; k < K; k += 256) {
+          const uint4 v0 = *reinterpret_cast<const uint4*>(w0 + k);
+          const uint4 v1 = *reinterpret_cast<const uint4*>(w1 + k);
+          const float4 xa = lo4[k >> 3], xb = hi4[k >> 3];
+          acc8(v0, xa, xb, s0);
+          acc8(v1, xa, xb, s1);
+        }
+        float a0 = ((s0[0] + s0[1]) + (s0[2] + s0[3])) + ((s0[4] + s0[5]) + (s0[6] + s0[7]));
+        float a1 = ((s1[0] + s1[1]) + (s1[2] + s1[3])) + ((s1[4] + s1[5]) + (s1[6] + s1[7]));
+        a0 = warp_sum(a0);
+        a1 = warp_sum(a1);
+        if (lane == 0) pair_epilogue(a, ph.kind, p, a0, a1, bv, bi);
+      }
+    } else {
+      const int seg = c.k1 - c.k0;
+      const uint16_t* w0 = wb;
+      const uint16_t* w1 = wb + seg;
+      float s0[8], s1[8];
+#pragma unroll
+      for (int i = 0; i < 8; i++) s0[i] = s1[i] = 0.f;
+#pragma unroll 4
+      for (int k = warp * 256 + lane * 8; k < seg; k += kWarps * 256) {
+        const uint4 v0 = *reinterpret_cast<const uint4*>(w0 + k);
+        const uint4 v1 = *reinterpret_cast<const uint4*>(w1 + k);
+        const int kk = c.k0 + k;
+        const float4 xa = lo4[kk >> 3], xb = hi4[kk >> 3];
+        acc8(v0, xa, xb, s0);
+        acc8(v1, xa, xb, s1);
+      }
+      float a0 = ((s0[0] + s0[1]) + (s0[2] + s0[3])) + ((s0[4] + s0[5]) + (s0[6] + s0[7]));
+      float a1 = ((s1[0] + s1[1]) + (s1[2] + s1[3])) + ((s1[4] + s1[5]) + (s1[6] + s1[7]));
+      a0 = warp_sum(a0);
+      a1 = warp_sum(a1);
+      if (lane == 0) {
+        red[warp] = a0;
+        red[kWarps + warp] = a1;
+      }
+      __syncthreads();
+      if (tid == 0) {
+        for (int w = 0; w < kWarps; w++) {
+          acc0 += red[w];
+          acc1 += red[kWarps + w];
+        }
+        if (c.last_seg) {
+          pair_epilogue(a, ph.kind, c.p0, acc0, acc1, bv, bi);
+          acc0 = acc1 = 0.f;
+        }
+      }
+    }
+    if (ci == s.nchunks - 1) trace_mark(a, nbar, MARK_COMPUTED);
+    __syncthreads();  // buffer b fully read
+    if (tid == 0) cursor_issue(a, r.cur, r.buf[b], r.bar + b);
+    if (ci == s.nchunks - 1) trace_mark(a, nbar, MARK_ISSUED);
+    r.g++;
+  }
+  trace_mark(a, nbar, MARK_CONSUMED);
+}
+
+// ---------------------------------------------------------------------------
+// Attention
+// ---------------------------------------------------------------------------
+// One warp: out[i] = RoPE(RMSNorm(src) * nw) for a head of HD values
+// (source/transformer.c:1293-1323); nw may be null. `scratch` holds HD
+// floats private to the warp.
+template <int HD>
+__device__ void head_norm_rope(const MegaArgs& a, const float* src, const uint16_t* nw,
+                               int pos, float* scratch, float* out) {
+  constexpr int V = HD / 32;
+  const int lane = threadIdx.x & 31;
+  float v[V];
+#pragma unroll
+  for (int j = 0; j < V; j++) v[j] = __ldcg(src + lane + 32 * j);
+  if (nw) {
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < V; j++) ss += v[j] * v[j];
+    ss = warp_sum(ss);
+    ss /= (float)HD;
+    const float inv = 1.0f / sqrtf(ss + a.eps);
+#pragma unroll
+    for (int j = 0; j < V; j++) v[j] = (v[j] * inv) * bf16_to_f32(nw[lane + 32 * j]);
+  }
+#pragma unroll
+  for (int j = 0; j < V; j++) scratch[lane + 32 * j] = v[j];
+  __syncwarp();
+  const float* cs = a.rope + (size_t)pos * HD;
+  const int off = a.pair_offset;
+#pragma unroll
+  for (int j = 0; j < V; j++) {
+    const int i = lane + 32 * j;
+    const bool first = (a.pair_stride == 1) ? (i < a.pair_bound) : ((i & 1) == 0);
+    float o;
+    if (first) {
+      o = scratch[i] * cs[i] - scratch[i + off] * cs[i + off];
+    } else {
+      const int hh = i - off;
+      o = scratch[hh] * cs[hh + off] + scratch[i] * cs[hh];
+    }
+    out[i] = o;
+  }
+  __syncwarp();
+}
+
+// L2 prefetch of the cache rows [s_begin, min(s_end, pos)) of this CTA's
+// attention items (rows below `pos` are final).
+template <int HD>
+__device__ void prefetch_kv(const MegaArgs& a, int l, int pos) {
+  if (threadIdx.x != 0) return;
+  const int items = a.KHl * a.nsplit;
+  for (int it = blockIdx.x; it < items; it += gridDim.x) {
+    const int kh = it % a.KHl, sp = it / a.KHl;
+    const int s0 = sp * a.split_len;
+    const int s1 = min(s0 + a.split_len, pos);
+    if (s1 <= s0) continue;
+    const size_t off = ((size_t)l * a.KHl + kh) * a.ctx * HD + (size_t)s0 * HD;
+    const uint32_t bytes = (uint32_t)(s1 - s0) * HD * 4;
+    prefetch_l2(a.kc + off, bytes);
+    prefetch_l2(a.vc + off, bytes);
+  }
+}
+
+// L2 prefetch of the small per-layer vectors of layer `l` (norm gains), or
+// of the final norm when l == L: they are evicted between decode steps by
+// the weight stream, and every CTA reads them on a phase's critical path.
+__device__ void prefetch_gains(const MegaArgs& a, int l) {
+  if (threadIdx.x != 32) return;
+  if (l >= a.L) {
+    prefetch_l2(a.out_norm, (uint32_t)a.D * 2);
+    return;
+  }
+  const MegaLayer& ly = s_layers[l];
+  prefetch_l2(ly.attn_norm, (uint32_t)a.D * 2);
+  prefetch_l2(ly.ffn_norm, (uint32_t)a.D * 2);
+  if (ly.q_norm) prefetch_l2(ly.q_norm, (uint32_t)a.HD * 2);
+  if (ly.k_norm) prefetch_l2(ly.k_norm, (uint32_t)a.HD * 2);
+}
+
+template <int HD, int G>
+__device__ void attn_item(const MegaArgs& a, const MegaLayer& ly, int l, int kh, int sp,
+                          int pos, float* sm) {
+  constexpr int V = HD / 32;
+  constexpr int QF = HD / 16;
+  float* qs = sm;                      // [G][HD]
+  float* wm = qs + G * HD;             // [kWarps][G]
+  float* wl = wm + kWarps * G;         // [kWarps][G]
+  float* wacc = wl + kWarps * G;       // [kWarps][G][HD]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const size_t layer_off = (size_t)l * a.KHl * a.ctx * HD;
+  float* kb = a.kc + layer_off + (size_t)kh * a.ctx * HD;
+  float* vb = a.vc + layer_off + (size_t)kh * a.ctx * HD;
+  const int s_begin = sp * a.split_len;
+  const int s_end = min(s_begin + a.split_len, pos + 1);
+
+  if (warp < G)
+    head_norm_rope<HD>(a, a.qkv + (size_t)(kh * G + warp) * HD, ly.q_norm, pos,
+                       wacc + (size_t)warp * HD, qs + warp * HD);
+  if (warp == kWarps - 1 && pos >= s_begin && pos < s_begin + a.split_len) {
+    head_norm_rope<HD>(a, a.qkv + (size_t)(a.QHl + kh) * HD, ly.k_norm, pos,
+                       wacc + (size_t)warp * HD, kb + (size_t)pos * HD);
+    const float* vsrc = a.qkv + (size_t)(a.QHl + a.KHl + kh) * HD;
+    for (int i = lane; i < HD; i += 32) vb[(size_t)pos * HD + i] = __ldcg(vsrc + i);
+  }
+  __syncthreads();
+
+  float m[G], lsum[G], acc[G][V];
+#pragma unroll
+  for (int g = 0; g < G; g++) {
+    m[g] = -INFINITY;
+    lsum[g] = 0.f;
+#pragma unroll
+    for (int v = 0; v < V; v++) acc[g][v] = 0.f;
+  }
+  const int j = lane >> 2, qd = lane & 3;
+  const float div = sqrtf((float)HD);
+  for (int base = s_begin + warp * 8; base < s_end; base += kPosPerPass) {
+    const int s = base + j;
+    const bool valid = s < s_end;
+    float d[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) d[g] = 0.f;
+    float4 kv[QF];
+    if (valid) {
+      const float4* kr = reinterpret_cast<const float4*>(kb + (size_t)s * HD);
+#pragma unroll
+      for (int i = 0; i < QF; i++) kv[i] = __ldcg(kr + qd + 4 * i);
+    }
+    float vv[8][V];
+#pragma unroll
+    for (int jj = 0; jj < 8; jj++) {
+      const int sj = base + jj;
+#pragma unroll
+      for (int v = 0; v < V; v++)
+        vv[jj][v] = (sj < s_end) ? __ldcg(vb + (size_t)sj * HD + lane * V + v) : 0.f;
+    }
+    if (valid) {
+#pragma unroll
+      for (int i = 0; i < QF; i++) {
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+          const float4 q4 = *reinterpret_cast<const float4*>(&qs[g * HD + (qd + 4 * i) * 4]);
+          d[g] = fmaf(q4.x, kv[i].x, d[g]);
+          d[g] = fmaf(q4.y, kv[i].y, d[g]);
+          d[g] = fmaf(q4.z, kv[i].z, d[g]);
+          d[g] = fmaf(q4.w, kv[i].w, d[g]);
+        }
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+      float dd = d[g];
+      dd += __shfl_xor_sync(0xFFFFFFFFu, dd, 1);
+      dd += __shfl_xor_sync(0xFFFFFFFFu, dd, 2);
+      const float sc = valid ? dd / div : -INFINITY;
+      float mx = sc;
+      mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 4));
+      mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 8));
+      mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 16));
+      const float mn = fmaxf(m[g], mx);
+      const float corr = expf(m[g] - mn);
+      const float p = valid ? expf(sc - mn) : 0.f;
+      float ps = (qd == 0) ? p : 0.f;
+      ps += __shfl_xor_sync(0xFFFFFFFFu, ps, 4);
+      ps += __shfl_xor_sync(0xFFFFFFFFu, ps, 8);
+      ps += __shfl_xor_sync(0xFFFFFFFFu, ps, 16);
+      lsum[g] = lsum[g] * corr + ps;
+#pragma unroll
+      for (int v = 0; v < V; v++) acc[g][v] *= corr;
+#pragma unroll
+      for (int jj = 0; jj < 8; jj++) {
+        const float pj = __shfl_sync(0xFFFFFFFFu, p, jj * 4);
+#pragma unroll
+        for (int v = 0; v < V; v++) acc[g][v] = fmaf(pj, vv[jj][v], acc[g][v]);
+      }
+      m[g] = mn;
+    }
+  }
+  __syncthreads();  // the q/k warps' scratch use of wacc is over
+#pragma unroll
+  for (int g = 0; g < G; g++) {
+    if (lane == 0) {
+      wm[warp * G + g] = m[g];
+      wl[warp * G + g] = lsum[g];
+    }
+#pragma unroll
+    for (int v = 0; v < V; v++) wacc[((size_t)warp * G + g) * HD + lane * V + v] = acc[g][v];
+  }
+  __syncthreads();
+  const int nsplit = a.nsplit;
+  for (int e = tid; e < G * HD; e += kThreads) {
+    const int g = e / HD, dd = e % HD;
+    float M = -INFINITY;
+    for (int w = 0; w < kWarps; w++) M = fmaxf(M, wm[w * G + g]);
+    float L = 0.f, A = 0.f;
+    if (M != -INFINITY) {
+      for (int w = 0; w < kWarps; w++) {
+        const float mw = wm[w * G + g];
+        if (mw == -INFINITY) continue;
+        const float c = expf(mw - M);
+        L += wl[w * G + g] * c;
+        A += wacc[((size_t)w * G + g) * HD + dd] * c;
+      }
+    }
+    // Partial record: [m, l, -, -, acc[HD]] (16-byte aligned acc).
+    float* P = a.attn_partial + ((size_t)(kh * G + g) * nsplit + sp) * (HD + 4);
+    if (dd == 0) {
+      P[0] = M;
+      P[1] = L;
+    }
+    P[4 + dd] = A;
+  }
+  // The splits are merged by every CTA while it stages the O phase input
+  // (stage_attention), after the grid barrier.
+  __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
+// The kernel
+// ---------------------------------------------------------------------------
+template <int HD, int G>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_mega_decode(const __grid_constant__ MegaArgs a, int buf_bytes) {
+  extern __shared__ __align__(128) char dyn[];
+  __shared__ float red[32];
+  __shared__ float cbest_v[kWarps];
+  __shared__ int cbest_i[kWarps];
+  __shared__ __align__(8) uint64_t ring_bar[kRing];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  Ring r;
+  for (int i = 0; i < kRing; i++) r.buf[i] = dyn + (size_t)i * buf_bytes;
+  r.bar = ring_bar;
+  r.buf_bytes = buf_bytes;
+  r.g = 0;
+  r.cur = {0, 0, 0};
+  float* xs = reinterpret_cast<float*>(dyn + (size_t)kRing * buf_bytes);
+  for (int i = threadIdx.x; i < a.L; i += kThreads) s_layers[i] = a.layers[i];
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kRing; i++) mbar_init(&ring_bar[i], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (threadIdx.x < 5) {
+    // Layer 0's phases stand for every layer (same shapes).
+    const int wp = (threadIdx.x == W_LM) ? 4 * a.L : threadIdx.x;
+    s_slices[threadIdx.x] = cta_slice(weight_phase(a, wp), buf_bytes);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int i = 0; i < kRing; i++) cursor_issue(a, r.cur, r.buf[i], &ring_bar[i]);
+  int nbar = 0;
+  int pos = __ldcg(a.pos);
+  int token = __ldcg(a.tok);
+  int step = __ldcg(a.step);
+  const int QD = a.QHl * a.HD;
+  const int attn_items = a.KHl * a.nsplit;
+  float bv = -INFINITY;
+  int bi = 0x7FFFFFFF;
+
+  for (int s = 0; s < a.steps; s++) {
+    for (int l = 0; l < a.L; l++) {
+      const MegaLayer& ly = s_layers[l];
+      // QKV
+      prefetch_kv<HD>(a, l, pos);
+      prefetch_gains(a, l + 1);
+      if (l == 0)
+        stage_embedding(a, token, ly.attn_norm, xs, red);
+      else
+        stage_x(a.x, ly.attn_norm, a.eps, a.D, xs, red);
+      consume_phase(a, r, 4 * l + W_QKV, xs, red, bv, bi, nbar);
+      grid_barrier(a, nbar);
+      // ATTN
+      for (int it = blockIdx.x; it < attn_items; it += gridDim.x)
+        attn_item<HD, G>(a, ly, l, it % a.KHl, it / a.KHl, pos, xs);
+      grid_barrier(a, nbar);
+      // O + residual (input: the attention splits, merged here)
+      stage_attention<HD>(a, xs, xs + QD);
+      consume_phase(a, r, 4 * l + W_O, xs, red, bv, bi, nbar);
+      grid_barrier(a, nbar);
+      // gate/up + SwiGLU
+      stage_x(a.x, ly.ffn_norm, a.eps, a.D, xs, red);
+      consume_phase(a, r, 4 * l + W_GU, xs, red, bv, bi, nbar);
+      grid_barrier(a, nbar);
+      // down + residual
+      stage_x(a.h, nullptr, 0.f, a.Fl, xs, red);
+      consume_phase(a, r, 4 * l + W_DOWN, xs, red, bv, bi, nbar);
+      grid_barrier(a, nbar);
+    }
+    // LM head with per-CTA argmax
+    prefetch_gains(a, 0);  // next step's layer 0
+    stage_x(a.x, a.out_norm, a.eps, a.D, xs, red);
+    bv = -INFINITY;
+    bi = 0x7FFFFFFF;
+    consume_phase(a, r, 4 * a.L, xs, red, bv, bi, nbar);
+    if (lane == 0) {
+      cbest_v[warp] = bv;
+      cbest_i[warp] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float v = cbest_v[0];
+      int i = cbest_i[0];
+      for (int w = 1; w < kWarps; w++) {
+        if (cbest_v[w] > v || (cbest_v[w] == v && cbest_i[w] < i)) {
+          v = cbest_v[w];
+          i = cbest_i[w];
+        }
+      }
+      a.am_val[blockIdx.x] = v;
+      a.am_idx[blockIdx.x] = i;
+    }
+    grid_barrier(a, nbar);
+    // Every CTA reduces the partials itself (no extra barrier).
+    if (warp == 0) {
+      float v = -INFINITY;
+      int i = 0x7FFFFFFF;
+      for (int b = lane; b < (int)gridDim.x; b += 32) {
+        const float vb = __ldcg(a.am_val + b);
+        const int ib = __ldcg(a.am_idx + b);
+        if (vb > v || (vb == v && ib < i)) {
+          v = vb;
+          i = ib;
+        }
+      }
+      for (int o = 16; o > 0; o >>= 1) {
+        const float v2 = __shfl_xor_sync(0xFFFFFFFFu, v, o);
+        const int i2 = __shfl_xor_sync(0xFFFFFFFFu, i, o);
+        if (v2 > v || (v2 == v && i2 < i)) {
+          v = v2;
+          i = i2;
+        }
+      }
+      if (lane == 0) cbest_i[0] = (i == 0x7FFFFFFF) ? 0 : i;
+    }
+    __syncthreads();
+    token = cbest_i[0];
+    if (blockIdx.x == 0 && threadIdx.x == 0 && step >= 0 && step < a.gen_len)
+      a.gen[step] = token;
+    step++;
+    pos++;
+    __syncthreads();
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    *a.tok = token;
+    *a.pos = pos;
+    *a.step = step;
+  }
+}
+
+template <int HD, int G>
+size_t attn_smem() {
+  return sizeof(float) * ((size_t)G * HD + 2 * kWarps * G + (size_t)kWarps * G * HD + 4);
+}
+
+template <int HD, int G>
+void* kernel_ptr() {
+  return (void*)k_mega_decode<HD, G>;
+}
+
+void* select(int HD, int G) {
+#define SG_SEL(h, g) \
+  if (HD == h && G == g) return kernel_ptr<h, g>();
+  SG_SEL(32, 1) SG_SEL(32, 2) SG_SEL(32, 4) SG_SEL(32, 8)
+  SG_SEL(64, 1) SG_SEL(64, 2) SG_SEL(64, 4) SG_SEL(64, 8)
+  SG_SEL(128, 1) SG_SEL(128, 2) SG_SEL(128, 4) SG_SEL(128, 8)
+#undef SG_SEL
+  return nullptr;
+}
+
+size_t select_attn_smem(int HD, int G) {
+#define SG_SEL(h, g) \
+  if (HD == h && G == g) return attn_smem<h, g>();
+  SG_SEL(32, 1) SG_SEL(32, 2) SG_SEL(32, 4) SG_SEL(32, 8)
+  SG_SEL(64, 1) SG_SEL(64, 2) SG_SEL(64, 4) SG_SEL(64, 8)
+  SG_SEL(128, 1) SG_SEL(128, 2) SG_SEL(128, 4) SG_SEL(128, 8)
+#undef SG_SEL
+  return 0;
+}
+
+// Activation / attention region, rounded to 128 bytes.
+// (matvec input; attention item; O-phase input plus split-merge weights).
+size_t act_bytes(int D, int QD, int Fl, int HD, int G) {
+  size_t k = (size_t)std::max(D, std::max(QD, Fl)) * sizeof(float);
+  k = std::max(k, select_attn_smem(HD, G));
+  k = std::max(k, sizeof(float) * ((size_t)QD + (size_t)(QD / HD) * (kMaxSplits + 1)));
+  return (k + 127) / 128 * 128;
+}
+
+}  // namespace
+
+// Two weight buffers take what the activations leave of the budget.
+size_t mega_smem_bytes(int D, int QD, int Fl, int HD, int G) {
+  const size_t act = act_bytes(D, QD, Fl, HD, G);
+  if (act + (size_t)kRing * 8 * 1024 > kSmemBudget) return 0;
+  size_t buf = (kSmemBudget - act) / kRing / 1024 * 1024;
+  return (size_t)kRing * buf + act;
+}
+
+static int buffer_bytes(size_t smem, int D, int QD, int Fl, int HD, int G) {
+  return (int)((smem - act_bytes(D, QD, Fl, HD, G)) / kRing);
+}
+
+void mega_configure(size_t smem) {
+  for (int hd : {32, 64, 128})
+    for (int g : {1, 2, 4, 8})
+      SG_CUDA(cudaFuncSetAttribute(select(hd, g), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)std::max(smem, (size_t)48 * 1024)));
+}
+
+int mega_grid(size_t smem, int HD, int G) {
+  void* k = select(HD, G);
+  if (!k || smem == 0) return 0;
+  int per_sm = 0;
+  SG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, smem));
+  if (per_sm < 1) return 0;
+  int dev, sms;
+  SG_CUDA(cudaGetDevice(&dev));
+  SG_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  return sms;
+}
+
+void mega_split(int ctx, int KHl, int grid, int* nsplit, int* split_len) {
+  int target = (grid + KHl - 1) / KHl;
+  if (target > kMaxSplits) target = kMaxSplits;
+  if (target < 1) target = 1;
+  int len = (ctx + target - 1) / target;
+  len = (len + kPosPerPass - 1) / kPosPerPass * kPosPerPass;
+  *split_len = len;
+  *nsplit = (ctx + len - 1) / len;
+}
+
+void mega_decode(const MegaArgs& a, int grid, size_t smem, cudaStream_t s) {
+  void* k = select(a.HD, a.G);
+  if (!k) SG_DIE("megakernel: unsupported head_dim / group");
+  if (a.nsplit > kMaxSplits) SG_DIE("megakernel: too many attention splits");
+  int buf = buffer_bytes(smem, a.D, a.QHl * a.HD, a.Fl, a.HD, a.G);
+  if (buf < 8 * 1024 || buf % 16) SG_DIE("megakernel: weight buffers too small");
+  // The barrier counter restarts at zero for every launch.
+  SG_CUDA(cudaMemsetAsync(a.bar, 0, 2 * sizeof(unsigned), s));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void* args[] = {(void*)&a, (void*)&buf};
+  SG_CUDA(cudaLaunchKernelExC(&cfg, k, args));
+}
+
+}  // namespace sg

@@ -800,7 +800,8 @@ __device__ __forceinline__ void argmax_merge(float& v, int& i, float v2,
 
 __global__ void __launch_bounds__(512)
     k_argmax(const float* __restrict__ logits, int n, int* out_token, int* pos,
-             int* step, int* tokens_out, float* pval, int* pidx, int* ticket) {
+             int* step, int* tokens_out, int tokens_len, float* pval, int* pidx,
+             int* ticket) {
   __shared__ float sv[32];
   __shared__ int si[32];
   __shared__ bool is_last;
@@ -842,20 +843,22 @@ __global__ void __launch_bounds__(512)
     argmax_merge(v, idx, __ldcg(pval + b), __ldcg(pidx + b));
   if (idx == 0x7FFFFFFF) idx = 0;  // all NaN: the reference returns 0
   *out_token = idx;
-  if (tokens_out) tokens_out[*step] = idx;
+  const int st = *step;
+  if (tokens_out && st >= 0 && st < tokens_len) tokens_out[st] = idx;
   *step += 1;
   if (pos) *pos += 1;
   *ticket = 0;
 }
 
 void argmax_advance(const float* logits, int n, int* out_token, int* pos,
-                    int* step, int* tokens_out, float* partial_val,
-                    int* partial_idx, int* ticket, cudaStream_t s) {
+                    int* step, int* tokens_out, int tokens_len,
+                    float* partial_val, int* partial_idx, int* ticket,
+                    cudaStream_t s) {
   int blocks = (n + 4095) / 4096;
   if (blocks > 64) blocks = 64;
   if (blocks < 1) blocks = 1;
   launch(k_argmax, dim3(blocks), dim3(512), 0, s, logits, n, out_token, pos,
-         step, tokens_out, partial_val, partial_idx, ticket);
+         step, tokens_out, tokens_len, partial_val, partial_idx, ticket);
 }
 
 // ---------------------------------------------------------------------------

@@ -2,15 +2,16 @@
 // every launch goes on `stream`. Shapes are checked on the host by the
 // callers (transformer.cu); the kernels assume:
 //   - row lengths (K) are multiples of 8 bf16 (16-byte rows),
-//   - gate/up weights are interleaved in groups of SG_GU_GROUP rows
-//     (gate rows g..g+15, then the matching up rows), see layout notes in
+//   - gate/up weights are interleaved row by row (gate row f at 2f, up row f
+//     at 2f+1; SG_GU_GROUP = 1)
+//     see the layout notes in
 //     transformer.cu.
 #pragma once
 
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#define SG_GU_GROUP 16
+#define SG_GU_GROUP 1
 
 namespace sg {
 
@@ -84,12 +85,13 @@ struct AttnPrefillArgs {
 void attn_prefill(const AttnPrefillArgs& a, cudaStream_t s);
 
 // Greedy argmax over rows [0, n): first index of the strict maximum, as
-// source/sampler.c:92-102. Writes *out_token, appends it to
-// tokens_out[*step] (if tokens_out), advances *step by 1 and, when pos is
-// not null, *pos by 1.
+// source/sampler.c:92-102. Writes *out_token, stores it at
+// tokens_out[*step] when tokens_out is set and *step < tokens_len, advances
+// *step by 1 and, when pos is not null, *pos by 1.
 void argmax_advance(const float* logits, int n, int* out_token, int* pos,
-                    int* step, int* tokens_out, float* partial_val,
-                    int* partial_idx, int* ticket, cudaStream_t s);
+                    int* step, int* tokens_out, int tokens_len,
+                    float* partial_val, int* partial_idx, int* ticket,
+                    cudaStream_t s);
 
 // --- Mixture of experts (MXFP4 experts) ---------------------------------
 // Router top-k: per token, the k largest logits (ties -> lower index),

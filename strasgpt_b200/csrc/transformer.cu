@@ -13,8 +13,8 @@
 //   wqkv[l]        bf16 [(QHl+2KHl)*HD][D]  q rows of this rank's heads,
 //                                         then its k rows, then its v rows
 //   wo[l]          bf16 [D][QHl*HD]       column slice of o_proj
-//   wgu[l]         bf16 [2*Fl][D]         gate/up rows interleaved in
-//                                         groups of 16 (g0..15,u0..15,...)
+//   wgu[l]         bf16 [2*Fl][D]         gate/up rows interleaved row by
+//                                         row (g0,u0,g1,u1,...)
 //   wd[l]          bf16 [D][Fl]           column slice of down_proj
 //   experts[l]     u8 codes/scales of the experts this rank owns
 //   k/v cache      fp32 [L][KHl][ctx][HD] this rank's kv heads
@@ -22,6 +22,7 @@
 //                                         reference's expressions
 #include "common.cuh"
 #include "kernels.h"
+#include "mega.h"
 
 #include <fcntl.h>
 #include <omp.h>
@@ -106,6 +107,15 @@ struct transformer_state {
   cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
   std::vector<void*> allocs;
   // profiling (eager launches between events)
+  // persistent decode megakernel (dense models, one GPU)
+  bool use_mega = false;
+  int mega_grid = 0, mega_nsplit = 1, mega_split_len = 1;
+  size_t mega_smem = 0;
+  sg::MegaLayer* mega_layers = nullptr;  // device [L]
+  unsigned* bar = nullptr;               // [2]
+  int* err = nullptr;
+  unsigned long long* trace = nullptr;   // STRASGPT_MEGA_TRACE=<file>
+  int trace_barriers = 0;
   size_t launches = 0;        // kernels enqueued (graph nodes at capture)
   size_t graph_nodes = 0;     // kernels in one greedy-graph replay
   strasgpt_kernel_profile_t* prof = nullptr;
@@ -509,12 +519,53 @@ void alloc_state(const W_t* w, const transformer_configuration_t* c, S_t* s) {
   s->pos = I32(1);
   s->step = I32(1);
   s->gen = I32((size_t)s->ctx + 1);
+  // Device-side token loop state starts at zero (cudaMalloc memory is not).
+  SG_CUDA(cudaMemset(s->tok, 0, T * 4));
+  SG_CUDA(cudaMemset(s->pos, 0, 4));
+  SG_CUDA(cudaMemset(s->step, 0, 4));
+  SG_CUDA(cudaMemset(s->gen, 0, ((size_t)s->ctx + 1) * 4));
   sg::attn_decode_split(s->ctx, w->KHl, &s->nsplit, &s->split_len);
-  s->attn_partial = F32((size_t)w->QHl * s->nsplit * (HD + 2));
+  // Megakernel decode: dense models on one GPU, when a CTA fits on every SM.
+  s->use_mega = !w->moe && w->world == 1 && (w->Vl % 2 == 0) && w->L <= 96 &&
+                w->D <= 8192 && env_int("STRASGPT_MEGA", 1) != 0;
+  if (s->use_mega) {
+    s->mega_smem = sg::mega_smem_bytes(w->D, w->QHl * w->HD, w->Fl, w->HD, w->G);
+    if (s->mega_smem == 0) s->use_mega = false;
+  }
+  if (s->use_mega) {
+    sg::mega_configure(s->mega_smem);
+    s->mega_grid = sg::mega_grid(s->mega_smem, w->HD, w->G);
+    if (s->mega_grid <= 0) s->use_mega = false;
+  }
+  int max_split = s->nsplit;
+  if (s->use_mega) {
+    sg::mega_split(s->ctx, w->KHl, s->mega_grid, &s->mega_nsplit, &s->mega_split_len);
+    max_split = std::max(max_split, s->mega_nsplit);
+    std::vector<sg::MegaLayer> ml(w->L);
+    for (int l = 0; l < w->L; l++) {
+      const Layer& y = w->layer[l];
+      ml[l] = {y.attn_norm, y.wqkv, y.q_norm, y.k_norm, y.wo, y.ffn_norm, y.wgu, y.wd};
+    }
+    s->mega_layers = (sg::MegaLayer*)dalloc(s->allocs, sizeof(sg::MegaLayer) * w->L, nullptr);
+    SG_CUDA(cudaMemcpy(s->mega_layers, ml.data(), sizeof(sg::MegaLayer) * w->L,
+                       cudaMemcpyHostToDevice));
+    s->bar = (unsigned*)I32(2);
+    s->err = I32(1);
+    if (getenv("STRASGPT_MEGA_TRACE")) {
+      // Barrier timestamps of the first two decode steps of a launch.
+      s->trace_barriers = 2 * (5 * w->L + 1);
+      const size_t n = (size_t)s->trace_barriers * s->mega_grid * sg::kMegaTraceWidth;
+      s->trace = (unsigned long long*)dalloc(s->allocs, n * 8, nullptr);
+      SG_CUDA(cudaMemset(s->trace, 0, n * 8));
+    }
+    SG_CUDA(cudaMemset(s->bar, 0, 8));
+    SG_CUDA(cudaMemset(s->err, 0, 4));
+  }
+  s->attn_partial = F32((size_t)w->QHl * max_split * (HD + 4));
   s->attn_ticket = I32(w->KHl);
   SG_CUDA(cudaMemset(s->attn_ticket, 0, w->KHl * 4));
-  s->am_val = F32(64);
-  s->am_idx = I32(64);
+  s->am_val = F32(1024);
+  s->am_idx = I32(1024);
   s->am_ticket = I32(1);
   SG_CUDA(cudaMemset(s->am_ticket, 0, 4));
   if (w->moe) {
@@ -640,8 +691,35 @@ struct Runner {
   void argmax(int advance_pos) {
     launch(FAM_ARGMAX, (double)w->Vl * 4, [&] {
       sg::argmax_advance(s->logits, w->Vl, s->tok, advance_pos ? s->pos : nullptr,
-                         s->step, s->gen, s->am_val, s->am_idx, s->am_ticket, st);
+                         s->step, s->gen, s->ctx + 1, s->am_val, s->am_idx,
+                         s->am_ticket, st);
     });
+  }
+
+  // `steps` decode steps in one persistent launch, starting from the token
+  // in s->tok at position *s->pos (see decode_mega.cu).
+  void mega(int steps, bool write_logits) {
+    sg::MegaArgs a;
+    a.D = w->D; a.HD = w->HD; a.QHl = w->QHl; a.KHl = w->KHl; a.G = w->G;
+    a.Fl = w->Fl; a.Vl = w->Vl; a.L = w->L; a.QKVl = w->QKVl; a.ctx = s->ctx;
+    a.eps = w->eps; a.layers = s->mega_layers;
+    a.emb = w->emb; a.out_norm = w->out_norm; a.out_w = w->out_w;
+    a.rope = s->rope;
+    a.pair_bound = (int)c->rope_pair_bound;
+    a.pair_offset = (int)c->rope_pair_offset;
+    a.pair_stride = (int)c->rope_pair_stride;
+    a.x = s->x; a.qkv = s->qkv; a.att = s->att; a.h = s->h; a.logits = s->logits;
+    a.kc = s->kc; a.vc = s->vc;
+    a.attn_partial = s->attn_partial; a.attn_ticket = s->attn_ticket;
+    a.nsplit = s->mega_nsplit; a.split_len = s->mega_split_len;
+    a.am_val = s->am_val; a.am_idx = s->am_idx;
+    a.tok = s->tok; a.pos = s->pos; a.step = s->step; a.gen = s->gen;
+    a.gen_len = s->ctx + 1;
+    a.bar = s->bar; a.err = s->err;
+    a.steps = steps; a.write_logits = write_logits ? 1 : 0;
+    a.trace = s->trace; a.trace_barriers = s->trace_barriers;
+    s->launches++;
+    sg::mega_decode(a, s->mega_grid, s->mega_smem, st);
   }
 
   // T > 1 tokens already in s->tok at host-known position pos0.
@@ -736,6 +814,28 @@ void require_single_rank(const W_t* w) {
     SG_DIE("tensor-parallel forward needs the communicator (world > 1)");
 }
 
+// After a synchronize: a megakernel barrier that timed out is fatal. With
+// STRASGPT_MEGA_TRACE=<file>, the barrier timestamps of the last launch
+// ([barrier][cta][arrive, release], uint64 ns) are written to <file>.
+void check_mega_error(S_t* s) {
+  if (!s->use_mega) return;
+  int err = 0;
+  SG_CUDA(cudaMemcpy(&err, s->err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (err) SG_DIE("decode megakernel: a grid barrier or weight copy wait timed out");
+  if (s->trace) {
+    const size_t n = (size_t)s->trace_barriers * s->mega_grid * sg::kMegaTraceWidth;
+    std::vector<unsigned long long> h(n);
+    SG_CUDA(cudaMemcpy(h.data(), s->trace, n * 8, cudaMemcpyDeviceToHost));
+    FILE* f = fopen(getenv("STRASGPT_MEGA_TRACE"), "wb");
+    if (f) {
+      const int hdr[3] = {s->trace_barriers, s->mega_grid, sg::kMegaTraceWidth};
+      fwrite(hdr, sizeof(hdr), 1, f);
+      fwrite(h.data(), 8, n, f);
+      fclose(f);
+    }
+  }
+}
+
 // Process `T` host tokens as chunks; copy logits of the last `n` of them to
 // the host buffer `out` (row-major [n][V]).
 void predict_impl(transformer_t* t, size_t T, const int* tok, size_t n,
@@ -754,11 +854,16 @@ void predict_impl(transformer_t* t, size_t T, const int* tok, size_t n,
     set_pos(s, (int)s->cached_count);
     const size_t lo = std::max(c0, lstart);
     if (Tc == 1) {
-      if (!s->graph_logits) s->graph_logits = capture(r, false);
-      SG_CUDA(cudaGraphLaunch(s->graph_logits, s->stream));
+      if (s->use_mega) {
+        r.mega(1, true);
+      } else {
+        if (!s->graph_logits) s->graph_logits = capture(r, false);
+        SG_CUDA(cudaGraphLaunch(s->graph_logits, s->stream));
+      }
       SG_CUDA(cudaMemcpyAsync(s->h_logits, s->logits, V * 4,
                               cudaMemcpyDeviceToHost, s->stream));
       SG_CUDA(cudaStreamSynchronize(s->stream));
+      check_mega_error(s);
       memcpy(out + (lo - lstart) * V, s->h_logits, V * 4);
     } else {
       r.prefill_layers((int)Tc, (int)s->cached_count);
@@ -869,7 +974,7 @@ transformer_t* transformer_from_safetensors(struct safetensors* st) {
     w->e_end = w->e_begin + w->El;
     w->Fl = w->F;
   } else {
-    if ((w->F / N) % SG_GU_GROUP) SG_DIE("FFN shard must be a multiple of 16 rows");
+    if ((w->F / N) % SG_GU_GROUP) SG_DIE("FFN shard must be a multiple of the gate/up group");
     w->Fl = w->F / N;
   }
   SG_CUDA(cudaSetDevice(w->device));
@@ -976,7 +1081,7 @@ int transformer_generate_greedy(transformer_t* t, size_t P, const int* prompt,
     SG_DIE("context length exhausted");
   SG_CUDA(cudaSetDevice(w->device));
   Runner r{w, st, t->config, st->stream};
-  if (!st->graph_greedy) st->graph_greedy = capture(r, true);
+  if (!st->use_mega && !st->graph_greedy) st->graph_greedy = capture(r, true);
   const int zero = 0;
   SG_CUDA(cudaMemcpyAsync(st->step, &zero, 4, cudaMemcpyHostToDevice, st->stream));
   const size_t launches0 = st->launches;
@@ -998,12 +1103,19 @@ int transformer_generate_greedy(transformer_t* t, size_t P, const int* prompt,
   set_pos(st, (int)st->cached_count);
   r.argmax(0);
   SG_CUDA(cudaEventRecord(st->ev[1], st->stream));
-  for (size_t i = 0; i < S; i++) SG_CUDA(cudaGraphLaunch(st->graph_greedy, st->stream));
+  size_t graph_replays = 0;
+  if (st->use_mega) {
+    if (S > 0) r.mega((int)S, false);
+  } else {
+    for (size_t i = 0; i < S; i++) SG_CUDA(cudaGraphLaunch(st->graph_greedy, st->stream));
+    graph_replays = S;
+  }
   SG_CUDA(cudaEventRecord(st->ev[2], st->stream));
   SG_CUDA(cudaMemcpyAsync(out_tokens, st->gen, (S + 1) * sizeof(int),
                           cudaMemcpyDeviceToHost, st->stream));
   SG_CUDA(cudaStreamSynchronize(st->stream));
   SG_CUDA(cudaGetLastError());
+  check_mega_error(st);
   st->cached_count += S;
   if (timing) {
     float a = 0, b = 0;
@@ -1013,7 +1125,7 @@ int transformer_generate_greedy(transformer_t* t, size_t P, const int* prompt,
     timing->decode_ms = b;
     timing->prefill_tokens = P;
     timing->decode_steps = S;
-    timing->kernel_launches = st->launches - launches0 + S * st->graph_nodes;
+    timing->kernel_launches = st->launches - launches0 + graph_replays * st->graph_nodes;
   }
   return 0;
 }

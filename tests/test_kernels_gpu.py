@@ -34,11 +34,10 @@ def ref_swiglu(g, u):
 
 
 def interleave_gate_up(gate, up):
-    """[F][K] gate and up -> [2F][K] in groups of 16 rows (g, u, g, u...)."""
+    """[F][K] gate and up -> [2F][K] row by row (g0, u0, g1, u1, ...)."""
     import torch
     F, K = gate.shape
-    return torch.stack([gate.view(F // 16, 16, K), up.view(F // 16, 16, K)],
-                       dim=1).reshape(2 * F, K).contiguous()
+    return torch.stack([gate, up], dim=1).reshape(2 * F, K).contiguous()
 
 
 def close(got, want, what):
@@ -115,8 +114,8 @@ def test_gemm_simt(cuda, m, n, k, epi):
     elif epi == ADD:
         want = full + base
     else:
-        v = full.view(m, n // 32, 2, 16)
-        want = ref_swiglu(v[:, :, 0, :], v[:, :, 1, :]).reshape(m, n // 2)
+        v = full.view(m, n // 2, 2)
+        want = ref_swiglu(v[:, :, 0], v[:, :, 1])
     close(c, want, f"gemm {m}x{n}x{k} epi {epi}")
 
 
