@@ -34,9 +34,19 @@ int strasgpt_k_gemm_simt(const float* a, int lda, const uint16_t* w, int k,
                          int m, int n, float* c, int ldc, int epi,
                          void* stream);
 
+// Same product as strasgpt_k_gemm_simt on the tcgen05 tensor cores: A is
+// split into bf16 halves a_hi + a_lo (caller-provided [m][k] buffers,
+// 16-byte aligned, k a multiple of 8) and both are multiplied with W in fp32
+// accumulation. `err` is a device int, zero at rest, set non-zero if the
+// kernel's pipeline waits time out (C is then incomplete).
+int strasgpt_k_gemm_tc(const float* a, int lda, uint16_t* a_hi,
+                       uint16_t* a_lo, const uint16_t* w, int k, int m, int n,
+                       float* c, int ldc, int epi, int* err, void* stream);
+
 // y[t] = rmsnorm(x[t]) * w for t < T, rows of D floats.
 int strasgpt_k_rmsnorm_rows(const float* x, int t, int d, const uint16_t* w,
                             float eps, float* y, void* stream);
+
 
 #ifdef __cplusplus
 }

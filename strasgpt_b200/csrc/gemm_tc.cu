@@ -1,0 +1,350 @@
+// Prefill projections on the 5th-generation tensor cores (tcgen05 + TMA).
+//
+// C[t][r] (op)= sum_k A[t][k] W[r][k] for a chunk of T tokens, with fp32
+// activations A and bf16 weights W, accumulated in fp32. The tensor cores
+// take bf16 operands, so the activations are split on the way in:
+// A = A_hi + A_lo with A_hi = bf16(A), A_lo = bf16(A - A_hi), which keeps
+// about 16 bits of A (relative error <= 2^-17) while every product stays
+// exact in fp32. Each 16-wide K step is two MMAs into the same accumulator,
+// W x A_hi and W x A_lo, with the weight tile loaded once.
+//
+// Tile: 128 weight rows (MMA M) x 128 tokens (MMA N), K in steps of 64
+// (one 128-byte swizzle row). Four pipeline stages of {W, A_hi, A_lo}
+// tiles (48 KB each) filled by TMA with 128-byte swizzling; the fp32
+// accumulator lives in tensor memory (128 columns).
+// Warp roles (6 warps): 0 TMA producer, 1 MMA issuer (one elected thread
+// each), 2..5 epilogue (each reads the 32 TMEM lanes of its quarter with
+// tcgen05.ld, applies STORE / ADD / SwiGLU and writes C coalesced along r).
+// Every wait is bounded: a timeout sets *err and the CTA finishes without
+// touching C further; the host reports the error.
+#include "common.cuh"
+#include "gemm_tc.h"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+namespace sg {
+namespace {
+
+constexpr int BM = 128;  // weight rows per tile
+constexpr int BN = 128;  // tokens per tile
+constexpr int BK = 64;   // K per stage
+constexpr int STAGES = 4;
+constexpr int kTileBytes = BM * BK * 2;       // 16 KB (BN == BM)
+constexpr int kStageBytes = 3 * kTileBytes;   // W, A_hi, A_lo
+constexpr int kSmemBytes = STAGES * kStageBytes + 1024;  // + alignment slack
+constexpr int kThreads = 192;
+constexpr unsigned long long kTimeoutNs = 2000000000ULL;
+
+__device__ __forceinline__ uint32_t saddr(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ unsigned long long now_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n .reg .pred p;\n"
+      " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait; false (and *err set) on timeout or when *err is already set.
+__device__ bool mbar_wait(uint32_t bar, unsigned parity, int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = now_ns();
+  unsigned spins = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if ((++spins & 63) == 0) {
+      if (*(volatile int*)err) return false;
+      if (now_ns() - t0 > kTimeoutNs) {
+        atomicExch(err, 3);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+// 2D TMA tile load (x = inner element offset, a multiple of 64 -> 128-byte
+// aligned; y = row offset; rows past the tensor read as zeros).
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand tile with 128-byte
+// swizzling, 8-row swizzle atoms 1024 bytes apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);  // start address
+  d |= (uint64_t)1 << 16;                 // leading byte offset (unused here)
+  d |= (uint64_t)(1024 >> 4) << 32;       // stride byte offset
+  d |= (uint64_t)1 << 46;                 // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                 // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: bf16 x bf16 -> f32, both operands K-major.
+constexpr uint32_t kIdesc = (1u << 4)                        // D: f32
+                            | (1u << 7) | (1u << 10)         // A, B: bf16
+                            | ((uint32_t)(BN >> 3) << 17)    // N
+                            | ((uint32_t)(BM >> 4) << 24);   // M
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem, uint64_t a, uint64_t b, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem),
+      "l"(a), "l"(b), "r"(kIdesc), "r"(acc)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+struct TcParams {
+  int T;       // tokens (rows of A and C)
+  int N;       // weight rows
+  int K;
+  float* C;
+  int ldc;
+  int epi;     // EPI_STORE / EPI_ADD / EPI_SWIGLU (C has N/2 columns)
+  int* err;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    k_gemm_tc(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmAh,
+              const __grid_constant__ CUtensorMap tmAl, const TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES], acc_bar;
+  __shared__ uint32_t tmem_slot;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t sbase = (saddr(smem_raw) + 1023u) & ~1023u;
+  const int r0 = blockIdx.x * BM;  // weight rows
+  const int t0 = blockIdx.y * BN;  // tokens
+  const int nk = (p.K + BK - 1) / BK;  // the K tail reads zeros from TMA
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(saddr(&full_bar[s]), 1);
+      mbar_init(saddr(&empty_bar[s]), 1);
+    }
+    mbar_init(saddr(&acc_bar), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     saddr(&tmem_slot)),
+                 "r"(BN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  }
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = tmem_slot;
+
+  if (warp == 0) {
+    // TMA producer (one thread)
+    if (lane == 0) {
+      for (int kb = 0; kb < nk; kb++) {
+        const int s = kb % STAGES;
+        if (kb >= STAGES && !mbar_wait(saddr(&empty_bar[s]), ((kb / STAGES) - 1) & 1, p.err))
+          break;
+        const uint32_t st = sbase + s * kStageBytes;
+        const uint32_t fb = saddr(&full_bar[s]);
+        mbar_expect_tx(fb, kStageBytes);
+        tma_load_2d(st, &tmW, kb * BK, r0, fb);
+        tma_load_2d(st + kTileBytes, &tmAh, kb * BK, t0, fb);
+        tma_load_2d(st + 2 * kTileBytes, &tmAl, kb * BK, t0, fb);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // MMA issuer (one thread)
+    if (lane == 0) {
+      for (int kb = 0; kb < nk; kb++) {
+        const int s = kb % STAGES;
+        if (!mbar_wait(saddr(&full_bar[s]), (kb / STAGES) & 1, p.err)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t st = sbase + s * kStageBytes;
+#pragma unroll
+        for (int k = 0; k < BK / 16; k++) {
+          const uint64_t aw = sw128_desc(st + k * 32);
+          const uint64_t bh = sw128_desc(st + kTileBytes + k * 32);
+          const uint64_t bl = sw128_desc(st + 2 * kTileBytes + k * 32);
+          mma_bf16(tmem, aw, bh, (kb | k) != 0);
+          mma_bf16(tmem, aw, bl, 1);
+        }
+        mma_commit(saddr(&empty_bar[s]));
+      }
+      mma_commit(saddr(&acc_bar));
+    }
+    __syncwarp();
+  } else {
+    // Epilogue: warp w owns TMEM lanes (w % 4) * 32 .. +31 = weight rows.
+    const int q = warp & 3;
+    const bool ok = mbar_wait(saddr(&acc_bar), 0, p.err);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (ok && !*(volatile int*)p.err) {
+      const int r = r0 + q * 32 + lane;
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        if (t0 + c0 >= p.T) break;  // warp-uniform
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+          const int t = t0 + c0 + j;
+          if (p.epi == EPI_SWIGLU) {
+            const float up = __shfl_down_sync(0xFFFFFFFFu, v[j], 1);
+            if (t < p.T && (r & 1) == 0 && r + 1 < p.N)
+              p.C[(size_t)t * p.ldc + (r >> 1)] = swiglu(v[j], up);
+          } else if (t < p.T && r < p.N) {
+            float* c = p.C + (size_t)t * p.ldc + r;
+            if (p.epi == EPI_STORE)
+              *c = v[j];
+            else
+              *c += v[j];
+          }
+        }
+      }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  }
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN)
+                 : "memory");
+  }
+}
+
+// fp32 -> (bf16 hi, bf16 lo) with hi = RNE(x), lo = RNE(x - hi).
+__device__ __forceinline__ uint16_t f2bf(float f) {
+  uint32_t u = __float_as_uint(f);
+  if ((u & 0x7F800000u) == 0x7F800000u) return (uint16_t)((u >> 16) | ((u & 0xFFFF) ? 0x40 : 0));
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+
+__global__ void k_split_hi_lo(const float* __restrict__ x, int ldx, int T, int K,
+                              uint16_t* __restrict__ hi, uint16_t* __restrict__ lo) {
+  pdl_trigger();
+  pdl_wait();
+  const size_t n = (size_t)T * K;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t t = i / K, k = i % K;
+    const float v = x[t * ldx + k];
+    const uint16_t h = f2bf(v);
+    const float hv = __uint_as_float((uint32_t)h << 16);
+    hi[i] = h;
+    lo[i] = f2bf(v - hv);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    SG_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q));
+    if (q != cudaDriverEntryPointSuccess || !ptr) SG_DIE("cuTensorMapEncodeTiled unavailable");
+    fn = (PFN_cuTensorMapEncodeTiled_v12000)ptr;
+  }
+  return fn;
+}
+
+}  // namespace
+
+// Row-major bf16 matrix [rows][K] as a TMA tensor with 64 x 128 boxes and
+// 128-byte swizzling.
+void tc_make_map(TcMap* m, const uint16_t* base, int rows, int K) {
+  if (K % 8) SG_DIE("tensor-core GEMM: K must be a multiple of 8");
+  if (rows <= 0) SG_DIE("tensor-core GEMM: empty matrix");
+  if (((uintptr_t)base) % 16) SG_DIE("tensor-core GEMM: base must be 16-byte aligned");
+  CUtensorMap* map = reinterpret_cast<CUtensorMap*>(m->bytes);
+  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  const cuuint32_t box[2] = {BK, BM};
+  const cuuint32_t estride[2] = {1, 1};
+  CUresult r = encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)base, dims, strides,
+                           box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) SG_DIE("cuTensorMapEncodeTiled failed");
+  m->rows = rows;
+  m->K = K;
+}
+
+void tc_split(const float* x, int ldx, int T, int K, uint16_t* hi, uint16_t* lo, cudaStream_t s) {
+  const size_t n = (size_t)T * K;
+  int blocks = (int)((n + 255) / 256);
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  launch(k_split_hi_lo, dim3(blocks), dim3(256), 0, s, x, ldx, T, K, hi, lo);
+}
+
+void tc_gemm(const TcMap& w, const TcMap& a_hi, const TcMap& a_lo, int T, float* C, int ldc,
+             Epilogue epi, int* err, cudaStream_t s) {
+  if (w.K != a_hi.K || w.K != a_lo.K) SG_DIE("tensor-core GEMM: K mismatch");
+  if (T > a_hi.rows || T > a_lo.rows)
+    SG_DIE("tensor-core GEMM: more tokens than the activation map holds");
+  if (T <= 0) return;
+  TcParams p{T, w.rows, w.K, C, ldc, (int)epi, err};
+  dim3 grid((w.rows + BM - 1) / BM, (T + BN - 1) / BN);
+  k_gemm_tc<<<grid, kThreads, kSmemBytes, s>>>(
+      *reinterpret_cast<const CUtensorMap*>(w.bytes),
+      *reinterpret_cast<const CUtensorMap*>(a_hi.bytes),
+      *reinterpret_cast<const CUtensorMap*>(a_lo.bytes), p);
+  SG_CUDA(cudaGetLastError());
+}
+
+void tc_configure() {
+  SG_CUDA(cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kSmemBytes));
+}
+
+}  // namespace sg

@@ -1,5 +1,6 @@
 // Kernel-level C entry points (include/strasgpt_kernels.h).
 #include "common.cuh"
+#include "gemm_tc.h"
 #include "kernels.h"
 
 extern "C" {
@@ -15,6 +16,7 @@ void ensure_configured() {
   SG_CUDA(cudaGetDevice(&dev));
   if (dev < 64 && !(done & (1ull << dev))) {
     sg::configure_kernels();
+    sg::tc_configure();
     done |= 1ull << dev;
   }
 }
@@ -46,6 +48,23 @@ int strasgpt_k_gemm_simt(const float* a, int lda, const uint16_t* w, int k,
   if (k <= 0 || m <= 0 || n <= 0) SG_DIE("gemm: empty shape");
   sg::gemm_simt(a, lda, w, k, m, n, c, ldc, epilogue(epi),
                 (cudaStream_t)stream);
+  SG_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int strasgpt_k_gemm_tc(const float* a, int lda, uint16_t* a_hi,
+                       uint16_t* a_lo, const uint16_t* w, int k, int m, int n,
+                       float* c, int ldc, int epi, int* err, void* stream) {
+  ensure_configured();
+  if (k <= 0 || m <= 0 || n <= 0) SG_DIE("gemm: empty shape");
+  if (epi == STRASGPT_EPI_SWIGLU && n % 2) SG_DIE("gemm: odd swiglu rows");
+  cudaStream_t s = (cudaStream_t)stream;
+  sg::TcMap mw, mh, ml;
+  sg::tc_make_map(&mw, w, n, k);
+  sg::tc_make_map(&mh, a_hi, m, k);
+  sg::tc_make_map(&ml, a_lo, m, k);
+  sg::tc_split(a, lda, m, k, a_hi, a_lo, s);
+  sg::tc_gemm(mw, mh, ml, m, c, ldc, epilogue(epi), err, s);
   SG_CUDA(cudaGetLastError());
   return 0;
 }

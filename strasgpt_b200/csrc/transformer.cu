@@ -21,6 +21,7 @@
 //   rope table     fp32 [ctx][HD]         computed on the host with the
 //                                         reference's expressions
 #include "common.cuh"
+#include "gemm_tc.h"
 #include "kernels.h"
 #include "mega.h"
 
@@ -116,6 +117,14 @@ struct transformer_state {
   int* err = nullptr;
   unsigned long long* trace = nullptr;   // STRASGPT_MEGA_TRACE=<file>
   int trace_barriers = 0;
+  // Tensor-core prefill projections: bf16 halves of the current projection
+  // input ([chunk_max][K]) with their TMA maps for K = D, QH*HD, F; weight
+  // maps per layer (qkv, o, gate/up, down), then the LM head.
+  bool use_tc = false;
+  uint16_t *a_hi = nullptr, *a_lo = nullptr;
+  sg::TcMap in_hi[3], in_lo[3];
+  std::vector<sg::TcMap> tc_w;
+  int* tc_err = nullptr;
   size_t launches = 0;        // kernels enqueued (graph nodes at capture)
   size_t graph_nodes = 0;     // kernels in one greedy-graph replay
   strasgpt_kernel_profile_t* prof = nullptr;
@@ -573,6 +582,33 @@ void alloc_state(const W_t* w, const transformer_configuration_t* c, S_t* s) {
     s->ew = F32(T * w->topk);
     s->eidx = I32(T * w->topk);
   }
+  const int QD = w->QHl * w->HD;
+  s->use_tc = env_int("STRASGPT_TC", 1) != 0 && w->D % 8 == 0 && QD % 8 == 0 &&
+              (w->moe || w->Fl % 8 == 0);
+  if (s->use_tc) {
+    sg::tc_configure();
+    const int ks[3] = {w->D, QD, w->moe ? w->D : w->Fl};
+    const size_t kmax = (size_t)std::max(ks[0], std::max(ks[1], ks[2]));
+    s->a_hi = (uint16_t*)dalloc(s->allocs, T * kmax * 2, nullptr);
+    s->a_lo = (uint16_t*)dalloc(s->allocs, T * kmax * 2, nullptr);
+    for (int i = 0; i < 3; i++) {
+      sg::tc_make_map(&s->in_hi[i], s->a_hi, (int)T, ks[i]);
+      sg::tc_make_map(&s->in_lo[i], s->a_lo, (int)T, ks[i]);
+    }
+    s->tc_w.resize((size_t)4 * w->L + 1);
+    for (int l = 0; l < w->L; l++) {
+      const Layer& y = w->layer[l];
+      sg::tc_make_map(&s->tc_w[4 * l + 0], y.wqkv, w->QKVl, w->D);
+      sg::tc_make_map(&s->tc_w[4 * l + 1], y.wo, w->D, QD);
+      if (!w->moe) {
+        sg::tc_make_map(&s->tc_w[4 * l + 2], y.wgu, 2 * w->Fl, w->D);
+        sg::tc_make_map(&s->tc_w[4 * l + 3], y.wd, w->D, w->Fl);
+      }
+    }
+    sg::tc_make_map(&s->tc_w[4 * w->L], w->out_w, w->Vl, w->D);
+    s->tc_err = I32(1);
+    SG_CUDA(cudaMemset(s->tc_err, 0, 4));
+  }
   SG_CUDA(cudaMallocHost(&s->h_logits, (size_t)s->logit_rows_max * w->Vl * 4));
   SG_CUDA(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
   for (auto& e : s->ev) SG_CUDA(cudaEventCreate(&e));
@@ -722,6 +758,21 @@ struct Runner {
     sg::mega_decode(a, s->mega_grid, s->mega_smem, st);
   }
 
+  // Chunk projection C[t] (op)= W a[t] for t < T: on the tensor cores when
+  // the state has them (input split into bf16 halves, `ki` selects the
+  // input maps by K), else on the SIMT tiles.
+  void proj(const float* a, int K, int ki, const uint16_t* wraw, int wmap, int N, float* C,
+            int ldc, sg::Epilogue epi, int T) {
+    if (s->use_tc) {
+      launch(FAM_OTHER, 0, [&] { sg::tc_split(a, K, T, K, s->a_hi, s->a_lo, st); });
+      launch(FAM_OTHER, 0, [&] {
+        sg::tc_gemm(s->tc_w[wmap], s->in_hi[ki], s->in_lo[ki], T, C, ldc, epi, s->tc_err, st);
+      });
+    } else {
+      launch(FAM_OTHER, 0, [&] { sg::gemm_simt(a, K, wraw, K, T, N, C, ldc, epi, st); });
+    }
+  }
+
   // T > 1 tokens already in s->tok at host-known position pos0.
   void prefill_layers(int T, int pos0) {
     const int D = w->D, HD = w->HD, QD = w->QHl * HD;
@@ -729,17 +780,14 @@ struct Runner {
     for (int l = 0; l < w->L; l++) {
       const Layer& ly = w->layer[l];
       launch(FAM_OTHER, 0, [&] { sg::rmsnorm_rows(s->x, T, D, ly.attn_norm, w->eps, s->xn, st); });
-      launch(FAM_OTHER, 0, [&] {
-        sg::gemm_simt(s->xn, D, ly.wqkv, D, T, w->QKVl, s->qkv, w->QKVl,
-                      sg::EPI_STORE, st);
-      });
+      proj(s->xn, D, 0, ly.wqkv, 4 * l + 0, w->QKVl, s->qkv, w->QKVl, sg::EPI_STORE, T);
       launch(FAM_QKV, 0, [&] { sg::qkv_post(qkv_args(l, T), st); });
       sg::AttnPrefillArgs a;
       a.q = s->q; a.k_cache = kc(l); a.v_cache = vc(l);
       a.T = T; a.KHl = w->KHl; a.G = w->G; a.HD = HD; a.ctx = s->ctx;
       a.pos0 = pos0; a.att = s->att;
       launch(FAM_ATTN, 0, [&] { sg::attn_prefill(a, st); });
-      launch(FAM_OTHER, 0, [&] { sg::gemm_simt(s->att, QD, ly.wo, QD, T, D, s->x, D, sg::EPI_ADD, st); });
+      proj(s->att, QD, 1, ly.wo, 4 * l + 1, D, s->x, D, sg::EPI_ADD, T);
       launch(FAM_OTHER, 0, [&] { sg::rmsnorm_rows(s->x, T, D, ly.ffn_norm, w->eps, s->xn, st); });
       if (w->moe) {
         launch(FAM_OTHER, 0, [&] { sg::gemm_simt(s->xn, D, ly.router, D, T, w->E, s->rl, w->E, sg::EPI_STORE, st); });
@@ -748,11 +796,8 @@ struct Runner {
         launch(FAM_OTHER, 0, [&] { sg::moe_gate_up(m, st); });
         launch(FAM_OTHER, 0, [&] { sg::moe_down(m, st); });
       } else {
-        launch(FAM_OTHER, 0, [&] {
-          sg::gemm_simt(s->xn, D, ly.wgu, D, T, 2 * w->Fl, s->h, w->Fl,
-                        sg::EPI_SWIGLU, st);
-        });
-        launch(FAM_OTHER, 0, [&] { sg::gemm_simt(s->h, w->Fl, ly.wd, w->Fl, T, D, s->x, D, sg::EPI_ADD, st); });
+        proj(s->xn, D, 0, ly.wgu, 4 * l + 2, 2 * w->Fl, s->h, w->Fl, sg::EPI_SWIGLU, T);
+        proj(s->h, w->Fl, 2, ly.wd, 4 * l + 3, D, s->x, D, sg::EPI_ADD, T);
       }
     }
   }
@@ -767,10 +812,7 @@ struct Runner {
       });
     } else {
       launch(FAM_OTHER, 0, [&] { sg::rmsnorm_rows(s->x + (size_t)r0 * D, n, D, w->out_norm, w->eps, s->xn, st); });
-      launch(FAM_LMHEAD, 0, [&] {
-        sg::gemm_simt(s->xn, D, w->out_w, D, n, w->Vl, s->logits, w->Vl,
-                      sg::EPI_STORE, st);
-      });
+      proj(s->xn, D, 0, w->out_w, 4 * w->L, w->Vl, s->logits, w->Vl, sg::EPI_STORE, n);
     }
   }
 };
@@ -817,7 +859,12 @@ void require_single_rank(const W_t* w) {
 // After a synchronize: a megakernel barrier that timed out is fatal. With
 // STRASGPT_MEGA_TRACE=<file>, the barrier timestamps of the last launch
 // ([barrier][cta][arrive, release], uint64 ns) are written to <file>.
-void check_mega_error(S_t* s) {
+void check_device_errors(S_t* s) {
+  if (s->use_tc) {
+    int err = 0;
+    SG_CUDA(cudaMemcpy(&err, s->tc_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (err) SG_DIE("tensor-core projection: a TMA or MMA pipeline wait timed out");
+  }
   if (!s->use_mega) return;
   int err = 0;
   SG_CUDA(cudaMemcpy(&err, s->err, sizeof(int), cudaMemcpyDeviceToHost));
@@ -863,7 +910,7 @@ void predict_impl(transformer_t* t, size_t T, const int* tok, size_t n,
       SG_CUDA(cudaMemcpyAsync(s->h_logits, s->logits, V * 4,
                               cudaMemcpyDeviceToHost, s->stream));
       SG_CUDA(cudaStreamSynchronize(s->stream));
-      check_mega_error(s);
+      check_device_errors(s);
       memcpy(out + (lo - lstart) * V, s->h_logits, V * 4);
     } else {
       r.prefill_layers((int)Tc, (int)s->cached_count);
@@ -880,6 +927,7 @@ void predict_impl(transformer_t* t, size_t T, const int* tok, size_t n,
   }
   SG_CUDA(cudaStreamSynchronize(s->stream));
   SG_CUDA(cudaGetLastError());
+  if (T > 1) check_device_errors(s);
 }
 
 }  // namespace
@@ -1115,7 +1163,7 @@ int transformer_generate_greedy(transformer_t* t, size_t P, const int* prompt,
                           cudaMemcpyDeviceToHost, st->stream));
   SG_CUDA(cudaStreamSynchronize(st->stream));
   SG_CUDA(cudaGetLastError());
-  check_mega_error(st);
+  check_device_errors(st);
   st->cached_count += S;
   if (timing) {
     float a = 0, b = 0;
