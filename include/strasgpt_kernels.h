@@ -47,6 +47,26 @@ int strasgpt_k_gemm_tc(const float* a, int lda, uint16_t* a_hi,
 int strasgpt_k_rmsnorm_rows(const float* x, int t, int d, const uint16_t* w,
                             float eps, float* y, void* stream);
 
+// Size of the fixed device scratch of strasgpt_k_matvec_noalloc, held by
+// every GPU that loads the library until the process exits.
+#define STRASGPT_NOALLOC_SCRATCH_BYTES (4 << 20)
+
+// strasgpt_k_matvec without any allocation, for callers that own all of the
+// GPU's memory through their own pools or cannot stall the device with
+// cudaMalloc/cudaFree between decode steps. No counterpart in the reference:
+// it is an extra way in to the same projection. Same arguments and result as
+// strasgpt_k_matvec (computed split-K: fp32 sums in another order); x, w and
+// norm_w must be 16-byte aligned. Its scratch is a fixed 4 MiB device array:
+// the weight rows (2*rows for STRASGPT_EPI_SWIGLU) may be at most
+// STRASGPT_NOALLOC_SCRATCH_BYTES / 4 - 64 = 1048512; larger shapes, and
+// other invalid arguments, return -1 with a message on stderr and enqueue
+// nothing. The first call on a device looks up the scratch's address, so
+// make it before any stream capture on that device. All calls on a device
+// share the scratch: calls that overlap on the GPU race, so serialise them
+// (one stream). Returns 0 once the work is enqueued.
+int strasgpt_k_matvec_noalloc(const float* x, const uint16_t* norm_w,
+                              float eps, const uint16_t* w, int k, int rows,
+                              float* out, int epi, void* stream);
 
 #ifdef __cplusplus
 }
