@@ -8,13 +8,19 @@
 // exact in fp32. Each 16-wide K step is two MMAs into the same accumulator,
 // W x A_hi and W x A_lo, with the weight tile loaded once.
 //
-// Tile: 128 weight rows (MMA M) x 128 tokens (MMA N), K in steps of 64
-// (one 128-byte swizzle row). Four pipeline stages of {W, A_hi, A_lo}
-// tiles (48 KB each) filled by TMA with 128-byte swizzling; the fp32
-// accumulator lives in tensor memory (128 columns).
+// Tile: 128 weight rows (MMA M) x BN tokens (MMA N, BN = 32, 64 or 128), K
+// in steps of 64 (one 128-byte swizzle row). A ring of stages of
+// {W, A_hi, A_lo} tiles filled by TMA with 128-byte swizzling; the fp32
+// accumulator lives in tensor memory (BN columns). The kernel streams its
+// operands at about 64 B/clk per SM, so the host picks BN to minimise
+// waves x bytes per stage (few weight-row tiles: narrow token tiles and
+// more CTAs; many: wide tiles and fewer bytes per MMA).
 // Warp roles (6 warps): 0 TMA producer, 1 MMA issuer (one elected thread
 // each), 2..5 epilogue (each reads the 32 TMEM lanes of its quarter with
 // tcgen05.ld, applies STORE / ADD / SwiGLU and writes C coalesced along r).
+// Launched with programmatic dependent launch: the weight tiles of the first
+// stages are requested before griddepcontrol.wait, i.e. while the kernel
+// that produces the activations is still finishing.
 // Every wait is bounded: a timeout sets *err and the CTA finishes without
 // touching C further; the host reports the error.
 #include "common.cuh"
@@ -27,14 +33,26 @@ namespace sg {
 namespace {
 
 constexpr int BM = 128;  // weight rows per tile
-constexpr int BN = 128;  // tokens per tile
 constexpr int BK = 64;   // K per stage
-constexpr int STAGES = 4;
-constexpr int kTileBytes = BM * BK * 2;       // 16 KB (BN == BM)
-constexpr int kStageBytes = 3 * kTileBytes;   // W, A_hi, A_lo
-constexpr int kSmemBytes = STAGES * kStageBytes + 1024;  // + alignment slack
+constexpr int kWTileBytes = BM * BK * 2;  // 16 KB
+constexpr int kSmemBudget = 200 * 1024;
 constexpr int kThreads = 192;
 constexpr unsigned long long kTimeoutNs = 2000000000ULL;
+
+template <int BN>
+struct Cfg {
+  static constexpr int kATileBytes = BN * BK * 2;
+  static constexpr int kStageBytes = kWTileBytes + 2 * kATileBytes;
+  static constexpr int kStagesFit = (kSmemBudget - 1024) / kStageBytes;
+  static constexpr int STAGES = kStagesFit > 8 ? 8 : kStagesFit;
+  static constexpr int kSmemBytes = STAGES * kStageBytes + 1024;  // + alignment slack
+  // Instruction descriptor: bf16 x bf16 -> f32, both operands K-major,
+  // N = BN, M = 128.
+  static constexpr uint32_t kIdesc = (1u << 4)                        // D: f32
+                                     | (1u << 7) | (1u << 10)         // A, B: bf16
+                                     | ((uint32_t)(BN >> 3) << 17)    // N
+                                     | ((uint32_t)(BM >> 4) << 24);   // M
+};
 
 __device__ __forceinline__ uint32_t saddr(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
@@ -85,7 +103,8 @@ __device__ bool mbar_wait(uint32_t bar, unsigned parity, int* err) {
 }
 
 // 2D TMA tile load (x = inner element offset, a multiple of 64 -> 128-byte
-// aligned; y = row offset; rows past the tensor read as zeros).
+// aligned; y = row offset; rows past the tensor read as zeros). No
+// multicast.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
                                             uint32_t bar) {
   asm volatile(
@@ -107,17 +126,12 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
   return d;
 }
 
-// Instruction descriptor: bf16 x bf16 -> f32, both operands K-major.
-constexpr uint32_t kIdesc = (1u << 4)                        // D: f32
-                            | (1u << 7) | (1u << 10)         // A, B: bf16
-                            | ((uint32_t)(BN >> 3) << 17)    // N
-                            | ((uint32_t)(BM >> 4) << 24);   // M
-
+template <int BN>
 __device__ __forceinline__ void mma_bf16(uint32_t tmem, uint64_t a, uint64_t b, uint32_t acc) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem),
-      "l"(a), "l"(b), "r"(kIdesc), "r"(acc)
+      "l"(a), "l"(b), "r"(Cfg<BN>::kIdesc), "r"(acc)
       : "memory");
 }
 
@@ -155,9 +169,12 @@ struct TcParams {
   int* err;
 };
 
+template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmAh,
               const __grid_constant__ CUtensorMap tmAl, const TcParams p) {
+  using C = Cfg<BN>;
+  constexpr int STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES], acc_bar;
   __shared__ uint32_t tmem_slot;
@@ -186,20 +203,30 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = tmem_slot;
+  pdl_trigger();
 
   if (warp == 0) {
-    // TMA producer (one thread)
+    // TMA producer (one thread). Weights are not written by earlier kernels:
+    // the first stages' weight tiles go out before the dependency wait.
     if (lane == 0) {
+      const int pre = nk < STAGES ? nk : STAGES;
+      for (int kb = 0; kb < pre; kb++) {
+        const uint32_t fb = saddr(&full_bar[kb]);
+        mbar_expect_tx(fb, C::kStageBytes);
+        tma_load_2d(sbase + kb * C::kStageBytes, &tmW, kb * BK, r0, fb);
+      }
+      pdl_wait();
       for (int kb = 0; kb < nk; kb++) {
         const int s = kb % STAGES;
-        if (kb >= STAGES && !mbar_wait(saddr(&empty_bar[s]), ((kb / STAGES) - 1) & 1, p.err))
-          break;
-        const uint32_t st = sbase + s * kStageBytes;
+        const uint32_t st = sbase + s * C::kStageBytes;
         const uint32_t fb = saddr(&full_bar[s]);
-        mbar_expect_tx(fb, kStageBytes);
-        tma_load_2d(st, &tmW, kb * BK, r0, fb);
-        tma_load_2d(st + kTileBytes, &tmAh, kb * BK, t0, fb);
-        tma_load_2d(st + 2 * kTileBytes, &tmAl, kb * BK, t0, fb);
+        if (kb >= STAGES) {
+          if (!mbar_wait(saddr(&empty_bar[s]), ((kb / STAGES) - 1) & 1, p.err)) break;
+          mbar_expect_tx(fb, C::kStageBytes);
+          tma_load_2d(st, &tmW, kb * BK, r0, fb);
+        }
+        tma_load_2d(st + kWTileBytes, &tmAh, kb * BK, t0, fb);
+        tma_load_2d(st + kWTileBytes + C::kATileBytes, &tmAl, kb * BK, t0, fb);
       }
     }
     __syncwarp();
@@ -210,14 +237,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = kb % STAGES;
         if (!mbar_wait(saddr(&full_bar[s]), (kb / STAGES) & 1, p.err)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t st = sbase + s * kStageBytes;
+        const uint32_t st = sbase + s * C::kStageBytes;
 #pragma unroll
         for (int k = 0; k < BK / 16; k++) {
           const uint64_t aw = sw128_desc(st + k * 32);
-          const uint64_t bh = sw128_desc(st + kTileBytes + k * 32);
-          const uint64_t bl = sw128_desc(st + 2 * kTileBytes + k * 32);
-          mma_bf16(tmem, aw, bh, (kb | k) != 0);
-          mma_bf16(tmem, aw, bl, 1);
+          const uint64_t bh = sw128_desc(st + kWTileBytes + k * 32);
+          const uint64_t bl = sw128_desc(st + kWTileBytes + C::kATileBytes + k * 32);
+          mma_bf16<BN>(tmem, aw, bh, (kb | k) != 0);
+          mma_bf16<BN>(tmem, aw, bl, 1);
         }
         mma_commit(saddr(&empty_bar[s]));
       }
@@ -227,10 +254,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // Epilogue: warp w owns TMEM lanes (w % 4) * 32 .. +31 = weight rows.
     const int q = warp & 3;
+    pdl_wait();
     const bool ok = mbar_wait(saddr(&acc_bar), 0, p.err);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (ok && !*(volatile int*)p.err) {
       const int r = r0 + q * 32 + lane;
+#pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         if (t0 + c0 >= p.T) break;  // warp-uniform
         float v[32];
@@ -270,19 +299,30 @@ __device__ __forceinline__ uint16_t f2bf(float f) {
   return (uint16_t)(u >> 16);
 }
 
+// Four consecutive activations per thread (K % 4 == 0 and ldx % 4 == 0 on
+// this path), 8-byte stores of each half.
 __global__ void k_split_hi_lo(const float* __restrict__ x, int ldx, int T, int K,
                               uint16_t* __restrict__ hi, uint16_t* __restrict__ lo) {
   pdl_trigger();
   pdl_wait();
-  const size_t n = (size_t)T * K;
+  const int kq = K >> 2;
+  const size_t n = (size_t)T * kq;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x) {
-    const size_t t = i / K, k = i % K;
-    const float v = x[t * ldx + k];
-    const uint16_t h = f2bf(v);
-    const float hv = __uint_as_float((uint32_t)h << 16);
-    hi[i] = h;
-    lo[i] = f2bf(v - hv);
+    const size_t t = i / kq, k = (i % kq) * 4;
+    const float4 v = *reinterpret_cast<const float4*>(x + t * ldx + k);
+    const float f[4] = {v.x, v.y, v.z, v.w};
+    uint16_t h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      h[j] = f2bf(f[j]);
+      l[j] = f2bf(f[j] - __uint_as_float((uint32_t)h[j] << 16));
+    }
+    const size_t o = t * K + k;
+    *reinterpret_cast<uint2*>(hi + o) =
+        make_uint2(h[0] | ((uint32_t)h[1] << 16), h[2] | ((uint32_t)h[3] << 16));
+    *reinterpret_cast<uint2*>(lo + o) =
+        make_uint2(l[0] | ((uint32_t)l[1] << 16), l[2] | ((uint32_t)l[3] << 16));
   }
 }
 
@@ -298,18 +338,14 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-}  // namespace
-
-// Row-major bf16 matrix [rows][K] as a TMA tensor with 64 x 128 boxes and
-// 128-byte swizzling.
-void tc_make_map(TcMap* m, const uint16_t* base, int rows, int K) {
+void encode(TcMap* m, const uint16_t* base, int rows, int K, int box_rows) {
   if (K % 8) SG_DIE("tensor-core GEMM: K must be a multiple of 8");
   if (rows <= 0) SG_DIE("tensor-core GEMM: empty matrix");
   if (((uintptr_t)base) % 16) SG_DIE("tensor-core GEMM: base must be 16-byte aligned");
   CUtensorMap* map = reinterpret_cast<CUtensorMap*>(m->bytes);
   const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-  const cuuint32_t box[2] = {BK, BM};
+  const cuuint32_t box[2] = {BK, (cuuint32_t)box_rows};
   const cuuint32_t estride[2] = {1, 1};
   CUresult r = encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)base, dims, strides,
                            box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -318,33 +354,83 @@ void tc_make_map(TcMap* m, const uint16_t* base, int rows, int K) {
   if (r != CUDA_SUCCESS) SG_DIE("cuTensorMapEncodeTiled failed");
   m->rows = rows;
   m->K = K;
+  m->box_rows = box_rows;
+}
+
+constexpr int kWidths[3] = {32, 64, 128};
+
+template <int BN>
+void launch_bn(const TcMap& w, const TcAct& a, int wi, const TcParams& p, cudaStream_t s) {
+  dim3 grid((w.rows + BM - 1) / BM, (p.T + BN - 1) / BN);
+  launch(k_gemm_tc<BN>, grid, dim3(kThreads), (size_t)Cfg<BN>::kSmemBytes, s,
+         *reinterpret_cast<const CUtensorMap*>(w.bytes),
+         *reinterpret_cast<const CUtensorMap*>(a.hi[wi].bytes),
+         *reinterpret_cast<const CUtensorMap*>(a.lo[wi].bytes), p);
+}
+
+}  // namespace
+
+void tc_make_map(TcMap* m, const uint16_t* base, int rows, int K) { encode(m, base, rows, K, BM); }
+
+void tc_make_act(TcAct* a, const uint16_t* hi, const uint16_t* lo, int rows, int K) {
+  for (int i = 0; i < 3; i++) {
+    encode(&a->hi[i], hi, rows, K, kWidths[i]);
+    encode(&a->lo[i], lo, rows, K, kWidths[i]);
+  }
+  a->hi_base = hi;
+  a->lo_base = lo;
 }
 
 void tc_split(const float* x, int ldx, int T, int K, uint16_t* hi, uint16_t* lo, cudaStream_t s) {
-  const size_t n = (size_t)T * K;
+  if (K % 4 || ldx % 4 || ((uintptr_t)x) % 16)
+    SG_DIE("tensor-core GEMM: activations need K and their row stride in multiples of 4");
+  const size_t n = (size_t)T * (K / 4);
   int blocks = (int)((n + 255) / 256);
-  if (blocks > 148 * 16) blocks = 148 * 16;
+  if (blocks > 148 * 8) blocks = 148 * 8;
   launch(k_split_hi_lo, dim3(blocks), dim3(256), 0, s, x, ldx, T, K, hi, lo);
 }
 
-void tc_gemm(const TcMap& w, const TcMap& a_hi, const TcMap& a_lo, int T, float* C, int ldc,
-             Epilogue epi, int* err, cudaStream_t s) {
-  if (w.K != a_hi.K || w.K != a_lo.K) SG_DIE("tensor-core GEMM: K mismatch");
-  if (T > a_hi.rows || T > a_lo.rows)
-    SG_DIE("tensor-core GEMM: more tokens than the activation map holds");
+int tc_width(int rows, int T) {
+  // Streaming-bound model: time ~ waves x bytes per stage; ties go to the
+  // wider tile.
+  const int rt = (rows + BM - 1) / BM;
+  int best = 0;
+  long best_cost = 0;
+  for (int i = 2; i >= 0; i--) {
+    const int bn = kWidths[i];
+    const long ctas = (long)rt * ((T + bn - 1) / bn);
+    const long waves = (ctas + 147) / 148;
+    const long cost = waves * (kWTileBytes + 2L * bn * BK * 2);
+    if (best == 0 || cost < best_cost) {
+      best = bn;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
+void tc_gemm(const TcMap& w, const TcAct& a, int T, float* C, int ldc, Epilogue epi, int* err,
+             cudaStream_t s) {
+  if (w.K != a.hi[0].K) SG_DIE("tensor-core GEMM: K mismatch");
+  if (T > a.hi[0].rows) SG_DIE("tensor-core GEMM: more tokens than the activation map holds");
   if (T <= 0) return;
-  TcParams p{T, w.rows, w.K, C, ldc, (int)epi, err};
-  dim3 grid((w.rows + BM - 1) / BM, (T + BN - 1) / BN);
-  k_gemm_tc<<<grid, kThreads, kSmemBytes, s>>>(
-      *reinterpret_cast<const CUtensorMap*>(w.bytes),
-      *reinterpret_cast<const CUtensorMap*>(a_hi.bytes),
-      *reinterpret_cast<const CUtensorMap*>(a_lo.bytes), p);
-  SG_CUDA(cudaGetLastError());
+  const TcParams p{T, w.rows, w.K, C, ldc, (int)epi, err};
+  const int bn = tc_width(w.rows, T);
+  if (bn == 128)
+    launch_bn<128>(w, a, 2, p, s);
+  else if (bn == 64)
+    launch_bn<64>(w, a, 1, p, s);
+  else
+    launch_bn<32>(w, a, 0, p, s);
 }
 
 void tc_configure() {
-  SG_CUDA(cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               kSmemBytes));
+  SG_CUDA(cudaFuncSetAttribute(k_gemm_tc<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               Cfg<32>::kSmemBytes));
+  SG_CUDA(cudaFuncSetAttribute(k_gemm_tc<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               Cfg<64>::kSmemBytes));
+  SG_CUDA(cudaFuncSetAttribute(k_gemm_tc<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               Cfg<128>::kSmemBytes));
 }
 
 }  // namespace sg

@@ -8,19 +8,32 @@
 
 namespace sg {
 
-// A row-major bf16 matrix [rows][K] described for TMA (64 x 128 boxes,
-// 128-byte swizzle). `bytes` holds the driver's 128-byte CUtensorMap.
+// A row-major bf16 matrix [rows][K] described for TMA (boxes of 64 x
+// box_rows elements, 128-byte swizzle). `bytes` holds the driver's 128-byte
+// CUtensorMap.
 struct TcMap {
   alignas(64) unsigned char bytes[128];
   int rows = 0;
   int K = 0;
+  int box_rows = 0;
 };
 
-// K must be a multiple of 8 (16-byte rows) and base 16-byte aligned.
+// The bf16 halves of a projection input, [rows][K] each, with one map per
+// token-tile width (32, 64, 128).
+struct TcAct {
+  TcMap hi[3], lo[3];
+  const uint16_t* hi_base = nullptr;
+  const uint16_t* lo_base = nullptr;
+};
+
+// Weight matrix [rows][K]: K a multiple of 8 (16-byte rows), base 16-byte
+// aligned.
 void tc_make_map(TcMap* m, const uint16_t* base, int rows, int K);
+void tc_make_act(TcAct* a, const uint16_t* hi, const uint16_t* lo, int rows, int K);
 
 // hi[t][k] = bf16(x[t][k]), lo[t][k] = bf16(x[t][k] - hi[t][k]) for t < T
-// (hi/lo rows of K elements, x rows `ldx` floats apart).
+// (hi/lo rows of K elements, x rows `ldx` floats apart; K, ldx multiples of
+// 4, x 16-byte aligned).
 void tc_split(const float* x, int ldx, int T, int K, uint16_t* hi, uint16_t* lo,
               cudaStream_t s);
 
@@ -28,8 +41,11 @@ void tc_split(const float* x, int ldx, int T, int K, uint16_t* hi, uint16_t* lo,
 // For EPI_SWIGLU, w holds gate/up rows interleaved and C has w.rows/2
 // columns. `err` (device int, zero at rest) is set if a pipeline wait times
 // out; the caller checks it.
-void tc_gemm(const TcMap& w, const TcMap& a_hi, const TcMap& a_lo, int T, float* C, int ldc,
-             Epilogue epi, int* err, cudaStream_t s);
+void tc_gemm(const TcMap& w, const TcAct& a, int T, float* C, int ldc, Epilogue epi, int* err,
+             cudaStream_t s);
+
+// Token-tile width tc_gemm uses for `rows` weight rows and T tokens.
+int tc_width(int rows, int T);
 
 void tc_configure();
 

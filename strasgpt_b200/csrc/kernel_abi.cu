@@ -59,12 +59,12 @@ int strasgpt_k_gemm_tc(const float* a, int lda, uint16_t* a_hi,
   if (k <= 0 || m <= 0 || n <= 0) SG_DIE("gemm: empty shape");
   if (epi == STRASGPT_EPI_SWIGLU && n % 2) SG_DIE("gemm: odd swiglu rows");
   cudaStream_t s = (cudaStream_t)stream;
-  sg::TcMap mw, mh, ml;
+  sg::TcMap mw;
+  sg::TcAct act;
   sg::tc_make_map(&mw, w, n, k);
-  sg::tc_make_map(&mh, a_hi, m, k);
-  sg::tc_make_map(&ml, a_lo, m, k);
+  sg::tc_make_act(&act, a_hi, a_lo, m, k);
   sg::tc_split(a, lda, m, k, a_hi, a_lo, s);
-  sg::tc_gemm(mw, mh, ml, m, c, ldc, epilogue(epi), err, s);
+  sg::tc_gemm(mw, act, m, c, ldc, epilogue(epi), err, s);
   SG_CUDA(cudaGetLastError());
   return 0;
 }

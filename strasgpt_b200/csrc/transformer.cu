@@ -122,7 +122,7 @@ struct transformer_state {
   // maps per layer (qkv, o, gate/up, down), then the LM head.
   bool use_tc = false;
   uint16_t *a_hi = nullptr, *a_lo = nullptr;
-  sg::TcMap in_hi[3], in_lo[3];
+  sg::TcAct in[3];
   std::vector<sg::TcMap> tc_w;
   int* tc_err = nullptr;
   size_t launches = 0;        // kernels enqueued (graph nodes at capture)
@@ -591,10 +591,7 @@ void alloc_state(const W_t* w, const transformer_configuration_t* c, S_t* s) {
     const size_t kmax = (size_t)std::max(ks[0], std::max(ks[1], ks[2]));
     s->a_hi = (uint16_t*)dalloc(s->allocs, T * kmax * 2, nullptr);
     s->a_lo = (uint16_t*)dalloc(s->allocs, T * kmax * 2, nullptr);
-    for (int i = 0; i < 3; i++) {
-      sg::tc_make_map(&s->in_hi[i], s->a_hi, (int)T, ks[i]);
-      sg::tc_make_map(&s->in_lo[i], s->a_lo, (int)T, ks[i]);
-    }
+    for (int i = 0; i < 3; i++) sg::tc_make_act(&s->in[i], s->a_hi, s->a_lo, (int)T, ks[i]);
     s->tc_w.resize((size_t)4 * w->L + 1);
     for (int l = 0; l < w->L; l++) {
       const Layer& y = w->layer[l];
@@ -766,7 +763,7 @@ struct Runner {
     if (s->use_tc) {
       launch(FAM_OTHER, 0, [&] { sg::tc_split(a, K, T, K, s->a_hi, s->a_lo, st); });
       launch(FAM_OTHER, 0, [&] {
-        sg::tc_gemm(s->tc_w[wmap], s->in_hi[ki], s->in_lo[ki], T, C, ldc, epi, s->tc_err, st);
+        sg::tc_gemm(s->tc_w[wmap], s->in[ki], T, C, ldc, epi, s->tc_err, st);
       });
     } else {
       launch(FAM_OTHER, 0, [&] { sg::gemm_simt(a, K, wraw, K, T, N, C, ldc, epi, st); });
