@@ -43,6 +43,15 @@ int strasgpt_k_gemm_tc(const float* a, int lda, uint16_t* a_hi,
                        uint16_t* a_lo, const uint16_t* w, int k, int m, int n,
                        float* c, int ldc, int epi, int* err, void* stream);
 
+// Causal GQA attention of a chunk (source/transformer.c:1375-1422): q
+// [t][kv_heads*group][head_dim] at positions pos0.., caches
+// [kv_heads][ctx][head_dim] holding keys/values 0..pos0+t-1; att gets
+// [t][kv_heads*group][head_dim]. head_dim 32, 64 or 128; group divides 64.
+int strasgpt_k_attn_prefill(const float* q, const float* k_cache,
+                            const float* v_cache, int t, int kv_heads,
+                            int group, int head_dim, int ctx, int pos0,
+                            float* att, void* stream);
+
 // y[t] = rmsnorm(x[t]) * w for t < T, rows of D floats.
 int strasgpt_k_rmsnorm_rows(const float* x, int t, int d, const uint16_t* w,
                             float eps, float* y, void* stream);

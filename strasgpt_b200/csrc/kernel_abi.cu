@@ -69,6 +69,23 @@ int strasgpt_k_gemm_tc(const float* a, int lda, uint16_t* a_hi,
   return 0;
 }
 
+int strasgpt_k_attn_prefill(const float* q, const float* k_cache,
+                            const float* v_cache, int t, int kv_heads,
+                            int group, int head_dim, int ctx, int pos0,
+                            float* att, void* stream) {
+  ensure_configured();
+  if (t <= 0 || kv_heads <= 0 || group <= 0 || pos0 < 0)
+    SG_DIE("attn_prefill: empty shape");
+  if ((long)pos0 + t > ctx) SG_DIE("attn_prefill: positions beyond the cache");
+  sg::AttnPrefillArgs a;
+  a.q = q; a.k_cache = k_cache; a.v_cache = v_cache;
+  a.T = t; a.KHl = kv_heads; a.G = group; a.HD = head_dim; a.ctx = ctx;
+  a.pos0 = pos0; a.att = att;
+  sg::attn_prefill(a, (cudaStream_t)stream);
+  SG_CUDA(cudaGetLastError());
+  return 0;
+}
+
 int strasgpt_k_rmsnorm_rows(const float* x, int t, int d, const uint16_t* w,
                             float eps, float* y, void* stream) {
   ensure_configured();

@@ -687,93 +687,183 @@ void attn_decode(const AttnDecodeArgs& a, cudaStream_t s) {
 }
 
 // ---------------------------------------------------------------------------
-// Prefill attention: CTA = (q head, 32-token tile); 8 warps x 4 queries.
-// K/V tiles of 32 cache rows are staged in shared memory; lane j scores key
-// j, the warp runs an online softmax and accumulates P.V.
+// Prefill attention (causal GQA, source/transformer.c:1375-1422), fp32 on
+// the CUDA cores, register-tiled. CTA = (kv head, tile of 64/G queries): its
+// 64 rows are the G q heads of each query (row = query * G + head), which
+// share every K/V tile. Per tile of 64 keys:
+//   S = Q K^T / sqrtf(HD) as an 8 x 4 block per thread (128 threads),
+//   online softmax per row (the 16 threads of a row reduce with shuffles),
+//   P staged in shared memory, O += P V as an 8 x HD/16 block per thread.
+// The same thread owns the same 8 rows in both products, so the running
+// maximum, sum and rescale factor of each row stay in registers.
+// Shared memory (fp32): Q^T [HD][64], K^T [HD][64], V [64][HD], P [64][64].
 // ---------------------------------------------------------------------------
+constexpr int kPfRows = 64, kPfKeys = 64;
+
 template <int HD>
-__global__ void __launch_bounds__(256) k_attn_prefill(AttnPrefillArgs a) {
-  constexpr int V = HD / 32, QT = 32, KT = 32, QW = 4;
-  extern __shared__ float sm[];
-  float* qs = sm;                  // [QT][HD]
-  float* ks = qs + QT * HD;        // [KT][HD+1]
-  float* vs = ks + KT * (HD + 1);  // [KT][HD]
+constexpr size_t attn_prefill_smem() {
+  return (size_t)(HD * kPfRows + HD * kPfKeys + kPfKeys * HD + kPfRows * kPfKeys) * 4;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(128) k_attn_prefill(AttnPrefillArgs a) {
+  constexpr int R = kPfRows, KT = kPfKeys;
+  constexpr int VW = HD >= 64 ? 4 : 2;  // O columns per vector
+  constexpr int NC = HD / (16 * VW);    // O vectors per row and thread
+  constexpr int OD = NC * VW;           // O columns per thread
+  extern __shared__ float4 sm4[];
+  float* qs = reinterpret_cast<float*>(sm4);  // [HD][R]
+  float* ks = qs + HD * R;                    // [HD][KT]
+  float* vs = ks + HD * KT;                   // [KT][HD]
+  float* ps = vs + KT * HD;                   // [R][KT]
   pdl_trigger();
   pdl_wait();
-  const int qh = blockIdx.x, kh = qh / a.G, QHl = a.KHl * a.G;
-  const int tq0 = blockIdx.y * QT;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int tq1 = min(tq0 + QT, a.T);
-  for (int e = tid; e < QT * HD; e += blockDim.x) {
-    const int r = e / HD, d = e % HD, t = tq0 + r;
-    qs[e] = (t < a.T) ? a.q[((size_t)t * QHl + qh) * HD + d] : 0.f;
+  const int G = a.G, QT = R / G, QHl = a.KHl * G;
+  const int kh = blockIdx.x;
+  const int ntile = (a.T + QT - 1) / QT;
+  const int t0 = (ntile - 1 - (int)blockIdx.y) * QT;  // latest (heaviest) tiles first
+  const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+  for (int e = tid; e < R * (HD / 4); e += blockDim.x) {
+    const int r = e % R, d4 = (e / R) * 4;
+    const int t = t0 + r / G, g = r % G;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (t < a.T)
+      v = *reinterpret_cast<const float4*>(a.q + ((size_t)t * QHl + kh * G + g) * HD + d4);
+    qs[(d4 + 0) * R + r] = v.x;
+    qs[(d4 + 1) * R + r] = v.y;
+    qs[(d4 + 2) * R + r] = v.z;
+    qs[(d4 + 3) * R + r] = v.w;
   }
-  float m[QW], l[QW], acc[QW][V];
+  float m[8], lsum[8], o[8][OD];
 #pragma unroll
-  for (int j = 0; j < QW; j++) {
-    m[j] = -INFINITY;
-    l[j] = 0.f;
+  for (int i = 0; i < 8; i++) {
+    m[i] = -INFINITY;
+    lsum[i] = 0.f;
 #pragma unroll
-    for (int i = 0; i < V; i++) acc[j][i] = 0.f;
+    for (int c = 0; c < OD; c++) o[i][c] = 0.f;
   }
   const float div = sqrtf((float)HD);
-  const int kmax = a.pos0 + tq1 - 1;
+  const int kmax = a.pos0 + min(t0 + QT, a.T) - 1;
+  const int pq0 = a.pos0 + t0;  // position of the tile's first query
   const float* kb = a.k_cache + (size_t)kh * a.ctx * HD;
   const float* vb = a.v_cache + (size_t)kh * a.ctx * HD;
-  for (int kt0 = 0; kt0 <= kmax; kt0 += KT) {
-    __syncthreads();
-    for (int e = tid; e < KT * HD; e += blockDim.x) {
-      const int r = e / HD, d = e % HD, sidx = kt0 + r;
-      const bool ok = sidx <= kmax;
-      ks[r * (HD + 1) + d] = ok ? kb[(size_t)sidx * HD + d] : 0.f;
-      vs[r * HD + d] = ok ? vb[(size_t)sidx * HD + d] : 0.f;
+  for (int k0 = 0; k0 <= kmax; k0 += KT) {
+    __syncthreads();  // the previous tile's K, V and P are consumed
+    for (int e = tid; e < KT * (HD / 4); e += blockDim.x) {
+      const int key = e % KT, d4 = (e / KT) * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (k0 + key <= kmax) v = *reinterpret_cast<const float4*>(kb + (size_t)(k0 + key) * HD + d4);
+      ks[(d4 + 0) * KT + key] = v.x;
+      ks[(d4 + 1) * KT + key] = v.y;
+      ks[(d4 + 2) * KT + key] = v.z;
+      ks[(d4 + 3) * KT + key] = v.w;
+    }
+    for (int e = tid; e < KT * (HD / 4); e += blockDim.x) {
+      const int key = e / (HD / 4), d4 = (e % (HD / 4)) * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (k0 + key <= kmax) v = *reinterpret_cast<const float4*>(vb + (size_t)(k0 + key) * HD + d4);
+      *reinterpret_cast<float4*>(vs + key * HD + d4) = v;
     }
     __syncthreads();
+    float s[8][4];
 #pragma unroll
-    for (int j = 0; j < QW; j++) {
-      const int r = warp * QW + j, t = tq0 + r;
-      if (t >= a.T) continue;
-      const int pt = a.pos0 + t;
-      if (kt0 > pt) continue;
-      const int sidx = kt0 + lane;
-      const bool valid = sidx <= pt;
-      float sc = -INFINITY;
-      if (valid) {
-        float d = 0.f;
-#pragma unroll 16
-        for (int i = 0; i < HD; i++) d = fmaf(qs[r * HD + i], ks[lane * (HD + 1) + i], d);
-        sc = d / div;
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+      for (int j = 0; j < 4; j++) s[i][j] = 0.f;
+#pragma unroll 4
+    for (int d = 0; d < HD; d++) {
+      const float4 qa = *reinterpret_cast<const float4*>(qs + d * R + ty * 8);
+      const float4 qb = *reinterpret_cast<const float4*>(qs + d * R + ty * 8 + 4);
+      const float4 kv = *reinterpret_cast<const float4*>(ks + d * KT + tx * 4);
+      const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+      const float kk[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+      for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) s[i][j] = fmaf(qv[i], kk[j], s[i][j]);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const int r = ty * 8 + i;
+      const int pq = pq0 + r / G;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int key = k0 + tx * 4 + j;
+        s[i][j] = key <= pq ? s[i][j] / div : -INFINITY;
+        mx = fmaxf(mx, s[i][j]);
       }
-      const float mn = fmaxf(m[j], warp_max(sc));
-      const float corr = expf(m[j] - mn);
-      const float p = valid ? expf(sc - mn) : 0.f;
-      l[j] = l[j] * corr + warp_sum(p);
 #pragma unroll
-      for (int i = 0; i < V; i++) acc[j][i] *= corr;
-      for (int jj = 0; jj < 32; jj++) {
-        const float pj = __shfl_sync(0xFFFFFFFFu, p, jj);
+      for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, off));
+      const float mn = fmaxf(m[i], mx);  // finite: key 0 is visible to every row
+      const float corr = expf(m[i] - mn);
+      m[i] = mn;
+      lsum[i] *= corr;
 #pragma unroll
-        for (int i = 0; i < V; i++)
-          acc[j][i] = fmaf(pj, vs[jj * HD + lane + 32 * i], acc[j][i]);
+      for (int c = 0; c < OD; c++) o[i][c] *= corr;
+      float4 p;
+      p.x = expf(s[i][0] - mn);
+      p.y = expf(s[i][1] - mn);
+      p.z = expf(s[i][2] - mn);
+      p.w = expf(s[i][3] - mn);
+      lsum[i] += (p.x + p.y) + (p.z + p.w);
+      *reinterpret_cast<float4*>(ps + r * KT + tx * 4) = p;
+    }
+    __syncthreads();
+#pragma unroll 1
+    for (int k4 = 0; k4 < KT; k4 += 4) {
+      float4 p4[8];
+#pragma unroll
+      for (int i = 0; i < 8; i++) p4[i] = *reinterpret_cast<const float4*>(ps + (ty * 8 + i) * KT + k4);
+#pragma unroll
+      for (int jj = 0; jj < 4; jj++) {
+        float vv[OD];
+#pragma unroll
+        for (int c = 0; c < NC; c++) {
+          const float* src = vs + (k4 + jj) * HD + c * 16 * VW + tx * VW;
+          if (VW == 4) {
+            const float4 t4 = *reinterpret_cast<const float4*>(src);
+            vv[c * VW + 0] = t4.x;
+            vv[c * VW + 1] = t4.y;
+            vv[c * VW + 2] = t4.z;
+            vv[c * VW + 3] = t4.w;
+          } else {
+            const float2 t2 = *reinterpret_cast<const float2*>(src);
+            vv[c * VW + 0] = t2.x;
+            vv[c * VW + 1] = t2.y;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          const float pj = jj == 0 ? p4[i].x : jj == 1 ? p4[i].y : jj == 2 ? p4[i].z : p4[i].w;
+#pragma unroll
+          for (int c = 0; c < OD; c++) o[i][c] = fmaf(pj, vv[c], o[i][c]);
+        }
       }
-      m[j] = mn;
     }
   }
 #pragma unroll
-  for (int j = 0; j < QW; j++) {
-    const int t = tq0 + warp * QW + j;
-    if (t >= a.T) continue;
+  for (int i = 0; i < 8; i++) {
+    float l = lsum[i];
 #pragma unroll
-    for (int i = 0; i < V; i++)
-      a.att[((size_t)t * QHl + qh) * HD + lane + 32 * i] = acc[j][i] / l[j];
+    for (int off = 8; off > 0; off >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, off);
+    const int r = ty * 8 + i, t = t0 + r / G, g = r % G;
+    if (t >= a.T) continue;
+    float* dst = a.att + ((size_t)t * QHl + kh * G + g) * HD;
+#pragma unroll
+    for (int c = 0; c < NC; c++)
+#pragma unroll
+      for (int e = 0; e < VW; e++) dst[c * 16 * VW + tx * VW + e] = o[i][c * VW + e] / l;
   }
 }
 
 template <int HD>
 static void attn_prefill_hd(const AttnPrefillArgs& a, cudaStream_t s) {
-  const size_t smem = (size_t)(32 * HD + 32 * (HD + 1) + 32 * HD) * 4;
-  dim3 grid(a.KHl * a.G, (a.T + 31) / 32);
-  launch(k_attn_prefill<HD>, grid, dim3(256), smem, s, a);
+  if (a.G < 1 || a.G > kPfRows || kPfRows % a.G)
+    SG_DIE("attn_prefill: the q heads per kv head must divide 64");
+  const int qt = kPfRows / a.G;
+  dim3 grid(a.KHl, (a.T + qt - 1) / qt);
+  launch(k_attn_prefill<HD>, grid, dim3(128), attn_prefill_smem<HD>(), s, a);
 }
 
 void attn_prefill(const AttnPrefillArgs& a, cudaStream_t s) {

@@ -100,6 +100,8 @@ def lib() -> ctypes.CDLL:
         f.argtypes = [vp, vp, ctypes.c_float, vp, i32, i32, vp, i32, vp]
     L.strasgpt_k_gemm_simt.restype = i32
     L.strasgpt_k_gemm_simt.argtypes = [vp, i32, vp, i32, i32, i32, vp, i32, i32, vp]
+    L.strasgpt_k_attn_prefill.restype = i32
+    L.strasgpt_k_attn_prefill.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, vp]
     L.strasgpt_k_gemm_tc.restype = i32
     L.strasgpt_k_gemm_tc.argtypes = [vp, i32, vp, vp, vp, i32, i32, i32, vp, i32, i32,
                                      vp, vp]

@@ -163,6 +163,34 @@ def test_gemm_tc(cuda, m, n, k, epi):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("t,kh,g,hd,ctx,pos0", [
+    (24, 2, 2, 64, 64, 0), (77, 2, 8, 32, 128, 10), (512, 8, 2, 128, 640, 0),
+    (100, 1, 4, 128, 800, 600), (40, 2, 16, 64, 64, 3), (2, 1, 1, 128, 16, 5),
+    (130, 2, 64, 64, 192, 0)])
+def test_attn_prefill(cuda, t, kh, g, hd, ctx, pos0):
+    """Causal GQA attention of a chunk against a float64 softmax
+    (source/transformer.c:1375-1422)."""
+    torch = cuda
+    gen = torch.Generator(device="cuda").manual_seed(t * 7 + g + hd + pos0)
+    q = torch.randn(t, kh * g, hd, device="cuda", generator=gen)
+    kc = torch.randn(kh, ctx, hd, device="cuda", generator=gen)
+    vc = torch.randn(kh, ctx, hd, device="cuda", generator=gen)
+    att = torch.full((t, kh * g, hd), float("nan"), device="cuda")
+    runtime.lib().strasgpt_k_attn_prefill(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), t, kh,
+                                          g, hd, ctx, pos0, att.data_ptr(), None)
+    torch.cuda.synchronize()
+    n = pos0 + t
+    qd = q.double().view(t, kh, g, hd)
+    k = kc[:, :n].double()
+    v = vc[:, :n].double()
+    s = torch.einsum("tkgd,knd->tkgn", qd, k) / hd ** 0.5
+    pos = pos0 + torch.arange(t, device="cuda").view(t, 1, 1, 1)
+    s = s.masked_fill(torch.arange(n, device="cuda").view(1, 1, 1, n) > pos, float("-inf"))
+    want = torch.einsum("tkgn,knd->tkgd", torch.softmax(s, dim=-1), v).reshape(t, kh * g, hd)
+    close(att, want, f"attn_prefill t={t} kh={kh} g={g} hd={hd} pos0={pos0}")
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("t,d", [(1, 256), (3, 2048), (17, 5120)])
 def test_rmsnorm_rows(cuda, t, d):
     torch = cuda
