@@ -21,6 +21,8 @@ typedef struct strasgpt_timing {
   size_t prefill_tokens;
   size_t decode_steps;
   size_t kernel_launches; // kernels this call launched (graph nodes counted)
+  size_t decode_launches; // of which in the decode steps (1: the persistent
+                          // decode kernel ran all of them)
 } strasgpt_timing_t;
 
 // Greedy generation with the token loop kept on the GPU: process the
@@ -50,6 +52,21 @@ size_t transformer_cached_count(const transformer_t* transformer);
 // STRASGPT_TP_RANK / STRASGPT_TP_SIZE / STRASGPT_DEVICE are read (default:
 // rank 0 of 1 on device 0). Returns 0, or -1 on an invalid placement.
 int strasgpt_set_placement(int rank, int world, int device);
+
+// Tensor parallelism, one process per GPU of one node. Each rank's
+// transformer owns an exchange buffer in its GPU's memory; the ranks map
+// each other's buffers (CUDA IPC over NVLink) and run one all-reduce after
+// o_proj and one after the FFN of every layer, plus a gather of the
+// vocabulary slices of the logits. The library does no host networking:
+// the caller moves the handles. Every rank: build the transformer, write
+// its STRASGPT_TP_HANDLE_BYTES handle with strasgpt_tp_handle(), exchange
+// the handles (e.g. an all-gather), then call strasgpt_tp_connect() with
+// all of them in rank order. All ranks must then make the same calls with
+// the same tokens; each returns the full logits. Both return 0, or -1 when
+// world is 1 or an argument is NULL.
+#define STRASGPT_TP_HANDLE_BYTES 64
+int strasgpt_tp_handle(transformer_t* transformer, void* handle);
+int strasgpt_tp_connect(transformer_t* transformer, const void* handles);
 
 // Per-kernel-family device time of the last profiled decode steps (see
 // strasgpt_profile_decode). Families: 0 matvec, 1 attention, 2 qkv_post,

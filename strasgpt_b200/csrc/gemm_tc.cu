@@ -5,16 +5,18 @@
 // take bf16 operands, so the activations are split on the way in:
 // A = A_hi + A_lo with A_hi = bf16(A), A_lo = bf16(A - A_hi), which keeps
 // about 16 bits of A (relative error <= 2^-17) while every product stays
-// exact in fp32. Each 16-wide K step is two MMAs into the same accumulator,
-// W x A_hi and W x A_lo, with the weight tile loaded once.
+// exact in fp32. Each 16-wide K step is one MMA of N = 2*BN: the A_hi and
+// A_lo tiles are adjacent in shared memory and form a single operand, so
+// the weight tile is read once; the epilogue adds the two accumulator
+// halves.
 //
-// Tile: 128 weight rows (MMA M) x BN tokens (MMA N, BN = 32, 64 or 128), K
-// in steps of 64 (one 128-byte swizzle row). A ring of stages of
+// Tile: 128 weight rows (MMA M) x BN tokens (BN = 32, 64 or 128), K in
+// steps of 64 (one 128-byte swizzle row). A ring of stages of
 // {W, A_hi, A_lo} tiles filled by TMA with 128-byte swizzling; the fp32
-// accumulator lives in tensor memory (BN columns). The kernel streams its
-// operands at about 64 B/clk per SM, so the host picks BN to minimise
-// waves x bytes per stage (few weight-row tiles: narrow token tiles and
-// more CTAs; many: wide tiles and fewer bytes per MMA).
+// accumulators live in tensor memory (2*BN columns). The stage ring is
+// bound by TMA latency, so the host picks BN to minimise waves x bytes per
+// stage (few weight-row tiles: narrow token tiles and more CTAs; many: wide
+// tiles and fewer bytes per MMA).
 // Warp roles (6 warps): 0 TMA producer, 1 MMA issuer (one elected thread
 // each), 2..5 epilogue (each reads the 32 TMEM lanes of its quarter with
 // tcgen05.ld, applies STORE / ADD / SwiGLU and writes C coalesced along r).
@@ -46,11 +48,16 @@ struct Cfg {
   static constexpr int kStagesFit = (kSmemBudget - 1024) / kStageBytes;
   static constexpr int STAGES = kStagesFit > 8 ? 8 : kStagesFit;
   static constexpr int kSmemBytes = STAGES * kStageBytes + 1024;  // + alignment slack
+  // One MMA per 16-wide K step covers both activation halves: the A_hi and
+  // A_lo tiles sit back to back in shared memory and form one operand of
+  // 2*BN rows, so the weight tile is read once per step. Accumulator
+  // columns [0, BN) hold W x A_hi, [BN, 2*BN) W x A_lo.
+  static constexpr int kN = 2 * BN;
   // Instruction descriptor: bf16 x bf16 -> f32, both operands K-major,
-  // N = BN, M = 128.
+  // N = 2*BN, M = 128.
   static constexpr uint32_t kIdesc = (1u << 4)                        // D: f32
                                      | (1u << 7) | (1u << 10)         // A, B: bf16
-                                     | ((uint32_t)(BN >> 3) << 17)    // N
+                                     | ((uint32_t)(kN >> 3) << 17)    // N
                                      | ((uint32_t)(BM >> 4) << 24);   // M
 };
 
@@ -195,7 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      saddr(&tmem_slot)),
-                 "r"(BN)
+                 "r"(C::kN)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -241,10 +248,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int k = 0; k < BK / 16; k++) {
           const uint64_t aw = sw128_desc(st + k * 32);
-          const uint64_t bh = sw128_desc(st + kWTileBytes + k * 32);
-          const uint64_t bl = sw128_desc(st + kWTileBytes + C::kATileBytes + k * 32);
-          mma_bf16<BN>(tmem, aw, bh, (kb | k) != 0);
-          mma_bf16<BN>(tmem, aw, bl, 1);
+          const uint64_t bhl = sw128_desc(st + kWTileBytes + k * 32);  // A_hi rows, then A_lo
+          mma_bf16<BN>(tmem, aw, bhl, (kb | k) != 0);
         }
         mma_commit(saddr(&empty_bar[s]));
       }
@@ -262,8 +267,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         if (t0 + c0 >= p.T) break;  // warp-uniform
-        float v[32];
+        float v[32], vl[32];
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(BN + c0), vl);
+#pragma unroll
+        for (int j = 0; j < 32; j++) v[j] += vl[j];
 #pragma unroll
         for (int j = 0; j < 32; j++) {
           const int t = t0 + c0 + j;
@@ -286,7 +294,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(C::kN)
                  : "memory");
   }
 }

@@ -1,0 +1,56 @@
+// Tensor-parallel exchanges between the GPUs of one node over NVLink peer
+// memory (CUDA IPC), one process per GPU.
+//
+// Every rank owns one exchange buffer (a single cudaMalloc, shared with the
+// other ranks through cudaIpcGetMemHandle / cudaIpcOpenMemHandle):
+//   flags  u32 [kTpMaxRanks]   latest exchange epoch posted by each rank
+//   epoch  u32                 this rank's last completed epoch (local)
+//   ticket u32                 last-CTA detection of multi-CTA exchanges
+//   data   f32 [2][cap]        staged operands, two halves by epoch parity
+// An exchange with epoch e: the rank stages its operand into data[e & 1],
+// posts e into every peer's flags[rank] (release, system scope), waits until
+// its own flags[p] >= e for every peer p (acquire, bounded), then reads the
+// peers' data[e & 1] over NVLink. A half is rewritten two exchanges later,
+// after every peer has posted the epoch in between, i.e. has finished
+// reading it. All ranks run the same exchanges in the same order; sums run
+// in rank order, so every rank gets bit-identical results.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace sg {
+
+constexpr int kTpMaxRanks = 8;
+
+struct TpComm {
+  int rank = 0, world = 1;
+  size_t cap = 0;                       // floats per data half
+  unsigned char* local = nullptr;       // this rank's exchange buffer
+  unsigned char* peer[kTpMaxRanks] = {};  // every rank's buffer (own included)
+  int* err = nullptr;                   // device int: non-zero after a timeout
+  bool connected = false;
+};
+
+// Bytes of the exchange buffer for `cap` floats per half.
+size_t tp_buffer_bytes(size_t cap);
+// Allocates and zeroes this rank's buffer (and the error flag).
+void tp_alloc(TpComm* c, int rank, int world, size_t cap);
+// 64-byte IPC handle of this rank's buffer.
+void tp_handle(const TpComm& c, void* out64);
+// Maps the peers' buffers from world x 64-byte handles (rank order).
+void tp_connect(TpComm* c, const void* handles);
+// Unmaps the peers (after a final barrier exchange) and frees the buffer.
+void tp_free(TpComm* c, cudaStream_t s);
+
+// x[i] += sum over ranks (in rank order) of part_r[i], i < n.
+void tp_allreduce_add(TpComm& c, const float* part, float* x, size_t n, cudaStream_t s);
+// dst[row][r * cols + j] = src_r[row][j] for every rank r (src rows `cols`
+// floats apart, dst rows world * cols).
+void tp_gather_rows(TpComm& c, const float* src, int rows, int cols, float* dst,
+                    cudaStream_t s);
+// Exchange without data: returns once every rank has reached it.
+void tp_barrier(TpComm& c, cudaStream_t s);
+
+}  // namespace sg

@@ -24,6 +24,7 @@
 #include "gemm_tc.h"
 #include "kernels.h"
 #include "mega.h"
+#include "tp.h"
 
 #include <fcntl.h>
 #include <omp.h>
@@ -102,7 +103,13 @@ struct transformer_state {
   float *rl = nullptr, *ew = nullptr;
   int* eidx = nullptr;
   size_t cached_count = 0;
-  float* h_logits = nullptr;  // pinned bounce buffer [logit_rows_max][Vl]
+  float* h_logits = nullptr;  // pinned bounce buffer [logit_rows_max][V]
+  // Tensor parallelism (world > 1): this rank's partial sums of o_proj and
+  // the FFN ([chunk][D]) before the all-reduce, its vocabulary slice of the
+  // logits before the gather, and the peer exchange buffers.
+  float* part = nullptr;
+  float* logits_local = nullptr;
+  sg::TpComm tp;
   cudaGraphExec_t graph_logits = nullptr;
   cudaGraphExec_t graph_greedy = nullptr;
   cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
@@ -515,7 +522,13 @@ void alloc_state(const W_t* w, const transformer_configuration_t* c, S_t* s) {
   s->q = F32(T * w->QHl * HD);
   s->att = F32(T * w->QHl * HD);
   s->h = F32(T * hid);
-  s->logits = F32((size_t)s->logit_rows_max * w->Vl);
+  s->logits = F32((size_t)s->logit_rows_max * w->V);
+  if (w->world > 1) {
+    s->part = F32(T * D);
+    s->logits_local = F32((size_t)s->logit_rows_max * w->Vl);
+    sg::tp_alloc(&s->tp, w->rank, w->world,
+                 std::max(T * D, (size_t)s->logit_rows_max * w->Vl));
+  }
   const size_t kv = (size_t)w->L * w->KHl * s->ctx * HD;
   s->kc = F32(kv);
   s->vc = F32(kv);
@@ -606,7 +619,7 @@ void alloc_state(const W_t* w, const transformer_configuration_t* c, S_t* s) {
     s->tc_err = I32(1);
     SG_CUDA(cudaMemset(s->tc_err, 0, 4));
   }
-  SG_CUDA(cudaMallocHost(&s->h_logits, (size_t)s->logit_rows_max * w->Vl * 4));
+  SG_CUDA(cudaMallocHost(&s->h_logits, (size_t)s->logit_rows_max * w->V * 4));
   SG_CUDA(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
   for (auto& e : s->ev) SG_CUDA(cudaEventCreate(&e));
 }
@@ -666,8 +679,35 @@ struct Runner {
     a.up_codes = ly.up_c; a.up_scales = ly.up_s;
     a.down_codes = ly.down_c; a.down_scales = ly.down_s;
     a.e_begin = w->e_begin; a.e_end = w->e_end;
-    a.h = s->h; a.out = s->x;
+    a.h = s->h; a.out = rp_out();
     return a;
+  }
+
+  bool tp() const { return w->world > 1; }
+  // Target and epilogue of a row-parallel projection (o_proj, down): the
+  // residual directly on one GPU, this rank's partial sum under TP.
+  float* rp_out() const { return tp() ? s->part : s->x; }
+  sg::Epilogue rp_epi() const { return tp() ? sg::EPI_STORE : sg::EPI_ADD; }
+  // Under TP: x += sum over ranks of `part` ([T][D]).
+  void rp_reduce(int T) {
+    if (!tp()) return;
+    s->launches++;  // stage + reduce
+    launch(FAM_OTHER, 0, [&] {
+      sg::tp_allreduce_add(s->tp, s->part, s->x, (size_t)T * w->D, st);
+    });
+  }
+  // LM head target ([rows][Vl] of this rank) and, under TP, the gather of the
+  // vocabulary slices into s->logits ([rows][V]).
+  float* lm_out() const { return tp() ? s->logits_local : s->logits; }
+  void lm_gather(int rows) {
+    if (!tp()) return;
+    s->launches++;
+    launch(FAM_OTHER, 0, [&] {
+      sg::tp_gather_rows(s->tp, s->logits_local, rows, w->Vl, s->logits, st);
+    });
+  }
+  void moe_zero_part(int T) {
+    if (tp()) SG_CUDA(cudaMemsetAsync(s->part, 0, (size_t)T * w->D * 4, st));
   }
 
   double moe_bytes_per_token() const {
@@ -693,9 +733,9 @@ struct Runner {
       a.partial = s->attn_partial; a.ticket = s->attn_ticket; a.att = s->att;
       launch(FAM_ATTN, 0, [&] { sg::attn_decode(a, st); });
       launch(FAM_MATVEC, (double)D * w->QHl * HD * 2, [&] {
-        sg::matvec(s->att, nullptr, 0.f, ly.wo, w->QHl * HD, D, s->x,
-                   sg::EPI_ADD, st);
+        sg::matvec(s->att, nullptr, 0.f, ly.wo, w->QHl * HD, D, rp_out(), rp_epi(), st);
       });
+      rp_reduce(1);
       if (w->moe) {
         launch(FAM_OTHER, 0, [&] { sg::rmsnorm_rows(s->x, 1, D, ly.ffn_norm, w->eps, s->xn, st); });
         launch(FAM_MATVEC, (double)w->E * D * 2, [&] {
@@ -703,6 +743,7 @@ struct Runner {
         });
         launch(FAM_OTHER, 0, [&] { sg::moe_topk(s->rl, 1, w->E, w->topk, s->eidx, s->ew, st); });
         sg::MoeArgs m = moe_args(l, 1);
+        moe_zero_part(1);
         launch(FAM_MATVEC, moe_bytes_per_token() * 2 / 3, [&] { sg::moe_gate_up(m, st); });
         launch(FAM_MATVEC, moe_bytes_per_token() / 3, [&] { sg::moe_down(m, st); });
       } else {
@@ -711,19 +752,21 @@ struct Runner {
                      sg::EPI_SWIGLU, st);
         });
         launch(FAM_MATVEC, (double)D * w->Fl * 2, [&] {
-          sg::matvec(s->h, nullptr, 0.f, ly.wd, w->Fl, D, s->x, sg::EPI_ADD, st);
+          sg::matvec(s->h, nullptr, 0.f, ly.wd, w->Fl, D, rp_out(), rp_epi(), st);
         });
       }
+      rp_reduce(1);
     }
     launch(FAM_LMHEAD, (double)w->Vl * D * 2, [&] {
-      sg::matvec(s->x, w->out_norm, w->eps, w->out_w, D, w->Vl, s->logits,
+      sg::matvec(s->x, w->out_norm, w->eps, w->out_w, D, w->Vl, lm_out(),
                  sg::EPI_STORE, st);
     });
+    lm_gather(1);
   }
 
   void argmax(int advance_pos) {
-    launch(FAM_ARGMAX, (double)w->Vl * 4, [&] {
-      sg::argmax_advance(s->logits, w->Vl, s->tok, advance_pos ? s->pos : nullptr,
+    launch(FAM_ARGMAX, (double)w->V * 4, [&] {
+      sg::argmax_advance(s->logits, w->V, s->tok, advance_pos ? s->pos : nullptr,
                          s->step, s->gen, s->ctx + 1, s->am_val, s->am_idx,
                          s->am_ticket, st);
     });
@@ -784,33 +827,38 @@ struct Runner {
       a.T = T; a.KHl = w->KHl; a.G = w->G; a.HD = HD; a.ctx = s->ctx;
       a.pos0 = pos0; a.att = s->att;
       launch(FAM_ATTN, 0, [&] { sg::attn_prefill(a, st); });
-      proj(s->att, QD, 1, ly.wo, 4 * l + 1, D, s->x, D, sg::EPI_ADD, T);
+      proj(s->att, QD, 1, ly.wo, 4 * l + 1, D, rp_out(), D, rp_epi(), T);
+      rp_reduce(T);
       launch(FAM_OTHER, 0, [&] { sg::rmsnorm_rows(s->x, T, D, ly.ffn_norm, w->eps, s->xn, st); });
       if (w->moe) {
         launch(FAM_OTHER, 0, [&] { sg::gemm_simt(s->xn, D, ly.router, D, T, w->E, s->rl, w->E, sg::EPI_STORE, st); });
         launch(FAM_OTHER, 0, [&] { sg::moe_topk(s->rl, T, w->E, w->topk, s->eidx, s->ew, st); });
         sg::MoeArgs m = moe_args(l, T);
+        moe_zero_part(T);
         launch(FAM_OTHER, 0, [&] { sg::moe_gate_up(m, st); });
         launch(FAM_OTHER, 0, [&] { sg::moe_down(m, st); });
       } else {
         proj(s->xn, D, 0, ly.wgu, 4 * l + 2, 2 * w->Fl, s->h, w->Fl, sg::EPI_SWIGLU, T);
-        proj(s->h, w->Fl, 2, ly.wd, 4 * l + 3, D, s->x, D, sg::EPI_ADD, T);
+        proj(s->h, w->Fl, 2, ly.wd, 4 * l + 3, D, rp_out(), D, rp_epi(), T);
       }
+      rp_reduce(T);
     }
   }
 
-  // LM head for rows [r0, r0+n) of the chunk (n <= logit_rows_max).
+  // LM head for rows [r0, r0+n) of the chunk (n <= logit_rows_max); the
+  // logits land in s->logits ([n][V]).
   void lm_head_rows(int r0, int n) {
     const int D = w->D;
     if (n == 1) {
       launch(FAM_LMHEAD, 0, [&] {
         sg::matvec(s->x + (size_t)r0 * D, w->out_norm, w->eps, w->out_w, D,
-                   w->Vl, s->logits, sg::EPI_STORE, st);
+                   w->Vl, lm_out(), sg::EPI_STORE, st);
       });
     } else {
       launch(FAM_OTHER, 0, [&] { sg::rmsnorm_rows(s->x + (size_t)r0 * D, n, D, w->out_norm, w->eps, s->xn, st); });
-      proj(s->xn, D, 0, w->out_w, 4 * w->L, w->Vl, s->logits, w->Vl, sg::EPI_STORE, n);
+      proj(s->xn, D, 0, w->out_w, 4 * w->L, w->Vl, lm_out(), w->Vl, sg::EPI_STORE, n);
     }
+    lm_gather(n);
   }
 };
 
@@ -848,9 +896,9 @@ cudaGraphExec_t capture(Runner& r, bool greedy) {
 W_t* weights_of(transformer_t* t) { return (W_t*)t->weights; }
 S_t* state_of(transformer_t* t) { return (S_t*)t->state; }
 
-void require_single_rank(const W_t* w) {
-  if (w->world != 1)
-    SG_DIE("tensor-parallel forward needs the communicator (world > 1)");
+void require_connected(const W_t* w, const S_t* s) {
+  if (w->world > 1 && !s->tp.connected)
+    SG_DIE("tensor-parallel forward before strasgpt_tp_connect (world > 1)");
 }
 
 // After a synchronize: a megakernel barrier that timed out is fatal. With
@@ -861,6 +909,11 @@ void check_device_errors(S_t* s) {
     int err = 0;
     SG_CUDA(cudaMemcpy(&err, s->tc_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (err) SG_DIE("tensor-core projection: a TMA or MMA pipeline wait timed out");
+  }
+  if (s->tp.world > 1) {
+    int err = 0;
+    SG_CUDA(cudaMemcpy(&err, s->tp.err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (err) SG_DIE("tensor-parallel exchange: a peer did not post within the time limit");
   }
   if (!s->use_mega) return;
   int err = 0;
@@ -887,10 +940,10 @@ void predict_impl(transformer_t* t, size_t T, const int* tok, size_t n,
   W_t* w = weights_of(t);
   S_t* s = state_of(t);
   const transformer_configuration_t* c = t->config;
-  require_single_rank(w);
+  require_connected(w, s);
   SG_CUDA(cudaSetDevice(w->device));
   Runner r{w, s, c, s->stream};
-  const size_t V = (size_t)w->Vl;
+  const size_t V = (size_t)w->V;
   const size_t lstart = T - n;
   for (size_t c0 = 0; c0 < T; c0 += (size_t)s->chunk_max) {
     const size_t Tc = std::min((size_t)s->chunk_max, T - c0);
@@ -940,6 +993,26 @@ int strasgpt_set_placement(int rank, int world, int device) {
   g_rank = rank;
   g_world = world;
   g_device = device;
+  return 0;
+}
+
+int strasgpt_tp_handle(transformer_t* t, void* handle) {
+  if (!t || !handle) return -1;
+  W_t* w = weights_of(t);
+  S_t* s = state_of(t);
+  if (w->world == 1) return -1;
+  SG_CUDA(cudaSetDevice(w->device));
+  sg::tp_handle(s->tp, handle);
+  return 0;
+}
+
+int strasgpt_tp_connect(transformer_t* t, const void* handles) {
+  if (!t || !handles) return -1;
+  W_t* w = weights_of(t);
+  S_t* s = state_of(t);
+  if (w->world == 1) return -1;
+  SG_CUDA(cudaSetDevice(w->device));
+  sg::tp_connect(&s->tp, handles);
   return 0;
 }
 
@@ -1046,6 +1119,7 @@ void transformer_free(transformer_t* t) {
       if (e) cudaEventDestroy(e);
     if (s->h_logits) cudaFreeHost(s->h_logits);
     for (auto e : s->prof_ev) cudaEventDestroy(e);
+    if (s->tp.local) sg::tp_free(&s->tp, s->stream);
     if (s->stream) cudaStreamDestroy(s->stream);
     for (void* p : s->allocs) cudaFree(p);
     delete s;
@@ -1121,7 +1195,7 @@ int transformer_generate_greedy(transformer_t* t, size_t P, const int* prompt,
   if (!t || !prompt || P == 0 || !out_tokens) SG_DIE("invalid arguments");
   W_t* w = weights_of(t);
   S_t* st = state_of(t);
-  require_single_rank(w);
+  require_connected(w, st);
   if (P + S + st->cached_count > t->config->context_len)
     SG_DIE("context length exhausted");
   SG_CUDA(cudaSetDevice(w->device));
@@ -1149,6 +1223,7 @@ int transformer_generate_greedy(transformer_t* t, size_t P, const int* prompt,
   r.argmax(0);
   SG_CUDA(cudaEventRecord(st->ev[1], st->stream));
   size_t graph_replays = 0;
+  const size_t launches_prefill = st->launches;
   if (st->use_mega) {
     if (S > 0) r.mega((int)S, false);
   } else {
@@ -1171,6 +1246,7 @@ int transformer_generate_greedy(transformer_t* t, size_t P, const int* prompt,
     timing->prefill_tokens = P;
     timing->decode_steps = S;
     timing->kernel_launches = st->launches - launches0 + graph_replays * st->graph_nodes;
+    timing->decode_launches = st->launches - launches_prefill + graph_replays * st->graph_nodes;
   }
   return 0;
 }
@@ -1188,7 +1264,7 @@ int strasgpt_profile_decode(transformer_t* t, int first_token, size_t steps,
   if (!t || !prof) SG_DIE("invalid arguments");
   W_t* w = weights_of(t);
   S_t* st = state_of(t);
-  require_single_rank(w);
+  require_connected(w, st);
   if (st->cached_count + steps > t->config->context_len)
     SG_DIE("context length exhausted");
   SG_CUDA(cudaSetDevice(w->device));

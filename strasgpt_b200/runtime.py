@@ -49,10 +49,12 @@ class Timing(ctypes.Structure):
     _fields_ = [("prefill_ms", ctypes.c_double), ("decode_ms", ctypes.c_double),
                 ("prefill_tokens", ctypes.c_size_t),
                 ("decode_steps", ctypes.c_size_t),
-                ("kernel_launches", ctypes.c_size_t)]
+                ("kernel_launches", ctypes.c_size_t),
+                ("decode_launches", ctypes.c_size_t)]
 
 
 KERNEL_FAMILIES = ("matvec", "attention", "qkv_post", "lm_head", "argmax", "other")
+TP_HANDLE_BYTES = 64  # STRASGPT_TP_HANDLE_BYTES (include/strasgpt.h)
 
 
 class KernelProfile(ctypes.Structure):
@@ -91,6 +93,10 @@ def lib() -> ctypes.CDLL:
     L.transformer_cached_count.argtypes = [ctypes.POINTER(_Transformer)]
     L.strasgpt_set_placement.restype = i32
     L.strasgpt_set_placement.argtypes = [i32, i32, i32]
+    L.strasgpt_tp_handle.restype = i32
+    L.strasgpt_tp_handle.argtypes = [ctypes.POINTER(_Transformer), ctypes.c_char_p]
+    L.strasgpt_tp_connect.restype = i32
+    L.strasgpt_tp_connect.argtypes = [ctypes.POINTER(_Transformer), ctypes.c_char_p]
     L.strasgpt_profile_decode.restype = i32
     L.strasgpt_profile_decode.argtypes = [ctypes.POINTER(_Transformer), i32, sz,
                                           ctypes.POINTER(KernelProfile)]
@@ -123,7 +129,10 @@ class Transformer:
     """A model resident on one GPU (or one tensor-parallel shard of it)."""
 
     def __init__(self, model_dir: str, rank: int = 0, world: int = 1,
-                 device: int = 0):
+                 device: int = 0, group=None):
+        """With world > 1 this is rank `rank`'s tensor-parallel shard; the
+        ranks' exchange handles are all-gathered over the torch.distributed
+        process group `group` (any backend, e.g. gloo) and connected."""
         L = lib()
         if L.strasgpt_set_placement(rank, world, device) != 0:
             raise ValueError(f"invalid placement rank={rank} world={world}")
@@ -136,6 +145,27 @@ class Transformer:
         self.vocab = int(cfg.vocabulary_len)
         self.context_len = int(cfg.context_len)
         self.dim = int(cfg.embedding_dim)
+        self.rank, self.world = rank, world
+        if world > 1:
+            import torch.distributed as dist
+            handles = [None] * world
+            dist.all_gather_object(handles, self.tp_handle(), group=group)
+            self.tp_connect(handles)
+
+    def tp_handle(self) -> bytes:
+        """strasgpt_tp_handle: this rank's exchange-buffer handle."""
+        buf = ctypes.create_string_buffer(TP_HANDLE_BYTES)
+        if lib().strasgpt_tp_handle(self._t, buf) != 0:
+            raise RuntimeError("strasgpt_tp_handle failed (world 1?)")
+        return buf.raw
+
+    def tp_connect(self, handles) -> None:
+        """strasgpt_tp_connect with every rank's handle in rank order."""
+        blob = b"".join(handles)
+        if len(blob) != TP_HANDLE_BYTES * self.world:
+            raise ValueError("one handle per rank expected")
+        if lib().strasgpt_tp_connect(self._t, blob) != 0:
+            raise RuntimeError("strasgpt_tp_connect failed")
 
     from_safetensors = classmethod(lambda cls, d, **kw: cls(d, **kw))
 

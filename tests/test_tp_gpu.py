@@ -1,0 +1,85 @@
+"""Tensor parallelism on 2 GPUs: one process per GPU, exchange handles
+all-gathered over gloo, the all-reduces and the logits gather running over
+NVLink peer memory. Every rank's logits and greedy ids must meet the same
+parity bar against the golden fixtures as the single-GPU path (greedy ids
+bit-exact, max-abs <= 1e-2, cosine >= 0.9999), and the ranks must agree
+bit for bit with each other. Skipped with fewer than 2 GPUs."""
+import json
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from conftest import model_dir
+from strasgpt_b200 import configs, synth
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+MAX_ABS = 1e-2
+MIN_COS = 0.9999
+NAMES = ["t_llama", "t_gqa8", "t_untied", "t_chunk", "t_moe"]
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _rank_main(rank, world, port, names, out_dir):
+    import datetime
+    import torch.distributed as dist
+    from strasgpt_b200 import Transformer
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=120))
+    try:
+        for name in names:
+            cfg = configs.get(name)
+            m = Transformer(model_dir(cfg), rank=rank, world=world, device=rank)
+            prompt = synth.prompt_tokens(cfg)
+            rows = [m.predict(prompt, 1)[0]]
+            for _ in range(cfg.steps):
+                rows.append(m.predict([int(np.argmax(rows[-1]))], 1)[0])
+            m.reset()
+            toks, _ = m.generate_greedy(prompt, cfg.steps)
+            m.free()
+            np.savez(os.path.join(out_dir, f"{name}_r{rank}.npz"), logits=np.stack(rows),
+                     tokens=np.asarray(toks))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_tp2_matches_golden(cuda, tmp_path):
+    torch = cuda
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import multiprocessing as mp
+    for n in NAMES:
+        model_dir(configs.get(n))  # written once, before the ranks start
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, NAMES, str(tmp_path)))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=600)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    for name in NAMES:
+        meta = json.load(open(os.path.join(GOLDEN, f"{name}.json")))
+        want = np.load(os.path.join(GOLDEN, f"{name}.npz"))["logits"].astype(np.float64)
+        r0 = np.load(os.path.join(str(tmp_path), f"{name}_r0.npz"))
+        r1 = np.load(os.path.join(str(tmp_path), f"{name}_r1.npz"))
+        assert np.array_equal(r0["logits"], r1["logits"]), f"{name}: ranks disagree"
+        got = r0["logits"].astype(np.float64)
+        err = np.abs(got - want).max()
+        cos = min(float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b))) for a, b in zip(got, want))
+        assert err <= MAX_ABS and cos >= MIN_COS, f"{name}: max-abs {err:.3e} cos {cos:.7f}"
+        assert [int(np.argmax(l)) for l in got] == meta["tokens"], name
+        assert list(r0["tokens"]) == meta["tokens"] and list(r1["tokens"]) == meta["tokens"], name
