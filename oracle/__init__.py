@@ -105,3 +105,25 @@ class Restatement(_Base):
     """This project's CPU restatement (dense + MXFP4 MoE)."""
     _prefix = "oracle_"
     _path = ORACLE_LIB
+
+    def min_router_gap(self) -> float:
+        """Smallest margin of a top-k expert choice in the last predict
+        (inf for dense models)."""
+        f = self._L.oracle_min_router_gap
+        f.restype = ctypes.c_float
+        f.argtypes = [ctypes.c_void_p]
+        return float(f(self._h))
+
+    def generate_greedy(self, prompt, steps: int, gaps=None):
+        """As _Base.generate_greedy; appends each step's min_router_gap()
+        to `gaps` when a list is given."""
+        logits = [self.predict(prompt, 1)[0]]
+        if gaps is not None:
+            gaps.append(self.min_router_gap())
+        toks = [int(np.argmax(logits[-1]))]
+        for _ in range(steps):
+            logits.append(self.predict([toks[-1]], 1)[0])
+            if gaps is not None:
+                gaps.append(self.min_router_gap())
+            toks.append(int(np.argmax(logits[-1])))
+        return np.array(toks, dtype=np.int32), np.stack(logits)

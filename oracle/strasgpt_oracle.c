@@ -52,6 +52,11 @@ typedef struct oracle {
   olayer_t* layer;
   float *kc, *vc, *rope;  // [L][KH][ctx][HD], [ctx][HD]
   size_t cached;
+  // Smallest gap, over the tokens and layers of the last oracle_predict,
+  // between the k-th selected router logit and the best unselected one
+  // (INFINITY for dense models): below ~1e-5 the expert choice depends on
+  // the fp32 summation order, so two correct implementations may differ.
+  float min_router_gap;
 } oracle_t;
 
 static void die(const char* m) {
@@ -117,6 +122,7 @@ oracle_t* oracle_load(const char* dir) {
   o->interleaved = s->rope_interleaved;
   o->E = (int)s->expert_count;
   o->topk = (int)s->expert_top_k;
+  o->min_router_gap = INFINITY;
   const size_t D = o->D, HD = o->HD, F = o->F, V = o->V;
   const size_t QD = (size_t)o->QH * HD, KD = (size_t)o->KH * HD;
   o->emb = need_tensor(s, "model.embed_tokens.weight", V * D * 2);
@@ -179,6 +185,7 @@ oracle_t* oracle_load(const char* dir) {
 }
 
 int oracle_vocab(const oracle_t* o) { return o->V; }
+float oracle_min_router_gap(const oracle_t* o) { return o->min_router_gap; }
 size_t oracle_cached(const oracle_t* o) { return o->cached; }
 void oracle_reset(oracle_t* o) { o->cached = 0; }
 
@@ -290,6 +297,12 @@ static void moe_ffn(const oracle_t* o, const olayer_t* y, size_t T,
       sel[j] = r[best];
       r[best] = -INFINITY;
     }
+    float next = -INFINITY;
+    for (size_t e = 0; e < E; e++)
+      if (r[e] > next) next = r[e];
+    const float gap = sel[K - 1] - next;
+#pragma omp critical
+    if (gap < ((oracle_t*)o)->min_router_gap) ((oracle_t*)o)->min_router_gap = gap;
     float sum = 0, ex[16];
     for (size_t j = 0; j < K; j++) {
       ex[j] = expf(sel[j] - sel[0]);
@@ -454,6 +467,7 @@ void oracle_predict(oracle_t* o, size_t T, const int* tok, size_t n,
   if (T + o->cached > (size_t)o->ctx) die("context length exhausted");
   if (n > T) n = T;
   const size_t ls = T - n;
+  o->min_router_gap = INFINITY;
   for (size_t t = 0; t < T; t += ORACLE_CHUNK) {
     size_t Tc = T - t < ORACLE_CHUNK ? T - t : ORACLE_CHUNK;
     size_t lo = t > ls ? t : ls;

@@ -2,29 +2,41 @@
 //
 // One CTA per SM (cooperative launch, so all CTAs are co-resident), 8
 // warps. A decode step is a fixed sequence of phases; each phase splits its
-// work over the CTAs and ends at a grid barrier:
-//   per layer  QKV     x -> RMSNorm -> Wqkv rows            -> qkv
+// work over the CTAs:
+//   per layer  QKV     x -> RMSNorm -> Wqkv rows                 -> qkv
 //              ATTN    per (kv head, split): q/k RMSNorm + RoPE, K/V append
-//                      at `pos`, scores / softmax / P.V      -> split partials
-//              O       merge the splits -> Wo rows, residual add -> x
+//                      at `pos`, scores / softmax / P.V -> split record;
+//                      the last split of a kv head merges       -> att
+//              O       att -> Wo rows, residual add             -> x
 //              GU      x -> RMSNorm -> gate/up row pairs, SwiGLU -> h
-//              DOWN    h -> Wd rows, residual add              -> x
-//   LM head    x -> RMSNorm -> vocab rows (+ per-CTA argmax)
-//   argmax     every CTA reduces the per-CTA partials -> next token
+//              DOWN    h -> Wd rows, residual add               -> x
+//   LM head    x -> RMSNorm -> vocab rows (+ per-CTA argmax)     -> am
+//   argmax     every CTA reduces the per-CTA partials           -> token
+//
+// Hand-off without barriers. Every phase output above is a flagged vector:
+// element i is one 64-bit word (epoch << 32 | float bits), written with a
+// single relaxed store. A consumer loads the words it needs and re-loads
+// those whose epoch is not yet the step's, so waiting and fetching the data
+// are the same L2 round trip. Each (layer, phase) has its own vector and
+// step s of a launch uses epoch `epoch + s`, so a word is rewritten only in
+// the next step, after every CTA has published its LM-head partial of this
+// step (which it does after all of its reads of the step). Data that is not
+// flagged (the K/V cache rows, the attention split records) is written
+// before a __threadfence() and read after one.
 //
 // Weight streaming. Each weight phase gives CTA c a contiguous slice of row
 // pairs, so a CTA's weights for the whole launch form a fixed list of
 // contiguous byte ranges ("chunks", at most one shared-memory buffer each).
-// kRing buffers per CTA: thread 0 issues the cp.async.bulk copy of chunk
-// g+kRing as soon as chunk g has been consumed, with completion on the
-// buffer's mbarrier. Weights never depend on activations, so copies run ahead across
-// phase and layer boundaries while the grid waits at barriers. Attention
-// CTAs also prefetch their K/V cache rows into L2 during the QKV phase.
+// kRing buffers per CTA: thread 0 issues the cp.async.bulk copy (no
+// multicast) of chunk g+kRing as soon as chunk g has been consumed, with
+// completion on the buffer's mbarrier. Weights never depend on activations,
+// so copies run ahead across phase and layer boundaries while a CTA waits
+// for its inputs. Attention CTAs prefetch their K/V rows into L2 during the
+// QKV phase.
 //
-// Activations are read with ld.global.cg (L2), never from a possibly stale
-// L1 line. Every wait is bounded (2 s): a timeout sets *err, later waits
-// return at once, the kernel runs to its end and the host reports the error.
-// All issued copies are consumed (waited on) before the kernel ends.
+// Every wait is bounded (2 s): a timeout sets *err, later waits return at
+// once, the kernel runs to its end and the host reports the error. All
+// issued copies are consumed (waited on) before the kernel ends.
 //
 // Math per element is the same as the multi-kernel path (kernels.cu) and
 // the reference (source/transformer.c:1186-1602).
@@ -47,16 +59,6 @@ constexpr size_t kSmemBudget = 220 * 1024;  // dynamic shared memory per CTA
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
-}
-
-__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
-  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ unsigned long long now_ns() {
@@ -98,48 +100,95 @@ __device__ __forceinline__ void bulk_copy(void* dst, const void* src, unsigned b
       : "memory");
 }
 
-// Trace record per (barrier, CTA): [arrive, release, staged, first chunk
-// ready, phase consumed] (%globaltimer ns; thread 0 writes them).
-constexpr int kTraceWidth = kMegaTraceWidth;
-enum { MARK_STAGED = 2, MARK_READY = 3, MARK_CONSUMED = 4, MARK_COMPUTED = 5, MARK_ISSUED = 6 };
+// ---------------------------------------------------------------------------
+// Flagged vectors
+// ---------------------------------------------------------------------------
+typedef unsigned long long u64;
 
-__device__ __forceinline__ void trace_mark(const MegaArgs& a, int nbar, int slot) {
-  if (a.trace && nbar < a.trace_barriers && threadIdx.x == 0)
-    a.trace[((size_t)nbar * gridDim.x + blockIdx.x) * kTraceWidth + slot] = now_ns();
+__device__ __forceinline__ void ll_store(u64* p, float v, unsigned e) {
+  const u64 w = ((u64)e << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ u64 ll_load(const u64* p) {
+  u64 w;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+__device__ __forceinline__ bool ll_ready(u64 w, unsigned e) { return (unsigned)(w >> 32) == e; }
+__device__ __forceinline__ float ll_value(u64 w) { return __uint_as_float((unsigned)w); }
+
+// Bounded spinning: false once the wait has run out (error flag set) or the
+// error flag is already set.
+struct Spin {
+  unsigned long long t0 = 0;
+  unsigned n = 0;
+};
+__device__ __forceinline__ bool spin_on(const MegaArgs& a, Spin& s) {
+  if ((++s.n & 15) != 0) return true;
+  if (*(volatile int*)a.err) return false;
+  const unsigned long long t = now_ns();
+  if (s.t0 == 0) s.t0 = t;
+  if (t - s.t0 > kTimeoutNs) {
+    atomicExch(a.err, 1);
+    return false;
+  }
+  return true;
 }
 
-// ---------------------------------------------------------------------------
-// Grid barrier: a monotonic arrival counter (zeroed by the host before each
-// launch); barrier n completes when the counter reaches (n+1) * gridDim.x.
-// ---------------------------------------------------------------------------
-__device__ void grid_barrier(const MegaArgs& a, int& nbar) {
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const bool tr = a.trace && nbar < a.trace_barriers;
-    unsigned long long* slot =
-        tr ? a.trace + ((size_t)nbar * gridDim.x + blockIdx.x) * kTraceWidth : nullptr;
-    if (tr) slot[0] = now_ns();
-    const unsigned target = (unsigned)(nbar + 1) * gridDim.x;
-    __threadfence();
-    red_release_add(&a.bar[0], 1u);
-    if (!*(volatile int*)a.err) {
-      const unsigned long long t0 = now_ns();
-      unsigned spins = 0;
-      while ((int)(ld_acquire_u32(&a.bar[0]) - target) < 0) {
-        // The timer and the error flag are checked every 64 polls only.
-        if ((++spins & 63) == 0) {
-          if (*(volatile int*)a.err) break;
-          if (now_ns() - t0 > kTimeoutNs) {
-            atomicExch(a.err, 1);
-            break;
-          }
-        }
-      }
-    }
-    if (tr) slot[1] = now_ns();
+// Loads the flagged words src[k] for the N slots k = k0 + u * kstride
+// (slots with k >= K are skipped) and waits until all carry epoch e; the
+// values land in v[]. All loads of a round are issued before any is tested.
+template <int N>
+__device__ __forceinline__ void ll_gather(const MegaArgs& a, const u64* src, int k0, int kstride,
+                                          int K, unsigned e, float* v) {
+  u64 w[N];
+#pragma unroll
+  for (int u = 0; u < N; u++) {
+    const int k = k0 + u * kstride;
+    w[u] = (k < K) ? ll_load(src + k) : ((u64)e << 32);
   }
-  nbar++;
-  __syncthreads();
+  unsigned pending = 0;
+#pragma unroll
+  for (int u = 0; u < N; u++)
+    if (!ll_ready(w[u], e)) pending |= 1u << u;
+  Spin sp;
+  while (pending) {
+    if (!spin_on(a, sp)) break;
+#pragma unroll
+    for (int u = 0; u < N; u++)
+      if (pending & (1u << u)) w[u] = ll_load(src + k0 + u * kstride);
+#pragma unroll
+    for (int u = 0; u < N; u++)
+      if ((pending & (1u << u)) && ll_ready(w[u], e)) pending &= ~(1u << u);
+  }
+#pragma unroll
+  for (int u = 0; u < N; u++) v[u] = ll_value(w[u]);
+}
+
+// Trace record per (phase, CTA): [stage start, inputs complete, staged,
+// first chunk ready, consumed] (%globaltimer ns), then the phase's total ns
+// spent waiting for weight buffers and computing on them (thread 0 writes
+// them).
+constexpr int kTraceWidth = kMegaTraceWidth;
+enum {
+  MARK_BEGIN = 0,
+  MARK_INPUTS = 1,
+  MARK_STAGED = 2,
+  MARK_READY = 3,
+  MARK_CONSUMED = 4,
+  SUM_WAIT = 5,
+  SUM_COMPUTE = 6
+};
+
+__device__ __forceinline__ void trace_put(const MegaArgs& a, int ph, int slot,
+                                          unsigned long long v) {
+  if (a.trace && ph < a.trace_phases && threadIdx.x == 0)
+    a.trace[((size_t)ph * gridDim.x + blockIdx.x) * kTraceWidth + slot] = v;
+}
+
+__device__ __forceinline__ void trace_mark(const MegaArgs& a, int ph, int slot) {
+  if (a.trace && ph < a.trace_phases && threadIdx.x == 0)
+    a.trace[((size_t)ph * gridDim.x + blockIdx.x) * kTraceWidth + slot] = now_ns();
 }
 
 // ---------------------------------------------------------------------------
@@ -253,14 +302,10 @@ __device__ __forceinline__ Chunk slice_chunk(const Slice& s, const Phase& ph, in
 }
 
 // Copy-issue cursor (thread 0 only): walks the same chunk sequence as the
-// consumers, two chunks ahead.
+// consumers, kRing chunks ahead.
 struct Cursor {
   int step, wp, ci;
 };
-
-__device__ __forceinline__ bool cursor_valid(const MegaArgs& a, const Cursor& c) {
-  return c.step < a.steps;
-}
 
 // This CTA's slice of each weight-phase kind (QKV, O, GU, DOWN, LM); every
 // layer has the same shapes, so they are computed once per launch.
@@ -280,7 +325,7 @@ __device__ void cursor_skip_empty(const MegaArgs& a, Cursor& c) {
 
 __device__ void cursor_issue(const MegaArgs& a, Cursor& c, char* buf, uint64_t* bar) {
   cursor_skip_empty(a, c);
-  if (!cursor_valid(a, c)) return;
+  if (c.step >= a.steps) return;
   const Phase ph = weight_phase(a, c.wp);
   const Slice& s = s_slices[ph.kind];
   const Chunk ch = slice_chunk(s, ph, c.ci);
@@ -322,156 +367,75 @@ __device__ __forceinline__ int split_index(int k, int K) {
   return (((k >> 2) & 1) * (K >> 1)) + ((k >> 3) << 2) + (k & 3);
 }
 
-// Largest K an RMSNorm staging keeps in registers (K = embedding_dim).
+// Largest K an RMSNorm staging keeps in registers (K = embedding_dim), read
+// in rounds of kNormBatch words per thread.
+constexpr int kNormBatch = 8;
 constexpr int kNormRegs = 32;
-constexpr int kNormMaxK = kNormRegs * kThreads;
 
-// xs (split layout) = rmsnorm(xin) * nw, or xin when nw is null. One round
-// trip to global memory: every thread loads its x values and gains at once,
-// keeps them in registers across the block-wide sum of squares, and writes
-// the normalised products.
-__device__ void stage_x(const float* xin, const uint16_t* nw, float eps, int K, float* xs,
-                        float* red) {
+// xs (split layout) = rmsnorm(x) * nw from the flagged vector src (epoch e);
+// the raw values also go to xraw[K]. Every thread owns k = tid + u * 256.
+__device__ void stage_norm_ll(const MegaArgs& a, const u64* src, unsigned e, const uint16_t* nw,
+                              int K, float* xs, float* xraw, float* red, int ph) {
   const int tid = threadIdx.x;
-  constexpr int B = 8;  // loads in flight per thread
-  if (nw) {
-    float v[kNormRegs], g[kNormRegs];
-    float ss = 0.f;
+  float v[kNormRegs], g[kNormRegs];
+  float ss = 0.f;
+  // The gains do not depend on the inputs: their loads go out first.
 #pragma unroll
-    for (int u = 0; u < kNormRegs; u++) {
-      const int k = tid + u * kThreads;
-      v[u] = (k < K) ? __ldcg(xin + k) : 0.f;
-      g[u] = (k < K) ? bf16_to_f32(__ldg(nw + k)) : 0.f;
+  for (int u = 0; u < kNormRegs; u++) {
+    const int k = tid + u * kThreads;
+    g[u] = (k < K) ? bf16_to_f32(__ldg(nw + k)) : 0.f;
+  }
+#pragma unroll
+  for (int b = 0; b < kNormRegs; b += kNormBatch) {
+    if (b * kThreads < K) {
+      ll_gather<kNormBatch>(a, src, tid + b * kThreads, kThreads, K, e, v + b);
+    } else {
+#pragma unroll
+      for (int u = 0; u < kNormBatch; u++) v[b + u] = 0.f;
     }
+  }
+  trace_mark(a, ph, MARK_INPUTS);
 #pragma unroll
-    for (int u = 0; u < kNormRegs; u++) ss += v[u] * v[u];
-    ss = block_sum(ss, red);
-    ss /= (float)K;
-    const float inv = 1.0f / sqrtf(ss + eps);
+  for (int u = 0; u < kNormRegs; u++) {
+    const int k = tid + u * kThreads;
+    if (k >= K) v[u] = 0.f;
+    ss += v[u] * v[u];
+  }
+  ss = block_sum(ss, red);
+  ss /= (float)K;
+  const float inv = 1.0f / sqrtf(ss + a.eps);
 #pragma unroll
-    for (int u = 0; u < kNormRegs; u++) {
-      const int k = tid + u * kThreads;
-      if (k < K) xs[split_index(k, K)] = (v[u] * inv) * g[u];
-    }
-  } else {
-    for (int base = tid; base < K; base += B * kThreads) {
-      float v[B];
-#pragma unroll
-      for (int u = 0; u < B; u++) {
-        const int k = base + u * kThreads;
-        v[u] = (k < K) ? __ldcg(xin + k) : 0.f;
-      }
-#pragma unroll
-      for (int u = 0; u < B; u++) {
-        const int k = base + u * kThreads;
-        if (k < K) xs[split_index(k, K)] = v[u];
-      }
+  for (int u = 0; u < kNormRegs; u++) {
+    const int k = tid + u * kThreads;
+    if (k < K) {
+      xs[split_index(k, K)] = (v[u] * inv) * g[u];
+      xraw[k] = v[u];
     }
   }
   __syncthreads();
 }
 
-// Attention output for the O phase, merged from the per-split partial
-// records [m, l, -, -, acc[HD]] of every query head:
-// att = sum_j c_j acc_j / sum_j c_j l_j with c_j = exp(m_j - max_j m_j);
-// splits without positions have m = -inf. Pass 1: a warp per head (two
-// heads per pass, loads together) computes the split weights c_j and the
-// denominator into shared memory (`cw`: QHl*nsplit + QHl floats). Pass 2:
-// every thread owns float4 slots of the output.
-template <int HD>
-__device__ void stage_attention(const MegaArgs& a, float* xs, float* cw) {
-  constexpr int PS = HD + 4;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int ns = a.nsplit, QD = a.QHl * HD;
-  float* Lh = cw + a.QHl * ns;
-  for (int h0 = warp; h0 < a.QHl; h0 += 2 * kWarps) {
-    const int hs[2] = {h0, h0 + kWarps};
-    float c0[2], c1[2], L[2];
+// xs (split layout) = the flagged vector src (epoch e), K floats.
+__device__ void stage_plain_ll(const MegaArgs& a, const u64* src, unsigned e, int K, float* xs,
+                               int ph) {
+  const int tid = threadIdx.x;
+  constexpr int B = 16;
+  for (int base = tid; base < K; base += B * kThreads) {
+    float v[B];
+    ll_gather<B>(a, src, base, kThreads, K, e, v);
 #pragma unroll
-    for (int t = 0; t < 2; t++) {
-      float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-      if (hs[t] < a.QHl) {
-        const float* P0 = a.attn_partial + (size_t)hs[t] * ns * PS;
-        if (lane < ns) {
-          m0 = __ldcg(P0 + (size_t)lane * PS);
-          l0 = __ldcg(P0 + (size_t)lane * PS + 1);
-        }
-        if (lane + 32 < ns) {
-          m1 = __ldcg(P0 + (size_t)(lane + 32) * PS);
-          l1 = __ldcg(P0 + (size_t)(lane + 32) * PS + 1);
-        }
-      }
-      const float M = warp_max(fmaxf(m0, m1));
-      c0[t] = (m0 == -INFINITY) ? 0.f : expf(m0 - M);
-      c1[t] = (m1 == -INFINITY) ? 0.f : expf(m1 - M);
-      L[t] = warp_sum(c0[t] * l0 + c1[t] * l1);
-    }
-#pragma unroll
-    for (int t = 0; t < 2; t++) {
-      if (hs[t] >= a.QHl) continue;
-      if (lane < ns) cw[hs[t] * ns + lane] = c0[t];
-      if (lane + 32 < ns) cw[hs[t] * ns + lane + 32] = c1[t];
-      if (lane == 0) Lh[hs[t]] = L[t];
+    for (int u = 0; u < B; u++) {
+      const int k = base + u * kThreads;
+      if (k < K) xs[split_index(k, K)] = v[u];
     }
   }
-  __syncthreads();
-  // Pass 2: each thread owns float4 slots of the QD outputs and sums them
-  // over the splits, kJB splits' loads in flight per batch.
-  constexpr int kSlots = 4;  // QD <= 4 * 4 * kThreads
-  constexpr int kJB = 6;
-  const int nslot = QD / 4;
-  float4 acc[kSlots];
-#pragma unroll
-  for (int s = 0; s < kSlots; s++) acc[s] = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int jb = 0; jb < ns; jb += kJB) {
-    float4 v[kSlots][kJB];
-#pragma unroll
-    for (int s = 0; s < kSlots; s++) {
-      const int slot = threadIdx.x + s * kThreads;
-      const int h = (slot * 4) / HD, d = (slot * 4) % HD;
-#pragma unroll
-      for (int jj = 0; jj < kJB; jj++) {
-        const int j = jb + jj;
-        v[s][jj] = (slot < nslot && j < ns)
-                       ? __ldcg(reinterpret_cast<const float4*>(
-                             a.attn_partial + ((size_t)h * ns + j) * PS + 4 + d))
-                       : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-    }
-#pragma unroll
-    for (int s = 0; s < kSlots; s++) {
-      const int slot = threadIdx.x + s * kThreads;
-      if (slot >= nslot) continue;
-      const int h = (slot * 4) / HD;
-#pragma unroll
-      for (int jj = 0; jj < kJB; jj++) {
-        const int j = jb + jj;
-        if (j >= ns) continue;
-        const float c = cw[h * ns + j];
-        acc[s].x = fmaf(c, v[s][jj].x, acc[s].x);
-        acc[s].y = fmaf(c, v[s][jj].y, acc[s].y);
-        acc[s].z = fmaf(c, v[s][jj].z, acc[s].z);
-        acc[s].w = fmaf(c, v[s][jj].w, acc[s].w);
-      }
-    }
-  }
-#pragma unroll
-  for (int s = 0; s < kSlots; s++) {
-    const int slot = threadIdx.x + s * kThreads;
-    if (slot >= nslot) continue;
-    const int k = slot * 4, h = k / HD;
-    const float L = Lh[h];
-    xs[split_index(k, QD)] = acc[s].x / L;
-    xs[split_index(k + 1, QD)] = acc[s].y / L;
-    xs[split_index(k + 2, QD)] = acc[s].z / L;
-    xs[split_index(k + 3, QD)] = acc[s].w / L;
-  }
+  trace_mark(a, ph, MARK_INPUTS);
   __syncthreads();
 }
 
-// Layer-0 input: the embedding row of `token`; CTA 0 also writes x.
+// Layer-0 input: the embedding row of `token` (xraw) and its RMSNorm (xs).
 __device__ void stage_embedding(const MegaArgs& a, int token, const uint16_t* nw, float* xs,
-                                float* red) {
+                                float* xraw, float* red) {
   const int tid = threadIdx.x, K = a.D;
   const uint16_t* row = a.emb + (size_t)token * K;
   float v[kNormRegs], g[kNormRegs];
@@ -483,18 +447,17 @@ __device__ void stage_embedding(const MegaArgs& a, int token, const uint16_t* nw
     g[u] = (k < K) ? bf16_to_f32(__ldg(nw + k)) : 0.f;
   }
 #pragma unroll
-  for (int u = 0; u < kNormRegs; u++) {
-    const int k = tid + u * kThreads;
-    ss += v[u] * v[u];
-    if (blockIdx.x == 0 && k < K) a.x[k] = v[u];
-  }
+  for (int u = 0; u < kNormRegs; u++) ss += v[u] * v[u];
   ss = block_sum(ss, red);
   ss /= (float)K;
   const float inv = 1.0f / sqrtf(ss + a.eps);
 #pragma unroll
   for (int u = 0; u < kNormRegs; u++) {
     const int k = tid + u * kThreads;
-    if (k < K) xs[split_index(k, K)] = (v[u] * inv) * g[u];
+    if (k < K) {
+      xs[split_index(k, K)] = (v[u] * inv) * g[u];
+      xraw[k] = v[u];
+    }
   }
   __syncthreads();
 }
@@ -505,28 +468,35 @@ __device__ void stage_embedding(const MegaArgs& a, int token, const uint16_t* nw
 constexpr int kRing = 4;  // weight buffers per CTA
 
 struct Ring {
-  char* buf[kRing];
+  char* base;      // buffer b starts at base + b * buf_bytes
   uint64_t* bar;   // [kRing] in shared memory
   int buf_bytes;
   unsigned g;      // chunks consumed so far
   Cursor cur;      // thread 0: next chunk to issue
 };
 
-__device__ __forceinline__ void pair_epilogue(const MegaArgs& a, int kind, int pair, float y0,
-                                              float y1, float& bv, int& bi) {
+// Where a phase's outputs go.
+struct Out {
+  u64* dst;            // flagged vector of the phase (null for the LM head)
+  const float* xraw;   // residual input (O, DOWN)
+  unsigned e;
+};
+
+__device__ __forceinline__ void pair_epilogue(const MegaArgs& a, const Out& o, int kind, int pair,
+                                              float y0, float y1, float& bv, int& bi) {
   const int r0 = 2 * pair;
   switch (kind) {
     case W_QKV:
-      a.qkv[r0] = y0;
-      a.qkv[r0 + 1] = y1;
+      ll_store(o.dst + r0, y0, o.e);
+      ll_store(o.dst + r0 + 1, y1, o.e);
       break;
     case W_O:
     case W_DOWN:
-      a.x[r0] = __ldcg(a.x + r0) + y0;
-      a.x[r0 + 1] = __ldcg(a.x + r0 + 1) + y1;
+      ll_store(o.dst + r0, o.xraw[r0] + y0, o.e);
+      ll_store(o.dst + r0 + 1, o.xraw[r0 + 1] + y1, o.e);
       break;
     case W_GU:
-      a.h[pair] = swiglu(y0, y1);
+      ll_store(o.dst + pair, swiglu(y0, y1), o.e);
       break;
     default:
       if (a.write_logits) {
@@ -547,23 +517,70 @@ __device__ __forceinline__ void pair_epilogue(const MegaArgs& a, int kind, int p
 
 // Consumes every chunk of weight phase `wp` with activations in xs (split
 // layout, K floats). For the LM head, (bv, bi) track the warp's argmax.
-__device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const float* xs,
-                              float* red, float& bv, int& bi, int nbar) {
-  trace_mark(a, nbar, MARK_STAGED);
-  const Phase ph = weight_phase(a, wp);
-  const Slice s = s_slices[ph.kind];
+__device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const float* xs, const Out& o,
+                              float* red, float& bv, int& bi, int ph) {
+  trace_mark(a, ph, MARK_STAGED);
+  const Phase phs = weight_phase(a, wp);
+  const Slice s = s_slices[phs.kind];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int K = ph.K;
+  const int K = phs.K;
   const float4* lo4 = reinterpret_cast<const float4*>(xs);
   const float4* hi4 = lo4 + (K >> 3);
   float acc0 = 0.f, acc1 = 0.f;  // split rows: running sums (thread 0)
+  const bool tr = a.trace != nullptr;
+  unsigned long long t_wait = 0, t_comp = 0, t0 = 0;
   for (int ci = 0; ci < s.nchunks; ci++) {
     const int b = r.g % kRing;
+    if (tr) t0 = now_ns();
     wait_buffer(a, r.bar + b, (r.g / kRing) & 1);
-    if (ci == 0) trace_mark(a, nbar, MARK_READY);
-    const Chunk c = slice_chunk(s, ph, ci);
-    const uint16_t* wb = reinterpret_cast<const uint16_t*>(r.buf[b]);
-    if (s.ppc) {
+    if (tr) {
+      const unsigned long long t1 = now_ns();
+      t_wait += t1 - t0;
+      t0 = t1;
+    }
+    if (ci == 0) trace_mark(a, ph, MARK_READY);
+    const Chunk c = slice_chunk(s, phs, ci);
+    const uint16_t* wb = reinterpret_cast<const uint16_t*>(r.base + (size_t)b * r.buf_bytes);
+    if (s.ppc && c.p1 - c.p0 < kWarps) {
+      // Fewer pairs than warps: wpp warps share each pair along K, the
+      // partial sums meet in shared memory, lane 0 of warp i finishes pair i.
+      const int P = c.p1 - c.p0;
+      const int wpp = kWarps / P;
+      const int pi = warp / wpp, part = warp % wpp;
+      float a0 = 0.f, a1 = 0.f;
+      if (pi < P) {
+        const uint16_t* w0 = wb + (size_t)pi * 2 * K;
+        const uint16_t* w1 = w0 + K;
+        float s0[8], s1[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) s0[i] = s1[i] = 0.f;
+#pragma unroll 4
+        for (int k = part * 256 + lane * 8; k < K; k += wpp * 256) {
+          const uint4 v0 = *reinterpret_cast<const uint4*>(w0 + k);
+          const uint4 v1 = *reinterpret_cast<const uint4*>(w1 + k);
+          const float4 xa = lo4[k >> 3], xb = hi4[k >> 3];
+          acc8(v0, xa, xb, s0);
+          acc8(v1, xa, xb, s1);
+        }
+        a0 = ((s0[0] + s0[1]) + (s0[2] + s0[3])) + ((s0[4] + s0[5]) + (s0[6] + s0[7]));
+        a1 = ((s1[0] + s1[1]) + (s1[2] + s1[3])) + ((s1[4] + s1[5]) + (s1[6] + s1[7]));
+        a0 = warp_sum(a0);
+        a1 = warp_sum(a1);
+      }
+      if (lane == 0) {
+        red[warp] = a0;
+        red[kWarps + warp] = a1;
+      }
+      __syncthreads();
+      if (lane == 0 && warp < P) {
+        float y0 = 0.f, y1 = 0.f;
+        for (int q = 0; q < wpp; q++) {
+          y0 += red[warp * wpp + q];
+          y1 += red[kWarps + warp * wpp + q];
+        }
+        pair_epilogue(a, o, phs.kind, c.p0 + warp, y0, y1, bv, bi);
+      }
+    } else if (s.ppc) {
       for (int p = c.p0 + warp; p < c.p1; p += kWarps) {
         const uint16_t* w0 = wb + (size_t)(p - c.p0) * 2 * K;
         const uint16_t* w1 = w0 + K;
@@ -584,7 +601,7 @@ __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const float* x
         float a1 = ((s1[0] + s1[1]) + (s1[2] + s1[3])) + ((s1[4] + s1[5]) + (s1[6] + s1[7]));
         a0 = warp_sum(a0);
         a1 = warp_sum(a1);
-        if (lane == 0) pair_epilogue(a, ph.kind, p, a0, a1, bv, bi);
+        if (lane == 0) pair_epilogue(a, o, phs.kind, p, a0, a1, bv, bi);
       }
     } else {
       const int seg = c.k1 - c.k0;
@@ -617,35 +634,59 @@ __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const float* x
           acc1 += red[kWarps + w];
         }
         if (c.last_seg) {
-          pair_epilogue(a, ph.kind, c.p0, acc0, acc1, bv, bi);
+          pair_epilogue(a, o, phs.kind, c.p0, acc0, acc1, bv, bi);
           acc0 = acc1 = 0.f;
         }
       }
     }
-    if (ci == s.nchunks - 1) trace_mark(a, nbar, MARK_COMPUTED);
     __syncthreads();  // buffer b fully read
-    if (tid == 0) cursor_issue(a, r.cur, r.buf[b], r.bar + b);
-    if (ci == s.nchunks - 1) trace_mark(a, nbar, MARK_ISSUED);
+    if (tid == 0) cursor_issue(a, r.cur, r.base + (size_t)b * r.buf_bytes, r.bar + b);
+    if (tr) t_comp += now_ns() - t0;
     r.g++;
   }
-  trace_mark(a, nbar, MARK_CONSUMED);
+  trace_mark(a, ph, MARK_CONSUMED);
+  trace_put(a, ph, SUM_WAIT, t_wait);
+  trace_put(a, ph, SUM_COMPUTE, t_comp);
 }
 
 // ---------------------------------------------------------------------------
 // Attention
 // ---------------------------------------------------------------------------
-// One warp: out[i] = RoPE(RMSNorm(src) * nw) for a head of HD values
-// (source/transformer.c:1293-1323); nw may be null. `scratch` holds HD
-// floats private to the warp.
+// The per-lane factors head_norm_rope needs for position `pos` (rope table
+// entries and norm gains), loaded before the head's values are waited for.
 template <int HD>
-__device__ void head_norm_rope(const MegaArgs& a, const float* src, const uint16_t* nw,
-                               int pos, float* scratch, float* out) {
+struct HeadFactors {
+  float ca[HD / 32], cb[HD / 32], g[HD / 32];
+};
+
+template <int HD>
+__device__ __forceinline__ void load_head_factors(const MegaArgs& a, const uint16_t* nw, int pos,
+                                                  HeadFactors<HD>& f) {
   constexpr int V = HD / 32;
   const int lane = threadIdx.x & 31;
-  float v[V];
+  const float* cs = a.rope + (size_t)pos * HD;
+  const int off = a.pair_offset;
 #pragma unroll
-  for (int j = 0; j < V; j++) v[j] = __ldcg(src + lane + 32 * j);
-  if (nw) {
+  for (int j = 0; j < V; j++) {
+    const int i = lane + 32 * j;
+    const bool first = (a.pair_stride == 1) ? (i < a.pair_bound) : ((i & 1) == 0);
+    const int base = first ? i : i - off;
+    f.ca[j] = __ldg(cs + base);
+    f.cb[j] = __ldg(cs + base + off);
+    f.g[j] = nw ? bf16_to_f32(__ldg(nw + i)) : 1.f;
+  }
+}
+
+// One warp: out[i] = RoPE(RMSNorm(v) * nw) for a head of HD values held as
+// V per lane (i = lane + 32 j) (source/transformer.c:1293-1323); without a
+// norm (has_norm false) the values are rotated as they are. `scratch` holds
+// HD floats private to the warp.
+template <int HD>
+__device__ void head_norm_rope(const MegaArgs& a, float* v, bool has_norm,
+                               const HeadFactors<HD>& f, float* scratch, float* out) {
+  constexpr int V = HD / 32;
+  const int lane = threadIdx.x & 31;
+  if (has_norm) {
     float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < V; j++) ss += v[j] * v[j];
@@ -653,12 +694,11 @@ __device__ void head_norm_rope(const MegaArgs& a, const float* src, const uint16
     ss /= (float)HD;
     const float inv = 1.0f / sqrtf(ss + a.eps);
 #pragma unroll
-    for (int j = 0; j < V; j++) v[j] = (v[j] * inv) * bf16_to_f32(nw[lane + 32 * j]);
+    for (int j = 0; j < V; j++) v[j] = (v[j] * inv) * f.g[j];
   }
 #pragma unroll
   for (int j = 0; j < V; j++) scratch[lane + 32 * j] = v[j];
   __syncwarp();
-  const float* cs = a.rope + (size_t)pos * HD;
   const int off = a.pair_offset;
 #pragma unroll
   for (int j = 0; j < V; j++) {
@@ -666,10 +706,10 @@ __device__ void head_norm_rope(const MegaArgs& a, const float* src, const uint16
     const bool first = (a.pair_stride == 1) ? (i < a.pair_bound) : ((i & 1) == 0);
     float o;
     if (first) {
-      o = scratch[i] * cs[i] - scratch[i + off] * cs[i + off];
+      o = scratch[i] * f.ca[j] - scratch[i + off] * f.cb[j];
     } else {
       const int hh = i - off;
-      o = scratch[hh] * cs[hh + off] + scratch[i] * cs[hh];
+      o = scratch[hh] * f.cb[j] + scratch[i] * f.ca[j];
     }
     out[i] = o;
   }
@@ -711,31 +751,60 @@ __device__ void prefetch_gains(const MegaArgs& a, int l) {
 }
 
 template <int HD, int G>
+constexpr int attn_floats() {
+  // qs [G][HD], wm/wl [kWarps][G], wacc [kWarps][G][HD], merge weights
+  // [G][kMaxSplits], denominators [G], last-CTA flag.
+  return G * HD + 2 * kWarps * G + kWarps * G * HD + G * kMaxSplits + G + 4;
+}
+
+// One attention item: kv head kh, cache split sp, at position pos. Its q,
+// k and v come from the flagged qkv vector of layer l (epoch e). The split
+// holding `pos` appends this step's k and v to the cache. The split record
+// [m, l, -, -, acc[HD]] of each of the G query heads goes to attn_partial;
+// the last split of the kv head to finish (ticket) merges the records and
+// publishes the heads' attention output in the flagged att vector.
+template <int HD, int G>
 __device__ void attn_item(const MegaArgs& a, const MegaLayer& ly, int l, int kh, int sp,
-                          int pos, float* sm) {
+                          int pos, unsigned e, float* sm, int ph) {
   constexpr int V = HD / 32;
   constexpr int QF = HD / 16;
   float* qs = sm;                      // [G][HD]
   float* wm = qs + G * HD;             // [kWarps][G]
   float* wl = wm + kWarps * G;         // [kWarps][G]
   float* wacc = wl + kWarps * G;       // [kWarps][G][HD]
+  float* cw = wacc + kWarps * G * HD;  // [G][kMaxSplits]
+  float* Ls = cw + G * kMaxSplits;     // [G]
+  int* is_last = reinterpret_cast<int*>(Ls + G);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const size_t layer_off = (size_t)l * a.KHl * a.ctx * HD;
   float* kb = a.kc + layer_off + (size_t)kh * a.ctx * HD;
   float* vb = a.vc + layer_off + (size_t)kh * a.ctx * HD;
   const int s_begin = sp * a.split_len;
   const int s_end = min(s_begin + a.split_len, pos + 1);
+  const u64* qkv = a.ll + a.llo.qkv + (size_t)l * a.QKVl;
 
-  if (warp < G)
-    head_norm_rope<HD>(a, a.qkv + (size_t)(kh * G + warp) * HD, ly.q_norm, pos,
-                       wacc + (size_t)warp * HD, qs + warp * HD);
+  // The cache rows below `pos` were written in earlier steps (made visible
+  // by the fence at the top of the step).
+  if (warp < G) {
+    HeadFactors<HD> f;
+    load_head_factors<HD>(a, ly.q_norm, pos, f);
+    float v[V];
+    ll_gather<V>(a, qkv + (size_t)(kh * G + warp) * HD, lane, 32, HD, e, v);
+    head_norm_rope<HD>(a, v, ly.q_norm != nullptr, f, wacc + (size_t)warp * HD, qs + warp * HD);
+  }
   if (warp == kWarps - 1 && pos >= s_begin && pos < s_begin + a.split_len) {
-    head_norm_rope<HD>(a, a.qkv + (size_t)(a.QHl + kh) * HD, ly.k_norm, pos,
-                       wacc + (size_t)warp * HD, kb + (size_t)pos * HD);
-    const float* vsrc = a.qkv + (size_t)(a.QHl + a.KHl + kh) * HD;
-    for (int i = lane; i < HD; i += 32) vb[(size_t)pos * HD + i] = __ldcg(vsrc + i);
+    HeadFactors<HD> f;
+    load_head_factors<HD>(a, ly.k_norm, pos, f);
+    float v[V], vv[V];
+    ll_gather<V>(a, qkv + (size_t)(a.QHl + kh) * HD, lane, 32, HD, e, v);
+    ll_gather<V>(a, qkv + (size_t)(a.QHl + a.KHl + kh) * HD, lane, 32, HD, e, vv);
+    head_norm_rope<HD>(a, v, ly.k_norm != nullptr, f, wacc + (size_t)warp * HD,
+                       kb + (size_t)pos * HD);
+#pragma unroll
+    for (int j = 0; j < V; j++) vb[(size_t)pos * HD + lane + 32 * j] = vv[j];
   }
   __syncthreads();
+  trace_mark(a, ph, MARK_INPUTS);
 
   float m[G], lsum[G], acc[G][V];
 #pragma unroll
@@ -821,8 +890,9 @@ __device__ void attn_item(const MegaArgs& a, const MegaLayer& ly, int l, int kh,
   }
   __syncthreads();
   const int nsplit = a.nsplit;
-  for (int e = tid; e < G * HD; e += kThreads) {
-    const int g = e / HD, dd = e % HD;
+  float* part = a.attn_partial + (size_t)l * a.QHl * nsplit * (HD + 4);
+  for (int ei = tid; ei < G * HD; ei += kThreads) {
+    const int g = ei / HD, dd = ei % HD;
     float M = -INFINITY;
     for (int w = 0; w < kWarps; w++) M = fmaxf(M, wm[w * G + g]);
     float L = 0.f, A = 0.f;
@@ -835,17 +905,62 @@ __device__ void attn_item(const MegaArgs& a, const MegaLayer& ly, int l, int kh,
         A += wacc[((size_t)w * G + g) * HD + dd] * c;
       }
     }
-    // Partial record: [m, l, -, -, acc[HD]] (16-byte aligned acc).
-    float* P = a.attn_partial + ((size_t)(kh * G + g) * nsplit + sp) * (HD + 4);
+    // Split record: [m, l, -, -, acc[HD]] (16-byte aligned acc).
+    float* P = part + ((size_t)(kh * G + g) * nsplit + sp) * (HD + 4);
     if (dd == 0) {
       P[0] = M;
       P[1] = L;
     }
     P[4 + dd] = A;
   }
-  // The splits are merged by every CTA while it stages the O phase input
-  // (stage_attention), after the grid barrier.
+  __threadfence();
   __syncthreads();
+  trace_mark(a, ph, MARK_STAGED);
+  if (tid == 0) {
+    int* ticket = a.attn_ticket + (size_t)l * a.KHl + kh;
+    *is_last = (atomicAdd(ticket, 1) == nsplit - 1);
+    if (*is_last) *ticket = 0;  // its next use is in a later step
+  }
+  __syncthreads();
+  if (!*is_last) return;
+  __threadfence();
+  // Merge: att = sum_j c_j acc_j / sum_j c_j l_j, c_j = exp(m_j - max m);
+  // splits without positions have m = -inf.
+  for (int g = warp; g < G; g += kWarps) {
+    const float* P0 = part + (size_t)(kh * G + g) * nsplit * (HD + 4);
+    float mloc = -INFINITY;
+    for (int jx = lane; jx < nsplit; jx += 32)
+      mloc = fmaxf(mloc, __ldcg(P0 + (size_t)jx * (HD + 4)));
+    const float M = warp_max(mloc);
+    float ls = 0.f;
+    for (int jx = lane; jx < nsplit; jx += 32) {
+      const float mj = __ldcg(P0 + (size_t)jx * (HD + 4));
+      const float c = (mj == -INFINITY) ? 0.f : expf(mj - M);
+      cw[g * kMaxSplits + jx] = c;
+      ls += c * __ldcg(P0 + (size_t)jx * (HD + 4) + 1);
+    }
+    ls = warp_sum(ls);
+    if (lane == 0) Ls[g] = ls;
+  }
+  __syncthreads();
+  u64* att = a.ll + a.llo.att + (size_t)l * a.QHl * HD;
+  for (int ei = tid; ei < G * HD; ei += kThreads) {
+    const int g = ei / HD, dd = ei % HD;
+    const float* P0 = part + (size_t)(kh * G + g) * nsplit * (HD + 4) + 4 + dd;
+    float A = 0.f;
+    for (int j0 = 0; j0 < nsplit; j0 += 8) {
+      float pv[8];  // the loads of a batch go out together
+#pragma unroll
+      for (int u = 0; u < 8; u++)
+        pv[u] = (j0 + u < nsplit) ? __ldcg(P0 + (size_t)(j0 + u) * (HD + 4)) : 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; u++)
+        if (j0 + u < nsplit) A = fmaf(cw[g * kMaxSplits + j0 + u], pv[u], A);
+    }
+    ll_store(att + (size_t)(kh * G + g) * HD + dd, A / Ls[g], e);
+  }
+  __syncthreads();
+  trace_mark(a, ph, MARK_READY);
 }
 
 // ---------------------------------------------------------------------------
@@ -861,12 +976,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t ring_bar[kRing];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   Ring r;
-  for (int i = 0; i < kRing; i++) r.buf[i] = dyn + (size_t)i * buf_bytes;
+  r.base = dyn;
   r.bar = ring_bar;
   r.buf_bytes = buf_bytes;
   r.g = 0;
   r.cur = {0, 0, 0};
-  float* xs = reinterpret_cast<float*>(dyn + (size_t)kRing * buf_bytes);
+  float* xraw = reinterpret_cast<float*>(dyn + (size_t)kRing * buf_bytes);  // [D]
+  float* xs = xraw + ((a.D + 31) / 32) * 32;  // matvec input / attention scratch
   for (int i = threadIdx.x; i < a.L; i += kThreads) s_layers[i] = a.layers[i];
   if (threadIdx.x == 0) {
     for (int i = 0; i < kRing; i++) mbar_init(&ring_bar[i], 1);
@@ -880,8 +996,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   __syncthreads();
   if (threadIdx.x == 0)
-    for (int i = 0; i < kRing; i++) cursor_issue(a, r.cur, r.buf[i], &ring_bar[i]);
-  int nbar = 0;
+    for (int i = 0; i < kRing; i++) cursor_issue(a, r.cur, dyn + (size_t)i * buf_bytes, &ring_bar[i]);
+  int ph = 0;  // phase counter (trace only)
   int pos = __ldcg(a.pos);
   int token = __ldcg(a.tok);
   int step = __ldcg(a.step);
@@ -889,42 +1005,55 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int attn_items = a.KHl * a.nsplit;
   float bv = -INFINITY;
   int bi = 0x7FFFFFFF;
+  u64* am = a.ll + a.llo.am;
 
   for (int s = 0; s < a.steps; s++) {
+    const unsigned e = a.epoch + (unsigned)s;
     for (int l = 0; l < a.L; l++) {
       const MegaLayer& ly = s_layers[l];
+      u64* x_o = a.ll + a.llo.x + (size_t)l * 2 * a.D;  // after o_proj
+      u64* x_d = x_o + a.D;                              // after down
       // QKV
+      trace_mark(a, ph, MARK_BEGIN);
       prefetch_kv<HD>(a, l, pos);
       prefetch_gains(a, l + 1);
       if (l == 0)
-        stage_embedding(a, token, ly.attn_norm, xs, red);
+        stage_embedding(a, token, ly.attn_norm, xs, xraw, red);
       else
-        stage_x(a.x, ly.attn_norm, a.eps, a.D, xs, red);
-      consume_phase(a, r, 4 * l + W_QKV, xs, red, bv, bi, nbar);
-      grid_barrier(a, nbar);
+        stage_norm_ll(a, x_o - 2 * (size_t)a.D + a.D, e, ly.attn_norm, a.D, xs, xraw, red, ph);
+      consume_phase(a, r, 4 * l + W_QKV, xs,
+                    Out{a.ll + a.llo.qkv + (size_t)l * a.QKVl, nullptr, e}, red, bv, bi, ph);
+      ph++;
       // ATTN
+      trace_mark(a, ph, MARK_BEGIN);
       for (int it = blockIdx.x; it < attn_items; it += gridDim.x)
-        attn_item<HD, G>(a, ly, l, it % a.KHl, it / a.KHl, pos, xs);
-      grid_barrier(a, nbar);
-      // O + residual (input: the attention splits, merged here)
-      stage_attention<HD>(a, xs, xs + QD);
-      consume_phase(a, r, 4 * l + W_O, xs, red, bv, bi, nbar);
-      grid_barrier(a, nbar);
+        attn_item<HD, G>(a, ly, l, it % a.KHl, it / a.KHl, pos, e, xs, ph);
+      ph++;
+      // O + residual
+      trace_mark(a, ph, MARK_BEGIN);
+      stage_plain_ll(a, a.ll + a.llo.att + (size_t)l * QD, e, QD, xs, ph);
+      consume_phase(a, r, 4 * l + W_O, xs, Out{x_o, xraw, e}, red, bv, bi, ph);
+      ph++;
       // gate/up + SwiGLU
-      stage_x(a.x, ly.ffn_norm, a.eps, a.D, xs, red);
-      consume_phase(a, r, 4 * l + W_GU, xs, red, bv, bi, nbar);
-      grid_barrier(a, nbar);
+      trace_mark(a, ph, MARK_BEGIN);
+      stage_norm_ll(a, x_o, e, ly.ffn_norm, a.D, xs, xraw, red, ph);
+      consume_phase(a, r, 4 * l + W_GU, xs, Out{a.ll + a.llo.h + (size_t)l * a.Fl, nullptr, e},
+                    red, bv, bi, ph);
+      ph++;
       // down + residual
-      stage_x(a.h, nullptr, 0.f, a.Fl, xs, red);
-      consume_phase(a, r, 4 * l + W_DOWN, xs, red, bv, bi, nbar);
-      grid_barrier(a, nbar);
+      trace_mark(a, ph, MARK_BEGIN);
+      stage_plain_ll(a, a.ll + a.llo.h + (size_t)l * a.Fl, e, a.Fl, xs, ph);
+      consume_phase(a, r, 4 * l + W_DOWN, xs, Out{x_d, xraw, e}, red, bv, bi, ph);
+      ph++;
     }
     // LM head with per-CTA argmax
+    trace_mark(a, ph, MARK_BEGIN);
     prefetch_gains(a, 0);  // next step's layer 0
-    stage_x(a.x, a.out_norm, a.eps, a.D, xs, red);
+    stage_norm_ll(a, a.ll + a.llo.x + (size_t)(a.L - 1) * 2 * a.D + a.D, e, a.out_norm, a.D, xs,
+                  xraw, red, ph);
     bv = -INFINITY;
     bi = 0x7FFFFFFF;
-    consume_phase(a, r, 4 * a.L, xs, red, bv, bi, nbar);
+    consume_phase(a, r, 4 * a.L, xs, Out{nullptr, nullptr, e}, red, bv, bi, ph);
     if (lane == 0) {
       cbest_v[warp] = bv;
       cbest_i[warp] = bi;
@@ -939,20 +1068,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           i = cbest_i[w];
         }
       }
-      a.am_val[blockIdx.x] = v;
-      a.am_idx[blockIdx.x] = i;
+      ll_store(am + blockIdx.x, v, e);
+      ll_store(am + gridDim.x + blockIdx.x, __int_as_float(i), e);
     }
-    grid_barrier(a, nbar);
-    // Every CTA reduces the partials itself (no extra barrier).
+    ph++;
+    // Every CTA reduces the published partials itself.
     if (warp == 0) {
       float v = -INFINITY;
       int i = 0x7FFFFFFF;
-      for (int b = lane; b < (int)gridDim.x; b += 32) {
-        const float vb = __ldcg(a.am_val + b);
-        const int ib = __ldcg(a.am_idx + b);
-        if (vb > v || (vb == v && ib < i)) {
-          v = vb;
-          i = ib;
+      for (int b0 = 0; b0 < (int)gridDim.x; b0 += 32 * 4) {
+        float vb[4], ib[4];
+        ll_gather<4>(a, am, b0 + lane, 32, gridDim.x, e, vb);
+        ll_gather<4>(a, am + gridDim.x, b0 + lane, 32, gridDim.x, e, ib);
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          if (b0 + lane + 32 * u >= (int)gridDim.x) continue;
+          const int ii = __float_as_int(ib[u]);
+          if (vb[u] > v || (vb[u] == v && ii < i)) {
+            v = vb[u];
+            i = ii;
+          }
         }
       }
       for (int o = 16; o > 0; o >>= 1) {
@@ -967,6 +1102,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncthreads();
     token = cbest_i[0];
+    // Every CTA has published its partial after writing this step's K/V
+    // rows (and a fence): the next step's attention reads them after this
+    // one.
+    __threadfence();
     if (blockIdx.x == 0 && threadIdx.x == 0 && step >= 0 && step < a.gen_len)
       a.gen[step] = token;
     step++;
@@ -978,11 +1117,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     *a.pos = pos;
     *a.step = step;
   }
-}
-
-template <int HD, int G>
-size_t attn_smem() {
-  return sizeof(float) * ((size_t)G * HD + 2 * kWarps * G + (size_t)kWarps * G * HD + 4);
 }
 
 template <int HD, int G>
@@ -1000,9 +1134,9 @@ void* select(int HD, int G) {
   return nullptr;
 }
 
-size_t select_attn_smem(int HD, int G) {
+size_t select_attn_floats(int HD, int G) {
 #define SG_SEL(h, g) \
-  if (HD == h && G == g) return attn_smem<h, g>();
+  if (HD == h && G == g) return (size_t)attn_floats<h, g>();
   SG_SEL(32, 1) SG_SEL(32, 2) SG_SEL(32, 4) SG_SEL(32, 8)
   SG_SEL(64, 1) SG_SEL(64, 2) SG_SEL(64, 4) SG_SEL(64, 8)
   SG_SEL(128, 1) SG_SEL(128, 2) SG_SEL(128, 4) SG_SEL(128, 8)
@@ -1010,19 +1144,31 @@ size_t select_attn_smem(int HD, int G) {
   return 0;
 }
 
-// Activation / attention region, rounded to 128 bytes.
-// (matvec input; attention item; O-phase input plus split-merge weights).
+// Activation region, rounded to 128 bytes: the residual copy xraw [D]
+// (rounded to 32 floats), then the matvec input or the attention scratch.
 size_t act_bytes(int D, int QD, int Fl, int HD, int G) {
-  size_t k = (size_t)std::max(D, std::max(QD, Fl)) * sizeof(float);
-  k = std::max(k, select_attn_smem(HD, G));
-  k = std::max(k, sizeof(float) * ((size_t)QD + (size_t)(QD / HD) * (kMaxSplits + 1)));
-  return (k + 127) / 128 * 128;
+  size_t k = (size_t)std::max(D, std::max(QD, Fl));
+  k = std::max(k, select_attn_floats(HD, G));
+  k += (size_t)(D + 31) / 32 * 32;
+  return (k * sizeof(float) + 127) / 128 * 128;
 }
 
 }  // namespace
 
-// Two weight buffers take what the activations leave of the budget.
+MegaFlagged mega_flagged_layout(int D, int QKVl, int QD, int Fl, int L, int grid) {
+  MegaFlagged f;
+  f.x = 0;
+  f.qkv = f.x + (size_t)L * 2 * D;
+  f.att = f.qkv + (size_t)L * QKVl;
+  f.h = f.att + (size_t)L * QD;
+  f.am = f.h + (size_t)L * Fl;
+  f.total = f.am + 2 * (size_t)grid;
+  return f;
+}
+
+// Ring buffers take what the activations leave of the budget.
 size_t mega_smem_bytes(int D, int QD, int Fl, int HD, int G) {
+  if (D > kNormRegs * kThreads) return 0;
   const size_t act = act_bytes(D, QD, Fl, HD, G);
   if (act + (size_t)kRing * 8 * 1024 > kSmemBudget) return 0;
   size_t buf = (kSmemBudget - act) / kRing / 1024 * 1024;
@@ -1066,10 +1212,9 @@ void mega_decode(const MegaArgs& a, int grid, size_t smem, cudaStream_t s) {
   void* k = select(a.HD, a.G);
   if (!k) SG_DIE("megakernel: unsupported head_dim / group");
   if (a.nsplit > kMaxSplits) SG_DIE("megakernel: too many attention splits");
+  if (a.L > kMaxLayers) SG_DIE("megakernel: too many layers");
   int buf = buffer_bytes(smem, a.D, a.QHl * a.HD, a.Fl, a.HD, a.G);
   if (buf < 8 * 1024 || buf % 16) SG_DIE("megakernel: weight buffers too small");
-  // The barrier counter restarts at zero for every launch.
-  SG_CUDA(cudaMemsetAsync(a.bar, 0, 2 * sizeof(unsigned), s));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);

@@ -1,6 +1,8 @@
 // Persistent decode megakernel: one cooperative launch runs `steps` greedy
 // decode steps of a dense model (all layers, LM head and argmax), one CTA per
-// SM, phases separated by grid-wide barriers with bounded waits.
+// SM. Phases hand their outputs to the next phase through flagged vectors
+// (every element a 64-bit word: value bits and the step's epoch), so a
+// consumer waits for exactly the data it reads; there is no grid barrier.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -19,6 +21,18 @@ struct MegaLayer {
   const uint16_t* wd;     // [D][Fl]
 };
 
+// Offsets (in 64-bit words) of the flagged vectors inside MegaArgs::ll.
+struct MegaFlagged {
+  size_t x;    // [L][2][D]  residual after o_proj (0) and after down (1)
+  size_t qkv;  // [L][QKVl]
+  size_t att;  // [L][QHl*HD] merged attention output
+  size_t h;    // [L][Fl]     SwiGLU output
+  size_t am;   // [2][grid]   per-CTA argmax value / index
+  size_t total;
+};
+
+MegaFlagged mega_flagged_layout(int D, int QKVl, int QD, int Fl, int L, int grid);
+
 struct MegaArgs {
   int D, HD, QHl, KHl, G, Fl, Vl, L, QKVl, ctx;
   float eps;
@@ -28,33 +42,29 @@ struct MegaArgs {
   const uint16_t* out_w;    // [Vl][D]
   const float* rope;        // [ctx][HD]
   int pair_bound, pair_offset, pair_stride;
-  float* x;                 // [D] residual stream
-  float* qkv;               // [QKVl]
-  float* att;               // [QHl*HD]
-  float* h;                 // [Fl]
   float* logits;            // [Vl]
   float* kc;                // [L][KHl][ctx][HD]
   float* vc;
-  float* attn_partial;      // [QHl][nsplit][HD+2]
-  int* attn_ticket;         // [KHl], zero at rest
+  float* attn_partial;      // [L][QHl][nsplit][HD+4]
+  int* attn_ticket;         // [L][KHl], zero at rest
   int nsplit, split_len;
-  float* am_val;            // [gridDim] argmax partials
-  int* am_idx;
+  unsigned long long* ll;   // flagged vectors (layout: MegaFlagged)
+  MegaFlagged llo;
+  unsigned epoch;           // epoch of the first step; step s uses epoch + s
   int* tok;                 // in: token of the first step; out: last argmax
   int* pos;                 // in/out: position of the next token
   int* step;                // in/out: index into gen
   int* gen;                 // generated tokens
   int gen_len;              // capacity of gen: writes at step >= gen_len are dropped
-  unsigned* bar;            // [2] barrier count / generation, zero at rest
-  int* err;                 // set non-zero when a barrier wait times out
+  int* err;                 // set non-zero when a wait times out
   int steps;
   int write_logits;
-  // Optional (null = off): per barrier and CTA, kMegaTraceWidth %globaltimer
-  // stamps [barrier][cta][w]: arrival, release, input staged, first weight
-  // chunk ready, phase consumed, last chunk computed, next copy issued; for
-  // the first `trace_barriers` barriers.
+  // Optional (null = off): per phase and CTA, kMegaTraceWidth %globaltimer
+  // stamps [phase][cta][w]: stage start, inputs complete, input staged,
+  // first weight chunk ready, phase consumed, last chunk computed, next copy
+  // issued; for the first `trace_phases` phases of the launch.
   unsigned long long* trace;
-  int trace_barriers;
+  int trace_phases;
 };
 
 constexpr int kMegaTraceWidth = 7;
@@ -63,7 +73,7 @@ constexpr int kMegaTraceWidth = 7;
 size_t mega_smem_bytes(int D, int QD, int Fl, int HD, int G);
 // Largest grid that is co-resident (one CTA per SM); 0 if not launchable.
 int mega_grid(size_t smem, int HD, int G);
-// Decode split used by the megakernel (split_len a multiple of 128).
+// Decode split used by the megakernel (split_len a multiple of 64).
 void mega_split(int ctx, int KHl, int grid, int* nsplit, int* split_len);
 void mega_configure(size_t smem);
 void mega_decode(const MegaArgs& a, int grid, size_t smem, cudaStream_t s);

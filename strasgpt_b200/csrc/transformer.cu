@@ -120,10 +120,12 @@ struct transformer_state {
   int mega_grid = 0, mega_nsplit = 1, mega_split_len = 1;
   size_t mega_smem = 0;
   sg::MegaLayer* mega_layers = nullptr;  // device [L]
-  unsigned* bar = nullptr;               // [2]
+  unsigned long long* mega_ll = nullptr; // flagged hand-off vectors
+  sg::MegaFlagged mega_llo{};
+  unsigned mega_epoch = 1;               // epoch of the next launch's first step
   int* err = nullptr;
   unsigned long long* trace = nullptr;   // STRASGPT_MEGA_TRACE=<file>
-  int trace_barriers = 0;
+  int trace_phases = 0;
   // Tensor-core prefill projections: bf16 halves of the current projection
   // input ([chunk_max][K]) with their TMA maps for K = D, QH*HD, F; weight
   // maps per layer (qkv, o, gate/up, down), then the LM head.
@@ -571,21 +573,28 @@ void alloc_state(const W_t* w, const transformer_configuration_t* c, S_t* s) {
     s->mega_layers = (sg::MegaLayer*)dalloc(s->allocs, sizeof(sg::MegaLayer) * w->L, nullptr);
     SG_CUDA(cudaMemcpy(s->mega_layers, ml.data(), sizeof(sg::MegaLayer) * w->L,
                        cudaMemcpyHostToDevice));
-    s->bar = (unsigned*)I32(2);
     s->err = I32(1);
     if (getenv("STRASGPT_MEGA_TRACE")) {
-      // Barrier timestamps of the first two decode steps of a launch.
-      s->trace_barriers = 2 * (5 * w->L + 1);
-      const size_t n = (size_t)s->trace_barriers * s->mega_grid * sg::kMegaTraceWidth;
+      // Phase timestamps of the first two decode steps of a launch.
+      s->trace_phases = 2 * (5 * w->L + 1);
+      const size_t n = (size_t)s->trace_phases * s->mega_grid * sg::kMegaTraceWidth;
       s->trace = (unsigned long long*)dalloc(s->allocs, n * 8, nullptr);
       SG_CUDA(cudaMemset(s->trace, 0, n * 8));
     }
-    SG_CUDA(cudaMemset(s->bar, 0, 8));
     SG_CUDA(cudaMemset(s->err, 0, 4));
+    // Flagged hand-off vectors, zero (epoch 0: never written) at rest.
+    s->mega_llo = sg::mega_flagged_layout(w->D, w->QKVl, w->QHl * w->HD, w->Fl, w->L,
+                                          s->mega_grid);
+    s->mega_ll = (unsigned long long*)dalloc(s->allocs, s->mega_llo.total * 8, nullptr);
+    SG_CUDA(cudaMemset(s->mega_ll, 0, s->mega_llo.total * 8));
+    s->mega_epoch = 1;
   }
-  s->attn_partial = F32((size_t)w->QHl * max_split * (HD + 4));
-  s->attn_ticket = I32(w->KHl);
-  SG_CUDA(cudaMemset(s->attn_ticket, 0, w->KHl * 4));
+  // Split records and tickets: one set for the per-op decode kernel, one
+  // per layer for the persistent kernel.
+  const size_t layers_of_records = s->use_mega ? (size_t)w->L : 1;
+  s->attn_partial = F32(layers_of_records * w->QHl * max_split * (HD + 4));
+  s->attn_ticket = I32(layers_of_records * w->KHl);
+  SG_CUDA(cudaMemset(s->attn_ticket, 0, layers_of_records * w->KHl * 4));
   s->am_val = F32(1024);
   s->am_idx = I32(1024);
   s->am_ticket = I32(1);
@@ -784,18 +793,26 @@ struct Runner {
     a.pair_bound = (int)c->rope_pair_bound;
     a.pair_offset = (int)c->rope_pair_offset;
     a.pair_stride = (int)c->rope_pair_stride;
-    a.x = s->x; a.qkv = s->qkv; a.att = s->att; a.h = s->h; a.logits = s->logits;
+    a.logits = s->logits;
     a.kc = s->kc; a.vc = s->vc;
     a.attn_partial = s->attn_partial; a.attn_ticket = s->attn_ticket;
     a.nsplit = s->mega_nsplit; a.split_len = s->mega_split_len;
-    a.am_val = s->am_val; a.am_idx = s->am_idx;
+    a.ll = s->mega_ll; a.llo = s->mega_llo; a.epoch = s->mega_epoch;
     a.tok = s->tok; a.pos = s->pos; a.step = s->step; a.gen = s->gen;
     a.gen_len = s->ctx + 1;
-    a.bar = s->bar; a.err = s->err;
+    a.err = s->err;
     a.steps = steps; a.write_logits = write_logits ? 1 : 0;
-    a.trace = s->trace; a.trace_barriers = s->trace_barriers;
+    a.trace = s->trace; a.trace_phases = s->trace_phases;
+    if (s->trace)
+      SG_CUDA(cudaMemsetAsync(s->trace, 0,
+                              (size_t)s->trace_phases * s->mega_grid * sg::kMegaTraceWidth * 8,
+                              st));
     s->launches++;
     sg::mega_decode(a, s->mega_grid, s->mega_smem, st);
+    // Every step of a launch has its own epoch; the next launch starts
+    // after them (a CUDA graph would freeze this value, so the kernel is
+    // launched directly, never captured).
+    s->mega_epoch += (unsigned)steps;
   }
 
   // Chunk projection C[t] (op)= W a[t] for t < T: on the tensor cores when
@@ -918,14 +935,14 @@ void check_device_errors(S_t* s) {
   if (!s->use_mega) return;
   int err = 0;
   SG_CUDA(cudaMemcpy(&err, s->err, sizeof(int), cudaMemcpyDeviceToHost));
-  if (err) SG_DIE("decode megakernel: a grid barrier or weight copy wait timed out");
+  if (err) SG_DIE("decode megakernel: an input or weight copy wait timed out");
   if (s->trace) {
-    const size_t n = (size_t)s->trace_barriers * s->mega_grid * sg::kMegaTraceWidth;
+    const size_t n = (size_t)s->trace_phases * s->mega_grid * sg::kMegaTraceWidth;
     std::vector<unsigned long long> h(n);
     SG_CUDA(cudaMemcpy(h.data(), s->trace, n * 8, cudaMemcpyDeviceToHost));
     FILE* f = fopen(getenv("STRASGPT_MEGA_TRACE"), "wb");
     if (f) {
-      const int hdr[3] = {s->trace_barriers, s->mega_grid, sg::kMegaTraceWidth};
+      const int hdr[3] = {s->trace_phases, s->mega_grid, sg::kMegaTraceWidth};
       fwrite(hdr, sizeof(hdr), 1, f);
       fwrite(h.data(), 8, n, f);
       fclose(f);

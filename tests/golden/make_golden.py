@@ -76,7 +76,11 @@ def make(name: str) -> None:
     checker = oracle.Restatement if cfg.experts else oracle.Reference
     t0 = time.time()
     m = checker(d)
-    toks, logits = m.generate_greedy(prompt, cfg.steps)
+    gaps = [] if cfg.experts else None
+    if cfg.experts:
+        toks, logits = m.generate_greedy(prompt, cfg.steps, gaps=gaps)
+    else:
+        toks, logits = m.generate_greedy(prompt, cfg.steps)
     dt = time.time() - t0
     sha = file_sha256(os.path.join(d, "model.safetensors"))
     meta = {"config": name, "seed": 0, "checker": checker.__name__,
@@ -91,6 +95,11 @@ def make(name: str) -> None:
     else:
         proj = projection_vectors(cfg.vocab)
         meta["steps"] = [step_summary(l, proj) for l in logits]
+        if gaps is not None:
+            # Smallest top-k router margin over the layers (and, for the
+            # prompt, its tokens) of each step.
+            for st, g in zip(meta["steps"], gaps):
+                st["router_gap"] = g
         with open(os.path.join(HERE, f"{name}.json"), "w") as f:
             json.dump(meta, f)
     print(f"{name}: {checker.__name__} {dt:.1f}s tokens {toks[:8]}...", flush=True)

@@ -9,7 +9,16 @@ equal the reference's bit for bit; and for every step of the predict path
 (host logits, as strasgpt.c reads them) the logits of the reference's
 top-16 ids, the maximum, mean and standard deviation must be within the
 north-star max-abs bound 1e-2 (a size-independent stand-in for the
-full logits, which are 0.5-0.8 MB per step)."""
+full logits, which are 0.5-0.8 MB per step).
+
+MoE (C4): a top-k router choice whose k-th and (k+1)-th router logits lie
+within ROUTER_TIE of each other depends on the fp32 summation order (the
+two implementations agree to ~1e-6 on router logits), so a step whose
+smallest router margin (recorded by the restatement, `router_gap`) is
+below ROUTER_TIE is numerically undecidable: its logits are not compared,
+and the greedy ids are compared up to that step (later ids follow from a
+different token). In the committed C4 fixture this is step 57 (margin
+3.1e-5), where the GPU indeed picks another expert."""
 import hashlib
 import json
 import os
@@ -22,6 +31,7 @@ from strasgpt_b200 import configs, synth
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 MAX_ABS = 1e-2
+ROUTER_TIE = 1e-4
 NAMES = [n for n in ("c1_llama1b", "c2_qwen3_0p6b", "c4_moe_mxfp4", "c3_llama8b")
          if os.path.exists(os.path.join(GOLDEN, f"{n}.json"))]
 
@@ -46,15 +56,22 @@ def test_full_size_matches_reference(cuda, name):
     assert _sha256(os.path.join(d, "model.safetensors")) == meta["model_sha256"]
     prompt = synth.prompt_tokens(cfg)
     assert [int(x) for x in prompt] == meta["prompt"]
+    # Decode steps only: the prompt's margin is the minimum over all of its
+    # tokens, where a flipped choice moves one cache row, not the output.
+    ties = [s for s, st in enumerate(meta["steps"])
+            if s > 0 and st.get("router_gap", 1.0) < ROUTER_TIE]
+    upto = ties[0] if ties else len(meta["tokens"])
     m = Transformer(d)
     toks, _ = m.generate_greedy(prompt, cfg.steps)
-    assert [int(t) for t in toks] == meta["tokens"], f"{name}: greedy ids differ"
+    assert [int(t) for t in toks][:upto] == meta["tokens"][:upto], f"{name}: greedy ids differ"
     m.reset()
     logits = m.predict(prompt, 1)[0]
     worst = 0.0
     for s, want in enumerate(meta["steps"]):
         if s > 0:
             logits = m.predict([meta["tokens"][s - 1]], 1)[0]
+        if s in ties:
+            continue
         got = logits.astype(np.float64)
         ids = want["top_ids"]
         errs = [abs(got[i] - v) for i, v in zip(ids, want["top_vals"])]
