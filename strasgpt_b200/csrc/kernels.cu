@@ -1114,18 +1114,297 @@ __global__ void __launch_bounds__(256) k_moe_down(MoeArgs a) {
   }
 }
 
+// ---- one-token expert matvecs -------------------------------------------
+// A warp covers 8 MXFP4 blocks of a row per pass: lane l reads the 4 code
+// bytes [4 (l % 4), +4) of block (l / 4), i.e. 8 consecutive codes, so the
+// warp's code loads are one coalesced 128-byte line and its activation loads
+// (2 float4 per lane) one contiguous 1 KB run. Codes are decoded a byte at a
+// time through a 256-entry table of value pairs in shared memory (low
+// nibble = even element); the block scale multiplies each lane's 8-term
+// partial sum.
+__device__ __forceinline__ float mxfp4_dot8(uint32_t codes, const float2* pair_lut,
+                                            float4 xa, float4 xb) {
+  const float2 p0 = pair_lut[codes & 0xFF];
+  const float2 p1 = pair_lut[(codes >> 8) & 0xFF];
+  const float2 p2 = pair_lut[(codes >> 16) & 0xFF];
+  const float2 p3 = pair_lut[codes >> 24];
+  float s = p0.x * xa.x;
+  s = fmaf(p0.y, xa.y, s);
+  s = fmaf(p1.x, xa.z, s);
+  s = fmaf(p1.y, xa.w, s);
+  s = fmaf(p2.x, xb.x, s);
+  s = fmaf(p2.y, xb.y, s);
+  s = fmaf(p3.x, xb.z, s);
+  s = fmaf(p3.y, xb.w, s);
+  return s;
+}
+
+__device__ __forceinline__ void fill_pair_lut(float2* pair_lut) {
+  for (int i = threadIdx.x; i < 256; i += blockDim.x)
+    pair_lut[i] = make_float2(kE2M1[i & 0xF], kE2M1[i >> 4]);
+}
+
+// Dot of one MXFP4 row (nb blocks: codes [nb][16] bytes, scales [nb]) with
+// xs[nb * 32] (shared memory), reduced over the warp.
+// All of a lane's code and scale loads for up to kRowPasses passes are
+// issued before any is used, so a row costs one memory latency, not one per
+// pass.
+constexpr int kRowPasses = 16;
+
+__device__ __forceinline__ float mxfp4_row_dot(const uint8_t* __restrict__ codes,
+                                               const uint8_t* __restrict__ scales, int nb,
+                                               const float* xs, const float2* pair_lut) {
+  const int lane = threadIdx.x & 31;
+  const int bl = lane >> 2, q = lane & 3;
+  float acc = 0.f;
+  for (int b0 = 0; b0 < nb; b0 += 8 * kRowPasses) {
+    uint32_t c[kRowPasses];
+    uint32_t sc[kRowPasses];
+#pragma unroll
+    for (int p = 0; p < kRowPasses; p++) {
+      const int b = b0 + 8 * p + bl;
+      c[p] = (b < nb) ? __ldg(reinterpret_cast<const uint32_t*>(codes + (size_t)b * 16) + q) : 0u;
+      sc[p] = (b < nb) ? __ldg(scales + b) : 0u;
+    }
+#pragma unroll
+    for (int p = 0; p < kRowPasses; p++) {
+      const int b = b0 + 8 * p + bl;
+      if (b < nb) {
+        const float4* xv = reinterpret_cast<const float4*>(xs + b * 32 + q * 8);
+        acc = fmaf(mxfp4_dot8(c[p], pair_lut, xv[0], xv[1]), e8m0_scale(sc[p]), acc);
+      }
+    }
+  }
+  return warp_sum(acc);
+}
+
+// gate/up for one token: grid (k slots, F / 16); 8 warps x 2 outputs.
+__global__ void __launch_bounds__(256) k_moe_gate_up_tok(MoeArgs a) {
+  extern __shared__ float4 sm4[];
+  float* xs = reinterpret_cast<float*>(sm4);                   // [D]
+  float2* pair_lut = reinterpret_cast<float2*>(xs + a.D);      // [256]
+  pdl_trigger();
+  pdl_wait();
+  const int j = blockIdx.x;  // slot of token 0
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e = a.idx[j];
+  const int f0 = blockIdx.y * 16;
+  float* h = a.h + (size_t)j * a.F;
+  if (e < a.e_begin || e >= a.e_end) {
+    if (threadIdx.x < 16 && f0 + threadIdx.x < a.F) h[f0 + threadIdx.x] = 0.f;
+    return;
+  }
+  fill_pair_lut(pair_lut);
+  for (int k = threadIdx.x * 4; k < a.D; k += blockDim.x * 4)
+    *reinterpret_cast<float4*>(xs + k) = *reinterpret_cast<const float4*>(a.xn + k);
+  __syncthreads();
+  const int nb = a.D / 32;
+  const size_t el = (size_t)(e - a.e_begin);
+#pragma unroll
+  for (int i = 0; i < 2; i++) {
+    const int f = f0 + warp * 2 + i;
+    if (f >= a.F) break;
+    const size_t row = el * a.F + f;
+    const float g = mxfp4_row_dot(a.gate_codes + row * nb * 16, a.gate_scales + row * nb, nb,
+                                  xs, pair_lut);
+    const float u = mxfp4_row_dot(a.up_codes + row * nb * 16, a.up_scales + row * nb, nb, xs,
+                                  pair_lut);
+    if (lane == 0) h[f] = swiglu(g, u);
+  }
+}
+
+// down for one token: grid (D / 16); 8 warps x 2 outputs, summed over the
+// k selected experts with their router weights.
+__global__ void __launch_bounds__(256) k_moe_down_tok(MoeArgs a) {
+  extern __shared__ float4 sm4[];
+  float* hs = reinterpret_cast<float*>(sm4);                      // [k][F]
+  float2* pair_lut = reinterpret_cast<float2*>(hs + a.k * a.F);   // [256]
+  pdl_trigger();
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  fill_pair_lut(pair_lut);
+  for (int i = threadIdx.x * 4; i < a.k * a.F; i += blockDim.x * 4)
+    *reinterpret_cast<float4*>(hs + i) = *reinterpret_cast<const float4*>(a.h + i);
+  __syncthreads();
+  const int nb = a.F / 32;
+#pragma unroll
+  for (int i = 0; i < 2; i++) {
+    const int r = blockIdx.x * 16 + warp * 2 + i;
+    if (r >= a.D) break;
+    float y = 0.f;
+    for (int j = 0; j < a.k; j++) {
+      const int e = a.idx[j];
+      if (e < a.e_begin || e >= a.e_end) continue;
+      const size_t row = (size_t)(e - a.e_begin) * a.D + r;
+      const float d = mxfp4_row_dot(a.down_codes + row * nb * 16, a.down_scales + row * nb, nb,
+                                    hs + (size_t)j * a.F, pair_lut);
+      y = fmaf(a.weight[j], d, y);
+    }
+    if (lane == 0) a.out[r] += y;
+  }
+}
+
 void moe_gate_up(const MoeArgs& a, cudaStream_t s) {
   if (a.D % 32 || a.F % 32) SG_DIE("moe: dims must be multiples of 32");
+  if (a.T == 1) {
+    const size_t smem = (size_t)a.D * 4 + 256 * 8;
+    launch(k_moe_gate_up_tok, dim3(a.k, (a.F + 15) / 16), dim3(256), smem, s, a);
+    return;
+  }
   const size_t smem = (size_t)pad32(a.D) * 4;
   dim3 grid(a.T * a.k, (a.F + 63) / 64);
   launch(k_moe_gate_up, grid, dim3(256), smem, s, a);
 }
 
 void moe_down(const MoeArgs& a, cudaStream_t s) {
+  if (a.T == 1) {
+    const size_t smem = (size_t)a.k * a.F * 4 + 256 * 8;
+    if (smem > 200 * 1024) SG_DIE("moe_down: k * F too large");
+    launch(k_moe_down_tok, dim3((a.D + 15) / 16), dim3(256), smem, s, a);
+    return;
+  }
   const size_t smem = (size_t)a.k * pad32(a.F) * 4;
   if (smem > 200 * 1024) SG_DIE("moe_down: k * F too large");
   dim3 grid(a.T, (a.D + 63) / 64);
   launch(k_moe_down, grid, dim3(256), smem, s, a);
+}
+
+// ---- grouped experts for multi-token chunks -------------------------------
+// One CTA: counting sort of the slots by expert in shared memory.
+__global__ void __launch_bounds__(1024)
+    k_moe_group(const int* __restrict__ idx, int slots, int E, int* __restrict__ counts,
+                int* __restrict__ offsets, int* __restrict__ perm, int* __restrict__ inv) {
+  __shared__ int cnt[256], cur[256];
+  pdl_trigger();
+  pdl_wait();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  for (int s = threadIdx.x; s < slots; s += blockDim.x) atomicAdd(&cnt[idx[s]], 1);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int run = 0;
+    for (int e = 0; e < E; e++) {
+      counts[e] = cnt[e];
+      offsets[e] = run;
+      cur[e] = run;
+      run += cnt[e];
+    }
+  }
+  __syncthreads();
+  for (int s = threadIdx.x; s < slots; s += blockDim.x) {
+    const int pos = atomicAdd(&cur[idx[s]], 1);
+    perm[pos] = s;
+    inv[s] = pos;
+  }
+}
+
+void moe_group(const int* idx, int slots, int E, int* counts, int* offsets, int* perm, int* inv,
+               cudaStream_t s) {
+  if (E > 256) SG_DIE("moe_group: more than 256 experts");
+  launch(k_moe_group, dim3(1), dim3(1024), 0, s, idx, slots, E, counts, offsets, perm, inv);
+}
+
+__device__ __forceinline__ uint16_t f32_to_bf16_rne(float f) {
+  uint32_t u = __float_as_uint(f);
+  if ((u & 0x7F800000u) == 0x7F800000u) return (uint16_t)((u >> 16) | ((u & 0xFFFF) ? 0x40 : 0));
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+
+// Four activations per thread (D % 4 == 0).
+__global__ void k_moe_gather_split(const float* __restrict__ xn, int D, const int* __restrict__ perm,
+                                   int k, int n, uint16_t* __restrict__ hi,
+                                   uint16_t* __restrict__ lo) {
+  pdl_trigger();
+  pdl_wait();
+  const int dq = D >> 2;
+  const size_t total = (size_t)n * dq;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int r = (int)(i / dq), d = (int)(i % dq) * 4;
+    const int t = perm[r] / k;
+    const float4 v = *reinterpret_cast<const float4*>(xn + (size_t)t * D + d);
+    const float f[4] = {v.x, v.y, v.z, v.w};
+    uint16_t h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      h[j] = f32_to_bf16_rne(f[j]);
+      l[j] = f32_to_bf16_rne(f[j] - __uint_as_float((uint32_t)h[j] << 16));
+    }
+    const size_t o = (size_t)r * D + d;
+    *reinterpret_cast<uint2*>(hi + o) =
+        make_uint2(h[0] | ((uint32_t)h[1] << 16), h[2] | ((uint32_t)h[3] << 16));
+    *reinterpret_cast<uint2*>(lo + o) =
+        make_uint2(l[0] | ((uint32_t)l[1] << 16), l[2] | ((uint32_t)l[3] << 16));
+  }
+}
+
+void moe_gather_split(const float* xn, int D, const int* perm, int k, int n, uint16_t* hi,
+                      uint16_t* lo, cudaStream_t s) {
+  if (D % 4) SG_DIE("moe_gather_split: D must be a multiple of 4");
+  if (n <= 0) return;
+  size_t blocks = ((size_t)n * (D / 4) + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  launch(k_moe_gather_split, dim3((unsigned)blocks), dim3(256), 0, s, xn, D, perm, k, n, hi, lo);
+}
+
+// One code byte (two values) per thread; bf16 of e2m1 * 2^(e - 127) is the
+// top half of its fp32 bits (at most 2 mantissa bits).
+__global__ void k_mxfp4_to_bf16(const uint8_t* __restrict__ codes,
+                                const uint8_t* __restrict__ scales, int rows, int K,
+                                uint16_t* __restrict__ out, int row_stride, int row_offset) {
+  pdl_trigger();
+  pdl_wait();
+  const int kb = K / 2;  // bytes per row
+  const size_t total = (size_t)rows * kb;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int r = (int)(i / kb), byte = (int)(i % kb);
+    const uint32_t c = codes[i];
+    const float sc = e8m0_scale(scales[(size_t)r * (K / 32) + byte / 16]);
+    const float v0 = kE2M1[c & 0xF] * sc, v1 = kE2M1[c >> 4] * sc;
+    const uint32_t packed = (__float_as_uint(v0) >> 16) | (__float_as_uint(v1) & 0xFFFF0000u);
+    *reinterpret_cast<uint32_t*>(out + ((size_t)r * row_stride + row_offset) * K + 2 * byte) =
+        packed;
+  }
+}
+
+void mxfp4_to_bf16(const uint8_t* codes, const uint8_t* scales, int rows, int K, uint16_t* out,
+                   int row_stride, int row_offset, cudaStream_t s) {
+  if (K % 32) SG_DIE("mxfp4_to_bf16: K must be a multiple of 32");
+  size_t blocks = ((size_t)rows * (K / 2) + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  launch(k_mxfp4_to_bf16, dim3((unsigned)blocks), dim3(256), 0, s, codes, scales, rows, K, out,
+         row_stride, row_offset);
+}
+
+__global__ void k_moe_combine(float* __restrict__ out, const float* __restrict__ weight,
+                              const int* __restrict__ idx, const int* __restrict__ inv,
+                              const float* __restrict__ y, int T, int k, int D, int e_begin,
+                              int e_end) {
+  pdl_trigger();
+  pdl_wait();
+  const size_t total = (size_t)T * D;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int t = (int)(i / D), d = (int)(i % D);
+    float acc = 0.f;
+    for (int j = 0; j < k; j++) {
+      const int slot = t * k + j;
+      const int e = idx[slot];
+      if (e < e_begin || e >= e_end) continue;
+      acc = fmaf(weight[slot], y[(size_t)inv[slot] * D + d], acc);
+    }
+    out[i] += acc;
+  }
+}
+
+void moe_combine(float* out, const float* weight, const int* idx, const int* inv, const float* y,
+                 int T, int k, int D, int e_begin, int e_end, cudaStream_t s) {
+  size_t blocks = ((size_t)T * D + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  launch(k_moe_combine, dim3((unsigned)blocks), dim3(256), 0, s, out, weight, idx, inv, y, T, k,
+         D, e_begin, e_end);
 }
 
 // Busy-wait for a bounded number of SM cycles (always terminates). Used by
@@ -1157,6 +1436,8 @@ void configure_kernels() {
   SG_SMEM(k_attn_prefill<32>);
   SG_SMEM(k_attn_prefill<64>);
   SG_SMEM(k_attn_prefill<128>);
+  SG_SMEM(k_moe_gate_up_tok);
+  SG_SMEM(k_moe_down_tok);
   SG_SMEM(k_moe_gate_up);
   SG_SMEM(k_moe_down);
 #undef SG_SMEM

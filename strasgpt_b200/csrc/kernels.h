@@ -116,6 +116,27 @@ void moe_gate_up(const MoeArgs& a, cudaStream_t s);
 // out[t][r] += sum_j weight[t][j] * (down_e[r] . h[t][j])
 void moe_down(const MoeArgs& a, cudaStream_t s);
 
+// --- Grouped experts for multi-token chunks ------------------------------
+// Groups the `slots` = T*k (token, choice) slots by expert: counts[E],
+// offsets[E] (exclusive prefix), perm[pos] = slot index with the slots of
+// expert e at positions [offsets[e], offsets[e] + counts[e]), and
+// inv[slot] = pos. The order inside an expert is unspecified (every row of
+// an expert's product is computed independently of its position).
+void moe_group(const int* idx, int slots, int E, int* counts, int* offsets, int* perm, int* inv,
+               cudaStream_t s);
+// bf16 halves (hi, lo as in tc_split) of the rows xn[perm[r] / k] for r < n.
+void moe_gather_split(const float* xn, int D, const int* perm, int k, int n, uint16_t* hi,
+                      uint16_t* lo, cudaStream_t s);
+// bf16 rows from MXFP4 rows (codes [rows][K/32][16], scales [rows][K/32]):
+// source row r goes to out row r * row_stride + row_offset ([*][K]); the
+// values e2m1 * 2^(e8m0 - 127) are exact in bf16.
+void mxfp4_to_bf16(const uint8_t* codes, const uint8_t* scales, int rows, int K, uint16_t* out,
+                   int row_stride, int row_offset, cudaStream_t s);
+// out[t][d] += sum over j (in order) of weight[t][j] * y[inv[t*k+j]][d], for
+// the slots whose expert is in [e_begin, e_end).
+void moe_combine(float* out, const float* weight, const int* idx, const int* inv, const float* y,
+                 int T, int k, int D, int e_begin, int e_end, cudaStream_t s);
+
 }  // namespace sg
 
 namespace sg {

@@ -134,6 +134,14 @@ struct transformer_state {
   sg::TcAct in[3];
   std::vector<sg::TcMap> tc_w;
   int* tc_err = nullptr;
+  // MoE chunks on the tensor cores: one expert at a time, its MXFP4
+  // gate/up and down dequantised to bf16 scratch (gate/up interleaved), the
+  // expert's tokens gathered, two projections, then a weighted combine of
+  // the per-slot outputs moe_y [T*k][D].
+  uint16_t *moe_wgu = nullptr, *moe_wd = nullptr;
+  float* moe_y = nullptr;
+  int *moe_counts = nullptr, *moe_offsets = nullptr, *moe_perm = nullptr, *moe_inv = nullptr;
+  int* h_moe_counts = nullptr;  // pinned [E]
   size_t launches = 0;        // kernels enqueued (graph nodes at capture)
   size_t graph_nodes = 0;     // kernels in one greedy-graph replay
   strasgpt_kernel_profile_t* prof = nullptr;
@@ -609,12 +617,27 @@ void alloc_state(const W_t* w, const transformer_configuration_t* c, S_t* s) {
               (w->moe || w->Fl % 8 == 0);
   if (s->use_tc) {
     sg::tc_configure();
-    const int ks[3] = {w->D, QD, w->moe ? w->D : w->Fl};
+    // K of the three projection inputs: D, QH*HD, and F (this rank's FFN
+    // rows; a whole expert's F for MoE).
+    const int ks[3] = {w->D, QD, w->Fl};
     const size_t kmax = (size_t)std::max(ks[0], std::max(ks[1], ks[2]));
     s->a_hi = (uint16_t*)dalloc(s->allocs, T * kmax * 2, nullptr);
     s->a_lo = (uint16_t*)dalloc(s->allocs, T * kmax * 2, nullptr);
     for (int i = 0; i < 3; i++) sg::tc_make_act(&s->in[i], s->a_hi, s->a_lo, (int)T, ks[i]);
-    s->tc_w.resize((size_t)4 * w->L + 1);
+    s->tc_w.resize((size_t)4 * w->L + 3);
+    if (w->moe) {
+      const size_t F = w->F;
+      s->moe_wgu = (uint16_t*)dalloc(s->allocs, 2 * F * D * 2, nullptr);
+      s->moe_wd = (uint16_t*)dalloc(s->allocs, D * F * 2, nullptr);
+      s->moe_y = F32(T * w->topk * D);
+      s->moe_counts = I32(w->E);
+      s->moe_offsets = I32(w->E);
+      s->moe_perm = I32(T * w->topk);
+      s->moe_inv = I32(T * w->topk);
+      SG_CUDA(cudaMallocHost(&s->h_moe_counts, (size_t)w->E * sizeof(int)));
+      sg::tc_make_map(&s->tc_w[4 * w->L + 1], s->moe_wgu, 2 * w->F, w->D);
+      sg::tc_make_map(&s->tc_w[4 * w->L + 2], s->moe_wd, w->D, w->F);
+    }
     for (int l = 0; l < w->L; l++) {
       const Layer& y = w->layer[l];
       sg::tc_make_map(&s->tc_w[4 * l + 0], y.wqkv, w->QKVl, w->D);
@@ -830,6 +853,58 @@ struct Runner {
     }
   }
 
+  // MoE FFN of a chunk on the tensor cores, expert by expert (this rank's
+  // experts). The tokens routed to each expert are known on the host after
+  // one small read-back of the per-expert counts.
+  void moe_experts_tc(int l, int T) {
+    const Layer& ly = w->layer[l];
+    const int D = w->D, F = w->F, k = w->topk, E = w->E;
+    launch(FAM_OTHER, 0, [&] {
+      sg::moe_group(s->eidx, T * k, E, s->moe_counts, s->moe_offsets, s->moe_perm, s->moe_inv,
+                    st);
+    });
+    SG_CUDA(cudaMemcpyAsync(s->h_moe_counts, s->moe_counts, (size_t)E * sizeof(int),
+                            cudaMemcpyDeviceToHost, st));
+    SG_CUDA(cudaStreamSynchronize(st));
+    const size_t gu_codes = (size_t)F * (D / 32) * 16, gu_scales = (size_t)F * (D / 32);
+    const size_t d_codes = (size_t)D * (F / 32) * 16, d_scales = (size_t)D * (F / 32);
+    int off = 0;
+    for (int e = 0; e < E; e++) {
+      const int n = s->h_moe_counts[e];
+      if (n > 0 && e >= w->e_begin && e < w->e_end) {
+        const size_t el = (size_t)(e - w->e_begin);
+        launch(FAM_OTHER, 0, [&] {
+          sg::mxfp4_to_bf16(ly.gate_c + el * gu_codes, ly.gate_s + el * gu_scales, F, D,
+                            s->moe_wgu, 2, 0, st);
+        });
+        launch(FAM_OTHER, 0, [&] {
+          sg::mxfp4_to_bf16(ly.up_c + el * gu_codes, ly.up_s + el * gu_scales, F, D, s->moe_wgu,
+                            2, 1, st);
+        });
+        launch(FAM_OTHER, 0, [&] {
+          sg::mxfp4_to_bf16(ly.down_c + el * d_codes, ly.down_s + el * d_scales, D, F,
+                            s->moe_wd, 1, 0, st);
+        });
+        launch(FAM_OTHER, 0, [&] {
+          sg::moe_gather_split(s->xn, D, s->moe_perm + off, k, n, s->a_hi, s->a_lo, st);
+        });
+        launch(FAM_OTHER, 0, [&] {
+          sg::tc_gemm(s->tc_w[4 * w->L + 1], s->in[0], n, s->h, F, sg::EPI_SWIGLU, s->tc_err, st);
+        });
+        launch(FAM_OTHER, 0, [&] { sg::tc_split(s->h, F, n, F, s->a_hi, s->a_lo, st); });
+        launch(FAM_OTHER, 0, [&] {
+          sg::tc_gemm(s->tc_w[4 * w->L + 2], s->in[2], n, s->moe_y + (size_t)off * D, D,
+                      sg::EPI_STORE, s->tc_err, st);
+        });
+      }
+      off += n;
+    }
+    launch(FAM_OTHER, 0, [&] {
+      sg::moe_combine(rp_out(), s->ew, s->eidx, s->moe_inv, s->moe_y, T, k, D, w->e_begin,
+                      w->e_end, st);
+    });
+  }
+
   // T > 1 tokens already in s->tok at host-known position pos0.
   void prefill_layers(int T, int pos0) {
     const int D = w->D, HD = w->HD, QD = w->QHl * HD;
@@ -850,10 +925,14 @@ struct Runner {
       if (w->moe) {
         launch(FAM_OTHER, 0, [&] { sg::gemm_simt(s->xn, D, ly.router, D, T, w->E, s->rl, w->E, sg::EPI_STORE, st); });
         launch(FAM_OTHER, 0, [&] { sg::moe_topk(s->rl, T, w->E, w->topk, s->eidx, s->ew, st); });
-        sg::MoeArgs m = moe_args(l, T);
         moe_zero_part(T);
-        launch(FAM_OTHER, 0, [&] { sg::moe_gate_up(m, st); });
-        launch(FAM_OTHER, 0, [&] { sg::moe_down(m, st); });
+        if (s->use_tc) {
+          moe_experts_tc(l, T);
+        } else {
+          sg::MoeArgs m = moe_args(l, T);
+          launch(FAM_OTHER, 0, [&] { sg::moe_gate_up(m, st); });
+          launch(FAM_OTHER, 0, [&] { sg::moe_down(m, st); });
+        }
       } else {
         proj(s->xn, D, 0, ly.wgu, 4 * l + 2, 2 * w->Fl, s->h, w->Fl, sg::EPI_SWIGLU, T);
         proj(s->h, w->Fl, 2, ly.wd, 4 * l + 3, D, rp_out(), D, rp_epi(), T);
@@ -1135,6 +1214,7 @@ void transformer_free(transformer_t* t) {
     for (auto e : s->ev)
       if (e) cudaEventDestroy(e);
     if (s->h_logits) cudaFreeHost(s->h_logits);
+    if (s->h_moe_counts) cudaFreeHost(s->h_moe_counts);
     for (auto e : s->prof_ev) cudaEventDestroy(e);
     if (s->tp.local) sg::tp_free(&s->tp, s->stream);
     if (s->stream) cudaStreamDestroy(s->stream);
