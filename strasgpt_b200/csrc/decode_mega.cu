@@ -27,8 +27,8 @@
 // Weight streaming. Each weight phase gives CTA c a contiguous slice of row
 // pairs, so a CTA's weights for the whole launch form a fixed list of
 // contiguous byte ranges ("chunks", at most one shared-memory buffer each).
-// kRing buffers per CTA: thread 0 issues the cp.async.bulk copy (no
-// multicast) of chunk g+kRing as soon as chunk g has been consumed, with
+// kRing buffers per CTA: thread 0 issues the cp.async.bulk copy (into its
+// own CTA's buffer only) of chunk g+kRing as soon as chunk g has been consumed, with
 // completion on the buffer's mbarrier. Weights never depend on activations,
 // so copies run ahead across phase and layer boundaries while a CTA waits
 // for its inputs. Attention CTAs prefetch their K/V rows into L2 during the
@@ -51,6 +51,7 @@ constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kPosPerPass = kWarps * 8;  // cache rows per CTA pass
 constexpr int kMaxSplits = 64;
+constexpr int kTpMaxWorld = 8;
 constexpr unsigned long long kTimeoutNs = 2000000000ULL;
 constexpr size_t kSmemBudget = 220 * 1024;  // dynamic shared memory per CTA
 
@@ -114,6 +115,17 @@ __device__ __forceinline__ u64 ll_load(const u64* p) {
   asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
   return w;
 }
+// System scope: words another GPU writes into this GPU's memory (or this
+// GPU writes into a peer's) over NVLink.
+__device__ __forceinline__ void ll_store_sys(u64* p, float v, unsigned e) {
+  const u64 w = ((u64)e << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ u64 ll_load_sys(const u64* p) {
+  u64 w;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
 __device__ __forceinline__ bool ll_ready(u64 w, unsigned e) { return (unsigned)(w >> 32) == e; }
 __device__ __forceinline__ float ll_value(u64 w) { return __uint_as_float((unsigned)w); }
 
@@ -138,14 +150,14 @@ __device__ __forceinline__ bool spin_on(const MegaArgs& a, Spin& s) {
 // Loads the flagged words src[k] for the N slots k = k0 + u * kstride
 // (slots with k >= K are skipped) and waits until all carry epoch e; the
 // values land in v[]. All loads of a round are issued before any is tested.
-template <int N>
+template <int N, bool SYS = false>
 __device__ __forceinline__ void ll_gather(const MegaArgs& a, const u64* src, int k0, int kstride,
                                           int K, unsigned e, float* v) {
   u64 w[N];
 #pragma unroll
   for (int u = 0; u < N; u++) {
     const int k = k0 + u * kstride;
-    w[u] = (k < K) ? ll_load(src + k) : ((u64)e << 32);
+    w[u] = (k < K) ? (SYS ? ll_load_sys(src + k) : ll_load(src + k)) : ((u64)e << 32);
   }
   unsigned pending = 0;
 #pragma unroll
@@ -156,7 +168,8 @@ __device__ __forceinline__ void ll_gather(const MegaArgs& a, const u64* src, int
     if (!spin_on(a, sp)) break;
 #pragma unroll
     for (int u = 0; u < N; u++)
-      if (pending & (1u << u)) w[u] = ll_load(src + k0 + u * kstride);
+      if (pending & (1u << u))
+        w[u] = SYS ? ll_load_sys(src + k0 + u * kstride) : ll_load(src + k0 + u * kstride);
 #pragma unroll
     for (int u = 0; u < N; u++)
       if ((pending & (1u << u)) && ll_ready(w[u], e)) pending &= ~(1u << u);
@@ -480,6 +493,8 @@ struct Out {
   u64* dst;            // flagged vector of the phase (null for the LM head)
   const float* xraw;   // residual input (O, DOWN)
   unsigned e;
+  size_t part;         // tensor parallel (O, DOWN): word offset of this rank's
+                       // partial rows in every rank's xpart vector
 };
 
 __device__ __forceinline__ void pair_epilogue(const MegaArgs& a, const Out& o, int kind, int pair,
@@ -492,8 +507,17 @@ __device__ __forceinline__ void pair_epilogue(const MegaArgs& a, const Out& o, i
       break;
     case W_O:
     case W_DOWN:
-      ll_store(o.dst + r0, o.xraw[r0] + y0, o.e);
-      ll_store(o.dst + r0 + 1, o.xraw[r0 + 1] + y1, o.e);
+      if (a.world > 1) {
+        // This rank's partial sums go to every rank; the owner of the rows
+        // adds them up in rank order (tp_reduce_rows).
+        for (int p = 0; p < a.world; p++) {
+          ll_store_sys(a.ll_peer[p] + o.part + r0, y0, o.e);
+          ll_store_sys(a.ll_peer[p] + o.part + r0 + 1, y1, o.e);
+        }
+      } else {
+        ll_store(o.dst + r0, o.xraw[r0] + y0, o.e);
+        ll_store(o.dst + r0 + 1, o.xraw[r0 + 1] + y1, o.e);
+      }
       break;
     case W_GU:
       ll_store(o.dst + pair, swiglu(y0, y1), o.e);
@@ -647,6 +671,22 @@ __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const float* x
   trace_mark(a, ph, MARK_CONSUMED);
   trace_put(a, ph, SUM_WAIT, t_wait);
   trace_put(a, ph, SUM_COMPUTE, t_comp);
+}
+
+// Tensor parallelism: rows [r0, r1) of the residual (this CTA's rows of the
+// o_proj / down phase) = xraw + the sum over ranks, in rank order, of the
+// partial rows every rank pushed into this rank's xpart vector at `part0`
+// (rank 0's slot; rank p's at part0 + p * D). Same inputs and order on
+// every rank, so every rank's residual is bit-identical.
+__device__ void tp_reduce_rows(const MegaArgs& a, const float* xraw, size_t part0, u64* dst,
+                               int r0, int r1, unsigned e) {
+  for (int r = r0 + threadIdx.x; r < r1; r += kThreads) {
+    float v[kTpMaxWorld];
+    ll_gather<kTpMaxWorld, true>(a, a.ll + part0, r, a.D, a.world * a.D, e, v);
+    float s = v[0];
+    for (int p = 1; p < a.world; p++) s += v[p];
+    ll_store(dst + r, xraw[r] + s, e);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -1006,6 +1046,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   float bv = -INFINITY;
   int bi = 0x7FFFFFFF;
   u64* am = a.ll + a.llo.am;
+  const int nam = a.world * (int)gridDim.x;  // argmax partials of all ranks
 
   for (int s = 0; s < a.steps; s++) {
     const unsigned e = a.epoch + (unsigned)s;
@@ -1032,7 +1073,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       // O + residual
       trace_mark(a, ph, MARK_BEGIN);
       stage_plain_ll(a, a.ll + a.llo.att + (size_t)l * QD, e, QD, xs, ph);
-      consume_phase(a, r, 4 * l + W_O, xs, Out{x_o, xraw, e}, red, bv, bi, ph);
+      {
+        const size_t part0 = a.llo.xpart + (size_t)(l * 2 + 0) * a.world * a.D;
+        consume_phase(a, r, 4 * l + W_O, xs, Out{x_o, xraw, e, part0 + (size_t)a.rank * a.D},
+                      red, bv, bi, ph);
+        if (a.world > 1)
+          tp_reduce_rows(a, xraw, part0, x_o, 2 * s_slices[W_O].pb, 2 * s_slices[W_O].pe, e);
+      }
       ph++;
       // gate/up + SwiGLU
       trace_mark(a, ph, MARK_BEGIN);
@@ -1043,7 +1090,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       // down + residual
       trace_mark(a, ph, MARK_BEGIN);
       stage_plain_ll(a, a.ll + a.llo.h + (size_t)l * a.Fl, e, a.Fl, xs, ph);
-      consume_phase(a, r, 4 * l + W_DOWN, xs, Out{x_d, xraw, e}, red, bv, bi, ph);
+      {
+        const size_t part0 = a.llo.xpart + (size_t)(l * 2 + 1) * a.world * a.D;
+        consume_phase(a, r, 4 * l + W_DOWN, xs, Out{x_d, xraw, e, part0 + (size_t)a.rank * a.D},
+                      red, bv, bi, ph);
+        if (a.world > 1)
+          tp_reduce_rows(a, xraw, part0, x_d, 2 * s_slices[W_DOWN].pb, 2 * s_slices[W_DOWN].pe,
+                         e);
+      }
       ph++;
     }
     // LM head with per-CTA argmax
@@ -1068,21 +1122,31 @@ __global__ void __launch_bounds__(kThreads, 1)
           i = cbest_i[w];
         }
       }
-      ll_store(am + blockIdx.x, v, e);
-      ll_store(am + gridDim.x + blockIdx.x, __int_as_float(i), e);
+      // Global vocabulary index: this rank's rows start at rank * Vl.
+      const int gi = (i == 0x7FFFFFFF) ? i : a.rank * a.Vl + i;
+      const int slot = a.rank * gridDim.x + blockIdx.x;
+      if (a.world > 1) {
+        for (int p = 0; p < a.world; p++) {
+          ll_store_sys(a.ll_peer[p] + a.llo.am + slot, v, e);
+          ll_store_sys(a.ll_peer[p] + a.llo.am + nam + slot, __int_as_float(gi), e);
+        }
+      } else {
+        ll_store(am + slot, v, e);
+        ll_store(am + nam + slot, __int_as_float(gi), e);
+      }
     }
     ph++;
-    // Every CTA reduces the published partials itself.
+    // Every CTA reduces the published partials (of every rank) itself.
     if (warp == 0) {
       float v = -INFINITY;
       int i = 0x7FFFFFFF;
-      for (int b0 = 0; b0 < (int)gridDim.x; b0 += 32 * 4) {
+      for (int b0 = 0; b0 < nam; b0 += 32 * 4) {
         float vb[4], ib[4];
-        ll_gather<4>(a, am, b0 + lane, 32, gridDim.x, e, vb);
-        ll_gather<4>(a, am + gridDim.x, b0 + lane, 32, gridDim.x, e, ib);
+        ll_gather<4, true>(a, am, b0 + lane, 32, nam, e, vb);
+        ll_gather<4, true>(a, am + nam, b0 + lane, 32, nam, e, ib);
 #pragma unroll
         for (int u = 0; u < 4; u++) {
-          if (b0 + lane + 32 * u >= (int)gridDim.x) continue;
+          if (b0 + lane + 32 * u >= nam) continue;
           const int ii = __float_as_int(ib[u]);
           if (vb[u] > v || (vb[u] == v && ii < i)) {
             v = vb[u];
@@ -1155,14 +1219,15 @@ size_t act_bytes(int D, int QD, int Fl, int HD, int G) {
 
 }  // namespace
 
-MegaFlagged mega_flagged_layout(int D, int QKVl, int QD, int Fl, int L, int grid) {
+MegaFlagged mega_flagged_layout(int D, int QKVl, int QD, int Fl, int L, int grid, int world) {
   MegaFlagged f;
   f.x = 0;
   f.qkv = f.x + (size_t)L * 2 * D;
   f.att = f.qkv + (size_t)L * QKVl;
   f.h = f.att + (size_t)L * QD;
-  f.am = f.h + (size_t)L * Fl;
-  f.total = f.am + 2 * (size_t)grid;
+  f.xpart = f.h + (size_t)L * Fl;
+  f.am = f.xpart + (world > 1 ? (size_t)L * 2 * world * D : 0);
+  f.total = f.am + 2 * (size_t)world * grid;
   return f;
 }
 

@@ -110,8 +110,8 @@ __device__ bool mbar_wait(uint32_t bar, unsigned parity, int* err) {
 }
 
 // 2D TMA tile load (x = inner element offset, a multiple of 64 -> 128-byte
-// aligned; y = row offset; rows past the tensor read as zeros). No
-// multicast.
+// aligned; y = row offset; rows past the tensor read as zeros). Each load
+// fills only the issuing CTA's shared memory.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
                                             uint32_t bar) {
   asm volatile(

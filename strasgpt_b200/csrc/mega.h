@@ -22,16 +22,19 @@ struct MegaLayer {
 };
 
 // Offsets (in 64-bit words) of the flagged vectors inside MegaArgs::ll.
+// Under tensor parallelism (world N > 1) the ranks write into each other's
+// copies of `xpart` and `am` over NVLink.
 struct MegaFlagged {
-  size_t x;    // [L][2][D]  residual after o_proj (0) and after down (1)
-  size_t qkv;  // [L][QKVl]
-  size_t att;  // [L][QHl*HD] merged attention output
-  size_t h;    // [L][Fl]     SwiGLU output
-  size_t am;   // [2][grid]   per-CTA argmax value / index
+  size_t x;      // [L][2][D]     residual after o_proj (0) and after down (1)
+  size_t qkv;    // [L][QKVl]
+  size_t att;    // [L][QHl*HD]   merged attention output
+  size_t h;      // [L][Fl]       SwiGLU output
+  size_t xpart;  // [L][2][N][D]  every rank's partial o_proj / down rows (N > 1)
+  size_t am;     // [2][N][grid]  per-CTA argmax value / global index of every rank
   size_t total;
 };
 
-MegaFlagged mega_flagged_layout(int D, int QKVl, int QD, int Fl, int L, int grid);
+MegaFlagged mega_flagged_layout(int D, int QKVl, int QD, int Fl, int L, int grid, int world);
 
 struct MegaArgs {
   int D, HD, QHl, KHl, G, Fl, Vl, L, QKVl, ctx;
@@ -50,6 +53,10 @@ struct MegaArgs {
   int nsplit, split_len;
   unsigned long long* ll;   // flagged vectors (layout: MegaFlagged)
   MegaFlagged llo;
+  // Tensor parallelism: this rank of `world`, and every rank's `ll` as
+  // mapped in this process (ll_peer[rank] == ll). world 1: ll_peer unused.
+  int rank, world;
+  unsigned long long* ll_peer[8];
   unsigned epoch;           // epoch of the first step; step s uses epoch + s
   int* tok;                 // in: token of the first step; out: last argmax
   int* pos;                 // in/out: position of the next token

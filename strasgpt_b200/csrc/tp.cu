@@ -204,15 +204,18 @@ void stage(TpComm& c, const float* src, size_t n, cudaStream_t s) {
 
 }  // namespace
 
-size_t tp_buffer_bytes(size_t cap) { return kHeader + 2 * cap * sizeof(float); }
+size_t tp_buffer_bytes(size_t cap, size_t extra) {
+  return kHeader + 2 * cap * sizeof(float) + (extra + 255) / 256 * 256;
+}
 
-void tp_alloc(TpComm* c, int rank, int world, size_t cap) {
+void tp_alloc(TpComm* c, int rank, int world, size_t cap, size_t extra) {
   if (world < 1 || world > kTpMaxRanks || rank < 0 || rank >= world)
     SG_DIE("invalid tensor-parallel placement");
   c->rank = rank;
   c->world = world;
   c->cap = (cap + 63) & ~(size_t)63;
-  const size_t bytes = tp_buffer_bytes(c->cap);
+  c->extra_off = kHeader + 2 * c->cap * sizeof(float);
+  const size_t bytes = tp_buffer_bytes(c->cap, extra);
   SG_CUDA(cudaMalloc(&c->local, bytes));
   SG_CUDA(cudaMemset(c->local, 0, bytes));
   SG_CUDA(cudaMalloc(&c->err, sizeof(int)));

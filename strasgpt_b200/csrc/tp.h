@@ -27,16 +27,18 @@ constexpr int kTpMaxRanks = 8;
 struct TpComm {
   int rank = 0, world = 1;
   size_t cap = 0;                       // floats per data half
+  size_t extra_off = 0;                 // byte offset of the extra region
   unsigned char* local = nullptr;       // this rank's exchange buffer
   unsigned char* peer[kTpMaxRanks] = {};  // every rank's buffer (own included)
   int* err = nullptr;                   // device int: non-zero after a timeout
   bool connected = false;
 };
 
-// Bytes of the exchange buffer for `cap` floats per half.
-size_t tp_buffer_bytes(size_t cap);
+// Bytes of the exchange buffer for `cap` floats per half and `extra` bytes
+// of a region other kernels share with the peers (zeroed, 256-aligned).
+size_t tp_buffer_bytes(size_t cap, size_t extra);
 // Allocates and zeroes this rank's buffer (and the error flag).
-void tp_alloc(TpComm* c, int rank, int world, size_t cap);
+void tp_alloc(TpComm* c, int rank, int world, size_t cap, size_t extra = 0);
 // 64-byte IPC handle of this rank's buffer.
 void tp_handle(const TpComm& c, void* out64);
 // Maps the peers' buffers from world x 64-byte handles (rank order).

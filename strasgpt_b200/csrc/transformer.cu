@@ -536,8 +536,6 @@ void alloc_state(const W_t* w, const transformer_configuration_t* c, S_t* s) {
   if (w->world > 1) {
     s->part = F32(T * D);
     s->logits_local = F32((size_t)s->logit_rows_max * w->Vl);
-    sg::tp_alloc(&s->tp, w->rank, w->world,
-                 std::max(T * D, (size_t)s->logit_rows_max * w->Vl));
   }
   const size_t kv = (size_t)w->L * w->KHl * s->ctx * HD;
   s->kc = F32(kv);
@@ -557,8 +555,10 @@ void alloc_state(const W_t* w, const transformer_configuration_t* c, S_t* s) {
   SG_CUDA(cudaMemset(s->step, 0, 4));
   SG_CUDA(cudaMemset(s->gen, 0, ((size_t)s->ctx + 1) * 4));
   sg::attn_decode_split(s->ctx, w->KHl, &s->nsplit, &s->split_len);
-  // Megakernel decode: dense models on one GPU, when a CTA fits on every SM.
-  s->use_mega = !w->moe && w->world == 1 && (w->Vl % 2 == 0) && w->L <= 96 &&
+  // Megakernel decode: dense models, when a CTA fits on every SM (under
+  // tensor parallelism for the greedy loop; predict keeps the per-op path,
+  // which gathers the full logits).
+  s->use_mega = !w->moe && (w->Vl % 2 == 0) && w->L <= 96 && w->world <= 8 &&
                 w->D <= 8192 && env_int("STRASGPT_MEGA", 1) != 0;
   if (s->use_mega) {
     s->mega_smem = sg::mega_smem_bytes(w->D, w->QHl * w->HD, w->Fl, w->HD, w->G);
@@ -590,12 +590,20 @@ void alloc_state(const W_t* w, const transformer_configuration_t* c, S_t* s) {
       SG_CUDA(cudaMemset(s->trace, 0, n * 8));
     }
     SG_CUDA(cudaMemset(s->err, 0, 4));
-    // Flagged hand-off vectors, zero (epoch 0: never written) at rest.
+    // Flagged hand-off vectors, zero (epoch 0: never written) at rest. Under
+    // tensor parallelism they live in the exchange buffer the ranks map.
     s->mega_llo = sg::mega_flagged_layout(w->D, w->QKVl, w->QHl * w->HD, w->Fl, w->L,
-                                          s->mega_grid);
-    s->mega_ll = (unsigned long long*)dalloc(s->allocs, s->mega_llo.total * 8, nullptr);
-    SG_CUDA(cudaMemset(s->mega_ll, 0, s->mega_llo.total * 8));
+                                          s->mega_grid, w->world);
+    if (w->world == 1) {
+      s->mega_ll = (unsigned long long*)dalloc(s->allocs, s->mega_llo.total * 8, nullptr);
+      SG_CUDA(cudaMemset(s->mega_ll, 0, s->mega_llo.total * 8));
+    }
     s->mega_epoch = 1;
+  }
+  if (w->world > 1) {
+    sg::tp_alloc(&s->tp, w->rank, w->world, std::max(T * D, (size_t)s->logit_rows_max * w->Vl),
+                 s->use_mega ? s->mega_llo.total * 8 : 0);
+    if (s->use_mega) s->mega_ll = (unsigned long long*)(s->tp.local + s->tp.extra_off);
   }
   // Split records and tickets: one set for the per-op decode kernel, one
   // per layer for the persistent kernel.
@@ -821,6 +829,14 @@ struct Runner {
     a.attn_partial = s->attn_partial; a.attn_ticket = s->attn_ticket;
     a.nsplit = s->mega_nsplit; a.split_len = s->mega_split_len;
     a.ll = s->mega_ll; a.llo = s->mega_llo; a.epoch = s->mega_epoch;
+    a.rank = w->rank; a.world = w->world;
+    for (int p = 0; p < 8; p++) a.ll_peer[p] = nullptr;
+    if (w->world == 1) {
+      a.ll_peer[0] = s->mega_ll;
+    } else {
+      for (int p = 0; p < w->world; p++)
+        a.ll_peer[p] = (unsigned long long*)(s->tp.peer[p] + s->tp.extra_off);
+    }
     a.tok = s->tok; a.pos = s->pos; a.step = s->step; a.gen = s->gen;
     a.gen_len = s->ctx + 1;
     a.err = s->err;
@@ -1047,7 +1063,7 @@ void predict_impl(transformer_t* t, size_t T, const int* tok, size_t n,
     set_pos(s, (int)s->cached_count);
     const size_t lo = std::max(c0, lstart);
     if (Tc == 1) {
-      if (s->use_mega) {
+      if (s->use_mega && w->world == 1) {
         r.mega(1, true);
       } else {
         if (!s->graph_logits) s->graph_logits = capture(r, false);
