@@ -26,17 +26,30 @@
 //
 // Weight streaming. Each weight phase gives CTA c a contiguous slice of row
 // pairs, so a CTA's weights for the whole launch form a fixed list of
-// contiguous byte ranges ("chunks", at most one shared-memory buffer each).
-// kRing buffers per CTA: thread 0 issues the cp.async.bulk copy (into its
-// own CTA's buffer only) of chunk g+kRing as soon as chunk g has been consumed, with
-// completion on the buffer's mbarrier. Weights never depend on activations,
-// so copies run ahead across phase and layer boundaries while a CTA waits
-// for its inputs. Attention CTAs prefetch their K/V rows into L2 during the
-// QKV phase.
+// chunks (up to 64 rows by a column range, one shared-memory buffer each).
+// A ninth warp is the producer: it walks that list and, for each of the
+// kRing buffers, waits until the consumers have released the buffer (empty
+// mbarrier), then copies the chunk's rows into it with one cp.async.bulk per
+// row (into its own CTA's buffer only), completion counted on the buffer's
+// full mbarrier. Rows sit kPad bytes further apart than in memory, so the
+// eight rows of a tensor-core fragment fall into different banks. Weights
+// never depend on activations, so copies run ahead across phase and layer
+// boundaries while the consumers wait for their inputs. Attention CTAs
+// prefetch their K/V rows into L2 during the QKV phase.
+//
+// Dot products on the tensor cores. The activation x is staged in shared
+// memory as bf16 parts x = hi + mid + lo (each the bf16 rounding of what
+// the previous parts leave), which reproduces fp32 x to about 2^-24. One
+// mma.sync m16n8k16 multiplies A = sixteen weight rows (ldmatrix from the
+// padded buffer) by B = the parts (columns 0..2 of 8) over 16 columns; the
+// fp32 accumulator columns are summed at the end. Each of the eight
+// consumer warps takes every eighth 32-column block of the chunk for all of
+// its rows, and the warps' partial sums meet in shared memory.
 //
 // Every wait is bounded (2 s): a timeout sets *err, later waits return at
-// once, the kernel runs to its end and the host reports the error. All
-// issued copies are consumed (waited on) before the kernel ends.
+// once, the kernel runs to its end and the host reports the error. The
+// producer waits (bounded) for the completion of its last copies before it
+// exits.
 //
 // Math per element is the same as the multi-kernel path (kernels.cu) and
 // the reference (source/transformer.c:1186-1602).
@@ -47,13 +60,16 @@
 namespace sg {
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
+constexpr int kThreads = 256;               // consumer threads
+constexpr int kWarps = kThreads / 32;       // consumer warps
+constexpr int kBlockThreads = kThreads + 32;  // + the producer warp
 constexpr int kPosPerPass = kWarps * 8;  // cache rows per CTA pass
+constexpr int kMaxChunkRows = 64;        // rows per weight chunk (4 fragments)
+constexpr int kPad = 16;                 // extra bytes per row in a buffer
+constexpr int kRing = 2;                 // weight buffers per CTA
 constexpr int kMaxSplits = 64;
 constexpr int kTpMaxWorld = 8;
 constexpr unsigned long long kTimeoutNs = 2000000000ULL;
-constexpr size_t kSmemBudget = 220 * 1024;  // dynamic shared memory per CTA
 
 // ---------------------------------------------------------------------------
 // PTX helpers
@@ -99,6 +115,36 @@ __device__ __forceinline__ void bulk_copy(void* dst, const void* src, unsigned b
           "r"(smem_addr(dst)),
       "l"(src), "r"(bytes), "r"(smem_addr(bar))
       : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// Barrier of the consumer warps only (the producer warp never joins it).
+__device__ __forceinline__ void csync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory");
+}
+
+// Four 8x8 bf16 matrices; lane i gives the address of row i % 8 of matrix
+// i / 8 and receives, from each matrix, the pair (row i / 4, cols 2 (i % 4)).
+// For matrices (rows 0-7, cols 0-7), (rows 8-15, cols 0-7), (rows 0-7,
+// cols 8-15), (rows 8-15, cols 8-15) of a 16x16 tile these are the A
+// fragments of m16n8k16.
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+// d += A (16x16 bf16, row-major fragments a0..a3) * B (16x8 bf16, b0/b1),
+// fp32 accumulators (rows g, g + 8; columns 2c, 2c + 1 of lane 4g + c).
+__device__ __forceinline__ void mma_bf16(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
 // ---------------------------------------------------------------------------
@@ -180,8 +226,9 @@ __device__ __forceinline__ void ll_gather(const MegaArgs& a, const u64* src, int
 
 // Trace record per (phase, CTA): [stage start, inputs complete, staged,
 // first chunk ready, consumed] (%globaltimer ns), then the phase's total ns
-// spent waiting for weight buffers and computing on them (thread 0 writes
-// them).
+// spent waiting for weight buffers, on its chunks (wait excluded), on warp
+// 0's dot products, and on the cross-warp sums and epilogues (thread 0
+// writes them).
 constexpr int kTraceWidth = kMegaTraceWidth;
 enum {
   MARK_BEGIN = 0,
@@ -190,7 +237,13 @@ enum {
   MARK_READY = 3,
   MARK_CONSUMED = 4,
   SUM_WAIT = 5,
-  SUM_COMPUTE = 6
+  SUM_COMPUTE = 6,
+  SUM_DOT = 7,
+  SUM_REDUCE = 8,
+  MARK_NORMED = 9,
+  MARK_SCALED = 10,
+  MARK_SYNCED = 11,
+  MARK_GAINS = 12
 };
 
 __device__ __forceinline__ void trace_put(const MegaArgs& a, int ph, int slot,
@@ -258,64 +311,63 @@ __device__ __forceinline__ Phase weight_phase(const MegaArgs& a, int wp) {
   return p;
 }
 
-// One chunk: row pairs [p0, p1) over columns [k0, k1) (either whole rows,
-// several pairs; or one pair and a column segment when a pair does not fit a
-// buffer).
+// One chunk: rows [r0, r1) of the phase's matrix over columns [k0, k1): up
+// to kMaxChunkRows rows, whole when they fit a buffer, else a column segment
+// (a row group then spans several chunks).
 struct Chunk {
-  int p0, p1, k0, k1;
-  bool last_seg;  // the chunk completes its pair(s)
+  int r0, r1, k0, k1;
+  bool first_seg, last_seg;
 };
 
 struct Slice {
-  int pb, pe;     // pairs [pb, pe) of this CTA
-  int ppc;        // pairs per chunk (whole rows), 0 when rows are split
-  int kseg;       // columns per segment when rows are split
-  int spp;        // segments per pair
+  int rb, re;     // rows [rb, re) of this CTA (whole row pairs)
+  int rows;       // rows per chunk (even, at most kMaxChunkRows)
+  int kseg;       // columns per chunk (a multiple of 256, or K)
+  int spp;        // chunks per row group
   int nchunks;
 };
+
+__device__ __forceinline__ int row_stride(int cols) { return 2 * cols + kPad; }
 
 __device__ __forceinline__ Slice cta_slice(const Phase& ph, int buf_bytes) {
   Slice s;
   const long long np = ph.pairs;
-  s.pb = (int)(np * blockIdx.x / gridDim.x);
-  s.pe = (int)(np * (blockIdx.x + 1) / gridDim.x);
-  const int n = s.pe - s.pb;
-  const int pair_bytes = 4 * ph.K;
-  if (pair_bytes <= buf_bytes) {
-    s.ppc = buf_bytes / pair_bytes;
+  s.rb = 2 * (int)(np * blockIdx.x / gridDim.x);
+  s.re = 2 * (int)(np * (blockIdx.x + 1) / gridDim.x);
+  const int n = s.re - s.rb;
+  // Whole rows, as many as the slice has up to kMaxChunkRows and what a
+  // buffer holds, when that is at least 16 rows (or the whole slice); else
+  // up to kMaxChunkRows rows by equal column segments (multiples of 256
+  // columns).
+  const int want = min(kMaxChunkRows, max(n, 2));
+  const int whole = min(want, (buf_bytes / row_stride(ph.K)) & ~1);
+  if (whole >= min(16, want)) {
+    s.rows = whole;
     s.kseg = ph.K;
     s.spp = 1;
-    s.nchunks = (n + s.ppc - 1) / s.ppc;
   } else {
-    s.ppc = 0;
-    s.kseg = (buf_bytes / 4) / 256 * 256;
-    s.spp = (ph.K + s.kseg - 1) / s.kseg;
-    s.nchunks = n * s.spp;
+    s.rows = min(want, (buf_bytes / row_stride(256)) & ~1);
+    const int kmax = ((buf_bytes / s.rows - kPad) / 2) / 256 * 256;
+    s.spp = (ph.K + kmax - 1) / kmax;
+    s.kseg = ((ph.K + s.spp - 1) / s.spp + 255) / 256 * 256;
   }
+  s.nchunks = ((n + s.rows - 1) / s.rows) * s.spp;
   return s;
 }
 
 __device__ __forceinline__ Chunk slice_chunk(const Slice& s, const Phase& ph, int ci) {
   Chunk c;
-  if (s.ppc) {
-    c.p0 = s.pb + ci * s.ppc;
-    c.p1 = min(c.p0 + s.ppc, s.pe);
-    c.k0 = 0;
-    c.k1 = ph.K;
-    c.last_seg = true;
-  } else {
-    const int pair = s.pb + ci / s.spp, seg = ci % s.spp;
-    c.p0 = pair;
-    c.p1 = pair + 1;
-    c.k0 = seg * s.kseg;
-    c.k1 = min(c.k0 + s.kseg, ph.K);
-    c.last_seg = (seg == s.spp - 1);
-  }
+  const int grp = ci / s.spp, seg = ci % s.spp;
+  c.r0 = s.rb + grp * s.rows;
+  c.r1 = min(c.r0 + s.rows, s.re);
+  c.k0 = seg * s.kseg;
+  c.k1 = min(c.k0 + s.kseg, ph.K);
+  c.first_seg = (seg == 0);
+  c.last_seg = (seg == s.spp - 1);
   return c;
 }
 
-// Copy-issue cursor (thread 0 only): walks the same chunk sequence as the
-// consumers, kRing chunks ahead.
+// Position in the producer's walk over the chunks of the launch.
 struct Cursor {
   int step, wp, ci;
 };
@@ -336,35 +388,18 @@ __device__ void cursor_skip_empty(const MegaArgs& a, Cursor& c) {
   }
 }
 
-__device__ void cursor_issue(const MegaArgs& a, Cursor& c, char* buf, uint64_t* bar) {
-  cursor_skip_empty(a, c);
-  if (c.step >= a.steps) return;
-  const Phase ph = weight_phase(a, c.wp);
-  const Slice& s = s_slices[ph.kind];
-  const Chunk ch = slice_chunk(s, ph, c.ci);
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  if (s.ppc) {
-    const unsigned bytes = (unsigned)(ch.p1 - ch.p0) * 4u * (unsigned)ph.K;
-    mbar_expect_tx(bar, bytes);
-    bulk_copy(buf, ph.W + (size_t)2 * ch.p0 * ph.K, bytes, bar);
-  } else {
-    const unsigned seg = (unsigned)(ch.k1 - ch.k0) * 2u;
-    mbar_expect_tx(bar, 2 * seg);
-    const uint16_t* r0 = ph.W + (size_t)2 * ch.p0 * ph.K + ch.k0;
-    bulk_copy(buf, r0, seg, bar);
-    bulk_copy(buf + seg, r0 + ph.K, seg, bar);
-  }
-  c.ci++;
-}
-
-// Bounded wait on a buffer's mbarrier phase.
-__device__ void wait_buffer(const MegaArgs& a, uint64_t* bar, unsigned parity) {
+// Bounded wait on an mbarrier phase; with `stop_on_err` it also returns as
+// soon as the error flag is set. `nap` (ns) between polls keeps a waiting
+// producer from taking issue slots from the consumer warps beside it.
+__device__ void wait_bar(const MegaArgs& a, uint64_t* bar, unsigned parity,
+                         bool stop_on_err = true, unsigned nap = 0) {
   if (mbar_try_wait(bar, parity)) return;
   const unsigned long long t0 = now_ns();
   unsigned spins = 0;
   while (!mbar_try_wait(bar, parity)) {
+    if (nap) __nanosleep(nap);
     if ((++spins & 63) == 0) {
-      if (*(volatile int*)a.err) return;
+      if (stop_on_err && *(volatile int*)a.err) return;
       if (now_ns() - t0 > kTimeoutNs) {
         atomicExch(a.err, 2);
         return;
@@ -373,64 +408,155 @@ __device__ void wait_buffer(const MegaArgs& a, uint64_t* bar, unsigned parity) {
   }
 }
 
+// The producer warp: copies every chunk of the launch, in the consumers'
+// order, into the ring. Chunk g goes to buffer g % kRing once the consumer
+// warps have released that buffer's previous chunk (empty[b]); its rows land
+// row_stride(k1 - k0) bytes apart. Stops issuing once the error flag is set;
+// before returning it waits (bounded) until its copies have landed.
+__device__ void produce(const MegaArgs& a, char* base, int buf_bytes, uint64_t* full,
+                        uint64_t* empty) {
+  const int lane = threadIdx.x & 31;
+  Cursor c = {0, 0, 0};
+  unsigned g = 0;
+  for (;;) {
+    cursor_skip_empty(a, c);
+    if (c.step >= a.steps) break;
+    const int b = (int)(g % kRing);
+    if (g >= (unsigned)kRing) {
+      if (lane == 0) wait_bar(a, empty + b, (g / kRing - 1) & 1, true, 128);
+      __syncwarp();
+    }
+    if (*(volatile int*)a.err) break;
+    const Phase ph = weight_phase(a, c.wp);
+    const Chunk ch = slice_chunk(s_slices[ph.kind], ph, c.ci);
+    const int nr = ch.r1 - ch.r0, w = ch.k1 - ch.k0;
+    const int stride = row_stride(w);
+    char* buf = base + (size_t)b * buf_bytes;
+    if (lane == 0) mbar_expect_tx(full + b, (unsigned)(nr * w * 2));
+    __syncwarp();
+    const uint16_t* src = ph.W + (size_t)ch.r0 * ph.K + ch.k0;
+    for (int r = lane; r < nr; r += 32)
+      bulk_copy(buf + (size_t)r * stride, src + (size_t)r * ph.K, (unsigned)(w * 2), full + b);
+    c.ci++;
+    g++;
+  }
+  // The last use of each buffer: its copy has landed (or the wait ran out).
+  if (lane == 0)
+    for (unsigned i = (g > (unsigned)kRing ? g - kRing : 0); i < g; i++)
+      wait_bar(a, full + i % kRing, (i / kRing) & 1, false);
+  __syncwarp();
+}
+
 // ---------------------------------------------------------------------------
 // Activation staging
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ int split_index(int k, int K) {
-  return (((k >> 2) & 1) * (K >> 1)) + ((k >> 3) << 2) + (k & 3);
+// The matvec input lives in shared memory as `parts` bf16 arrays (hi, mid,
+// lo), part p at element p * (K + 32). Inside an array, each block of 32
+// columns holds, for c = 0..3, the 16 bytes lane c of a warp feeds to two
+// m16n8k16 steps: words (2c, 2c + 8) of the block's first 16 columns, then
+// of its last 16 (a word = two consecutive columns).
+__device__ __forceinline__ int xq_pos(int k) {
+  const int kk = k & 31;
+  const int step = kk >> 4, ks = kk & 15;
+  return (k & ~31) + ((ks & 7) >> 1) * 8 + (step * 2 + (ks >> 3)) * 2 + (ks & 1);
 }
 
-// Largest K an RMSNorm staging keeps in registers (K = embedding_dim), read
-// in rounds of kNormBatch words per thread.
-constexpr int kNormBatch = 8;
-constexpr int kNormRegs = 32;
+__device__ __forceinline__ int xq_stride(int K) { return K + 32; }
 
-// xs (split layout) = rmsnorm(x) * nw from the flagged vector src (epoch e);
-// the raw values also go to xraw[K]. Every thread owns k = tid + u * 256.
-__device__ void stage_norm_ll(const MegaArgs& a, const u64* src, unsigned e, const uint16_t* nw,
-                              int K, float* xs, float* xraw, float* red, int ph) {
-  const int tid = threadIdx.x;
-  float v[kNormRegs], g[kNormRegs];
-  float ss = 0.f;
-  // The gains do not depend on the inputs: their loads go out first.
-#pragma unroll
-  for (int u = 0; u < kNormRegs; u++) {
-    const int k = tid + u * kThreads;
-    g[u] = (k < K) ? bf16_to_f32(__ldg(nw + k)) : 0.f;
+// Round to nearest even, fp32 -> bf16 bits (finite inputs).
+__device__ __forceinline__ uint16_t bf16_rne(float f) {
+  uint32_t u = __float_as_uint(f);
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+
+__device__ __forceinline__ void xq_put(uint16_t* xq, int K, int parts, int k, float v) {
+  const int pos = xq_pos(k), ps = xq_stride(K);
+  const uint16_t p0 = bf16_rne(v);
+  const float r1 = v - bf16_to_f32(p0);
+  const uint16_t p1 = bf16_rne(r1);
+  xq[pos] = p0;
+  xq[ps + pos] = p1;
+  if (parts > 2) xq[2 * ps + pos] = bf16_rne(r1 - bf16_to_f32(p1));
+}
+
+// Sum over the consumer threads (warp sums, then the warps' in order).
+__device__ __forceinline__ float cta_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  csync();
+  if (lane == 0) red[warp] = v;
+  csync();
+  float t = (lane < kWarps) ? red[lane] : 0.f;
+  return warp_sum(t);
+}
+
+// Largest K an RMSNorm staging handles (K = embedding_dim), read in rounds
+// of kNormBatch flagged words per thread.
+constexpr int kNormBatch = 16;
+constexpr int kNormMaxK = 32 * kThreads;
+
+// RMSNorm gains in shared memory: two bf16 vectors of D, refilled by bulk
+// copies (consumer thread 0) one phase or more before they are needed, so
+// that no gain load sits on a phase's critical path. Buffer 0 holds the
+// attention norm of the coming QKV phase (or the final norm), buffer 1 the
+// FFN norm. Every consumer thread counts the fills; thread 0 issues them.
+struct Gains {
+  uint16_t* buf[2];
+  uint64_t* bar;   // [2] in shared memory
+  unsigned n[2];   // fills issued so far
+};
+
+__device__ __forceinline__ void gains_fill(Gains& gs, int i, const uint16_t* src, int D) {
+  if (threadIdx.x == 0) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_expect_tx(gs.bar + i, (unsigned)D * 2u);
+    bulk_copy(gs.buf[i], src, (unsigned)D * 2u, gs.bar + i);
   }
+  gs.n[i]++;
+}
+
+__device__ __forceinline__ const uint16_t* gains_ready(const MegaArgs& a, Gains& gs, int i) {
+  wait_bar(a, gs.bar + i, (gs.n[i] - 1) & 1);
+  return gs.buf[i];
+}
+
+// xq = rmsnorm(x) * gains from the flagged vector src (epoch e); the raw
+// values also go to xraw[K]. Thread t owns k = t + u * 256. The loops are
+// kept short: this code runs once per phase, from a cold instruction cache.
+__device__ void stage_norm_ll(const MegaArgs& a, const u64* src, unsigned e, Gains& gs, int gi,
+                              int K, uint16_t* xq, int parts, float* xraw, float* red, int ph) {
+  const int tid = threadIdx.x;
+  float ss = 0.f;
+  for (int b = 0; b * kThreads < K; b += kNormBatch) {
+    float v[kNormBatch];
+    ll_gather<kNormBatch>(a, src, tid + b * kThreads, kThreads, K, e, v);
 #pragma unroll
-  for (int b = 0; b < kNormRegs; b += kNormBatch) {
-    if (b * kThreads < K) {
-      ll_gather<kNormBatch>(a, src, tid + b * kThreads, kThreads, K, e, v + b);
-    } else {
-#pragma unroll
-      for (int u = 0; u < kNormBatch; u++) v[b + u] = 0.f;
+    for (int u = 0; u < kNormBatch; u++) {
+      const int k = tid + (b + u) * kThreads;
+      if (k < K) {
+        xraw[k] = v[u];
+        ss += v[u] * v[u];
+      }
     }
   }
   trace_mark(a, ph, MARK_INPUTS);
-#pragma unroll
-  for (int u = 0; u < kNormRegs; u++) {
-    const int k = tid + u * kThreads;
-    if (k >= K) v[u] = 0.f;
-    ss += v[u] * v[u];
-  }
-  ss = block_sum(ss, red);
+  ss = cta_sum(ss, red);
+  trace_mark(a, ph, MARK_NORMED);
   ss /= (float)K;
   const float inv = 1.0f / sqrtf(ss + a.eps);
-#pragma unroll
-  for (int u = 0; u < kNormRegs; u++) {
-    const int k = tid + u * kThreads;
-    if (k < K) {
-      xs[split_index(k, K)] = (v[u] * inv) * g[u];
-      xraw[k] = v[u];
-    }
-  }
-  __syncthreads();
+  const uint16_t* g = gains_ready(a, gs, gi);
+  trace_mark(a, ph, MARK_GAINS);
+  for (int k = tid; k < K; k += kThreads)
+    xq_put(xq, K, parts, k, (xraw[k] * inv) * bf16_to_f32(g[k]));
+  trace_mark(a, ph, MARK_SCALED);
+  csync();
+  trace_mark(a, ph, MARK_SYNCED);
 }
 
-// xs (split layout) = the flagged vector src (epoch e), K floats.
-__device__ void stage_plain_ll(const MegaArgs& a, const u64* src, unsigned e, int K, float* xs,
-                               int ph) {
+// xq = the flagged vector src (epoch e), K floats.
+__device__ void stage_plain_ll(const MegaArgs& a, const u64* src, unsigned e, int K, uint16_t* xq,
+                               int parts, int ph) {
   const int tid = threadIdx.x;
   constexpr int B = 16;
   for (int base = tid; base < K; base += B * kThreads) {
@@ -439,53 +565,56 @@ __device__ void stage_plain_ll(const MegaArgs& a, const u64* src, unsigned e, in
 #pragma unroll
     for (int u = 0; u < B; u++) {
       const int k = base + u * kThreads;
-      if (k < K) xs[split_index(k, K)] = v[u];
+      if (k < K) xq_put(xq, K, parts, k, v[u]);
     }
   }
   trace_mark(a, ph, MARK_INPUTS);
-  __syncthreads();
+  csync();
 }
 
-// Layer-0 input: the embedding row of `token` (xraw) and its RMSNorm (xs).
-__device__ void stage_embedding(const MegaArgs& a, int token, const uint16_t* nw, float* xs,
-                                float* xraw, float* red) {
+// Layer-0 input: the embedding row of `token` (xraw) and its RMSNorm (xq)
+// with the gains of buffer gi.
+__device__ void stage_embedding(const MegaArgs& a, int token, Gains& gs, int gi, uint16_t* xq,
+                                int parts, float* xraw, float* red) {
   const int tid = threadIdx.x, K = a.D;
   const uint16_t* row = a.emb + (size_t)token * K;
-  float v[kNormRegs], g[kNormRegs];
   float ss = 0.f;
+  for (int b = 0; b * kThreads < K; b += kNormBatch) {
+    float v[kNormBatch];
 #pragma unroll
-  for (int u = 0; u < kNormRegs; u++) {
-    const int k = tid + u * kThreads;
-    v[u] = (k < K) ? bf16_to_f32(__ldg(row + k)) : 0.f;
-    g[u] = (k < K) ? bf16_to_f32(__ldg(nw + k)) : 0.f;
-  }
+    for (int u = 0; u < kNormBatch; u++) {
+      const int k = tid + (b + u) * kThreads;
+      v[u] = (k < K) ? bf16_to_f32(__ldg(row + k)) : 0.f;
+    }
 #pragma unroll
-  for (int u = 0; u < kNormRegs; u++) ss += v[u] * v[u];
-  ss = block_sum(ss, red);
-  ss /= (float)K;
-  const float inv = 1.0f / sqrtf(ss + a.eps);
-#pragma unroll
-  for (int u = 0; u < kNormRegs; u++) {
-    const int k = tid + u * kThreads;
-    if (k < K) {
-      xs[split_index(k, K)] = (v[u] * inv) * g[u];
-      xraw[k] = v[u];
+    for (int u = 0; u < kNormBatch; u++) {
+      const int k = tid + (b + u) * kThreads;
+      if (k < K) {
+        xraw[k] = v[u];
+        ss += v[u] * v[u];
+      }
     }
   }
-  __syncthreads();
+  ss = cta_sum(ss, red);
+  ss /= (float)K;
+  const float inv = 1.0f / sqrtf(ss + a.eps);
+  const uint16_t* g = gains_ready(a, gs, gi);
+  for (int k = tid; k < K; k += kThreads)
+    xq_put(xq, K, parts, k, (xraw[k] * inv) * bf16_to_f32(g[k]));
+  csync();
 }
 
 // ---------------------------------------------------------------------------
 // Consuming one weight phase
 // ---------------------------------------------------------------------------
-constexpr int kRing = 4;  // weight buffers per CTA
-
 struct Ring {
   char* base;      // buffer b starts at base + b * buf_bytes
-  uint64_t* bar;   // [kRing] in shared memory
+  uint64_t* full;  // [kRing]: the chunk in buffer b has landed
+  uint64_t* empty; // [kRing]: the consumer warps are done with buffer b
   int buf_bytes;
   unsigned g;      // chunks consumed so far
-  Cursor cur;      // thread 0: next chunk to issue
+  unsigned nred;   // cross-warp reductions so far (selects the red half)
+  float* red;      // [2][kWarps][kMaxChunkRows] per-warp partial row sums
 };
 
 // Where a phase's outputs go.
@@ -539,138 +668,119 @@ __device__ __forceinline__ void pair_epilogue(const MegaArgs& a, const Out& o, i
   }
 }
 
-// Consumes every chunk of weight phase `wp` with activations in xs (split
-// layout, K floats). For the LM head, (bv, bi) track the warp's argmax.
-__device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const float* xs, const Out& o,
-                              float* red, float& bv, int& bi, int ph) {
+// Consumes every chunk of weight phase `wp` with the activation parts in xq
+// (K columns). Warp w multiplies 32-column blocks w, w + 8, ... of a chunk
+// for all of the chunk's 16-row groups and keeps its row sums in shared
+// memory (added up over the column segments of a row group); after the last
+// segment the warps' sums meet and thread t finishes row pair t. For the LM
+// head, (bv, bi) track the thread's argmax.
+__device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const uint16_t* xq, int parts,
+                              const Out& o, float& bv, int& bi, int ph) {
   trace_mark(a, ph, MARK_STAGED);
   const Phase phs = weight_phase(a, wp);
   const Slice s = s_slices[phs.kind];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int K = phs.K;
-  const float4* lo4 = reinterpret_cast<const float4*>(xs);
-  const float4* hi4 = lo4 + (K >> 3);
-  float acc0 = 0.f, acc1 = 0.f;  // split rows: running sums (thread 0)
+  const int g = lane >> 2, c = lane & 3;
+  const uint4* xq4 = reinterpret_cast<const uint4*>(xq) + (size_t)g * (xq_stride(phs.K) / 8);
+  const bool has_x = g < parts;
   const bool tr = a.trace != nullptr;
-  unsigned long long t_wait = 0, t_comp = 0, t0 = 0;
+  unsigned long long t_wait = 0, t_dot = 0, t_red = 0, t0 = 0;
   for (int ci = 0; ci < s.nchunks; ci++) {
-    const int b = r.g % kRing;
+    const int b = (int)(r.g % kRing);
     if (tr) t0 = now_ns();
-    wait_buffer(a, r.bar + b, (r.g / kRing) & 1);
+    wait_bar(a, r.full + b, (r.g / kRing) & 1);
     if (tr) {
       const unsigned long long t1 = now_ns();
       t_wait += t1 - t0;
       t0 = t1;
     }
     if (ci == 0) trace_mark(a, ph, MARK_READY);
-    const Chunk c = slice_chunk(s, phs, ci);
-    const uint16_t* wb = reinterpret_cast<const uint16_t*>(r.base + (size_t)b * r.buf_bytes);
-    if (s.ppc && c.p1 - c.p0 < kWarps) {
-      // Fewer pairs than warps: wpp warps share each pair along K, the
-      // partial sums meet in shared memory, lane 0 of warp i finishes pair i.
-      const int P = c.p1 - c.p0;
-      const int wpp = kWarps / P;
-      const int pi = warp / wpp, part = warp % wpp;
-      float a0 = 0.f, a1 = 0.f;
-      if (pi < P) {
-        const uint16_t* w0 = wb + (size_t)pi * 2 * K;
-        const uint16_t* w1 = w0 + K;
-        float s0[8], s1[8];
+    const Chunk ch = slice_chunk(s, phs, ci);
+    const int nr = ch.r1 - ch.r0;
+    const int ng = (nr + 15) >> 4;
+    const int stride = row_stride(ch.k1 - ch.k0);
+    const int nkb = (ch.k1 - ch.k0) >> 5;
+    float acc[kMaxChunkRows / 16][2][4];
 #pragma unroll
-        for (int i = 0; i < 8; i++) s0[i] = s1[i] = 0.f;
-#pragma unroll 4
-        for (int k = part * 256 + lane * 8; k < K; k += wpp * 256) {
-          const uint4 v0 = *reinterpret_cast<const uint4*>(w0 + k);
-          const uint4 v1 = *reinterpret_cast<const uint4*>(w1 + k);
-          const float4 xa = lo4[k >> 3], xb = hi4[k >> 3];
-          acc8(v0, xa, xb, s0);
-          acc8(v1, xa, xb, s1);
-        }
-        a0 = ((s0[0] + s0[1]) + (s0[2] + s0[3])) + ((s0[4] + s0[5]) + (s0[6] + s0[7]));
-        a1 = ((s1[0] + s1[1]) + (s1[2] + s1[3])) + ((s1[4] + s1[5]) + (s1[6] + s1[7]));
-        a0 = warp_sum(a0);
-        a1 = warp_sum(a1);
-      }
-      if (lane == 0) {
-        red[warp] = a0;
-        red[kWarps + warp] = a1;
-      }
-      __syncthreads();
-      if (lane == 0 && warp < P) {
-        float y0 = 0.f, y1 = 0.f;
-        for (int q = 0; q < wpp; q++) {
-          y0 += red[warp * wpp + q];
-          y1 += red[kWarps + warp * wpp + q];
-        }
-        pair_epilogue(a, o, phs.kind, c.p0 + warp, y0, y1, bv, bi);
-      }
-    } else if (s.ppc) {
-      for (int p = c.p0 + warp; p < c.p1; p += kWarps) {
-        const uint16_t* w0 = wb + (size_t)(p - c.p0) * 2 * K;
-        const uint16_t* w1 = w0 + K;
-        // One accumulator per element slot: no FMA dependency chain longer
-        // than K / 256.
-        float s0[8], s1[8];
+    for (int q = 0; q < kMaxChunkRows / 16; q++)
 #pragma unroll
-        for (int i = 0; i < 8; i++) s0[i] = s1[i] = 0.f;
-#pragma unroll 4
-        for (int k = lane * 8; k < K; k += 256) {
-          const uint4 v0 = *reinterpret_cast<const uint4*>(w0 + k);
-          const uint4 v1 = *reinterpret_cast<const uint4*>(w1 + k);
-          const float4 xa = lo4[k >> 3], xb = hi4[k >> 3];
-          acc8(v0, xa, xb, s0);
-          acc8(v1, xa, xb, s1);
-        }
-        float a0 = ((s0[0] + s0[1]) + (s0[2] + s0[3])) + ((s0[4] + s0[5]) + (s0[6] + s0[7]));
-        float a1 = ((s1[0] + s1[1]) + (s1[2] + s1[3])) + ((s1[4] + s1[5]) + (s1[6] + s1[7]));
-        a0 = warp_sum(a0);
-        a1 = warp_sum(a1);
-        if (lane == 0) pair_epilogue(a, o, phs.kind, p, a0, a1, bv, bi);
-      }
-    } else {
-      const int seg = c.k1 - c.k0;
-      const uint16_t* w0 = wb;
-      const uint16_t* w1 = wb + seg;
-      float s0[8], s1[8];
+      for (int h = 0; h < 2; h++)
 #pragma unroll
-      for (int i = 0; i < 8; i++) s0[i] = s1[i] = 0.f;
-#pragma unroll 4
-      for (int k = warp * 256 + lane * 8; k < seg; k += kWarps * 256) {
-        const uint4 v0 = *reinterpret_cast<const uint4*>(w0 + k);
-        const uint4 v1 = *reinterpret_cast<const uint4*>(w1 + k);
-        const int kk = c.k0 + k;
-        const float4 xa = lo4[kk >> 3], xb = hi4[kk >> 3];
-        acc8(v0, xa, xb, s0);
-        acc8(v1, xa, xb, s1);
-      }
-      float a0 = ((s0[0] + s0[1]) + (s0[2] + s0[3])) + ((s0[4] + s0[5]) + (s0[6] + s0[7]));
-      float a1 = ((s1[0] + s1[1]) + (s1[2] + s1[3])) + ((s1[4] + s1[5]) + (s1[6] + s1[7]));
-      a0 = warp_sum(a0);
-      a1 = warp_sum(a1);
-      if (lane == 0) {
-        red[warp] = a0;
-        red[kWarps + warp] = a1;
-      }
-      __syncthreads();
-      if (tid == 0) {
-        for (int w = 0; w < kWarps; w++) {
-          acc0 += red[w];
-          acc1 += red[kWarps + w];
-        }
-        if (c.last_seg) {
-          pair_epilogue(a, o, phs.kind, c.p0, acc0, acc1, bv, bi);
-          acc0 = acc1 = 0.f;
+        for (int i = 0; i < 4; i++) acc[q][h][i] = 0.f;
+    // Lane address for ldmatrix: row (lane % 8) + 8 ((lane / 8) % 2) of
+    // group q (rows past the chunk read its last row), 8 columns at
+    // 8 (lane / 16) of the 16-column step.
+    const uint32_t bbase = smem_addr(r.base + (size_t)b * r.buf_bytes) + (uint32_t)((lane >> 4) * 16);
+    uint32_t lrow[kMaxChunkRows / 16];
+#pragma unroll
+    for (int q = 0; q < kMaxChunkRows / 16; q++)
+      lrow[q] = bbase + (uint32_t)(min(q * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, nr - 1) * stride);
+    for (int kb = warp; kb < nkb; kb += kWarps) {
+      uint4 xb = make_uint4(0u, 0u, 0u, 0u);
+      if (has_x) xb = xq4[(size_t)(((ch.k0 >> 5) + kb) * 4 + c)];
+#pragma unroll
+      for (int q = 0; q < kMaxChunkRows / 16; q++) {
+        if (q < ng) {
+          uint32_t m0[4], m1[4];
+          ldsm_x4(lrow[q] + (uint32_t)(kb * 64), m0);
+          ldsm_x4(lrow[q] + (uint32_t)(kb * 64 + 32), m1);
+          mma_bf16(acc[q][0], m0, xb.x, xb.y);
+          mma_bf16(acc[q][1], m1, xb.z, xb.w);
         }
       }
     }
-    __syncthreads();  // buffer b fully read
-    if (tid == 0) cursor_issue(a, r.cur, r.base + (size_t)b * r.buf_bytes, r.bar + b);
-    if (tr) t_comp += now_ns() - t0;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(r.empty + b);  // this warp is done with buffer b
+    // Column p of the accumulators holds part p's products: lane 4g has
+    // parts 0, 1 and lane 4g + 1 part 2 of rows g and g + 8. The warp's row
+    // sums go to (or, for later column segments, add to) its red row.
+    float* red = r.red + (size_t)(r.nred & 1) * kWarps * kMaxChunkRows;
+    float* wred = red + warp * kMaxChunkRows;
+#pragma unroll
+    for (int q = 0; q < kMaxChunkRows / 16; q++) {
+      if (q < ng) {
+        const float c0 = acc[q][0][0] + acc[q][1][0], c1 = acc[q][0][1] + acc[q][1][1];
+        const float c2 = acc[q][0][2] + acc[q][1][2], c3 = acc[q][0][3] + acc[q][1][3];
+        const float lo0 = __shfl_down_sync(0xFFFFFFFFu, c0, 1);
+        const float lo2 = __shfl_down_sync(0xFFFFFFFFu, c2, 1);
+        if (c == 0) {
+          const float v0 = (c0 + c1) + lo0, v8 = (c2 + c3) + lo2;
+          if (ch.first_seg) {
+            wred[q * 16 + g] = v0;
+            wred[q * 16 + g + 8] = v8;
+          } else {
+            wred[q * 16 + g] += v0;
+            wred[q * 16 + g + 8] += v8;
+          }
+        }
+      }
+    }
+    if (tr) {
+      const unsigned long long t1 = now_ns();
+      t_dot += t1 - t0;
+      t0 = t1;
+    }
+    if (ch.last_seg) {
+      r.nred++;
+      csync();
+      if (tid < (nr >> 1)) {
+        float y0 = 0.f, y1 = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; w++) {
+          y0 += red[w * kMaxChunkRows + 2 * tid];
+          y1 += red[w * kMaxChunkRows + 2 * tid + 1];
+        }
+        pair_epilogue(a, o, phs.kind, (ch.r0 >> 1) + tid, y0, y1, bv, bi);
+      }
+      if (tr) t_red += now_ns() - t0;
+    }
     r.g++;
   }
   trace_mark(a, ph, MARK_CONSUMED);
   trace_put(a, ph, SUM_WAIT, t_wait);
-  trace_put(a, ph, SUM_COMPUTE, t_comp);
+  trace_put(a, ph, SUM_COMPUTE, t_dot + t_red);
+  trace_put(a, ph, SUM_DOT, t_dot);
+  trace_put(a, ph, SUM_REDUCE, t_red);
 }
 
 // Tensor parallelism: rows [r0, r1) of the residual (this CTA's rows of the
@@ -774,18 +884,11 @@ __device__ void prefetch_kv(const MegaArgs& a, int l, int pos) {
   }
 }
 
-// L2 prefetch of the small per-layer vectors of layer `l` (norm gains), or
-// of the final norm when l == L: they are evicted between decode steps by
-// the weight stream, and every CTA reads them on a phase's critical path.
+// L2 prefetch of the q/k norm gains of layer `l` (l < L): the attention
+// CTAs read them on the phase's critical path.
 __device__ void prefetch_gains(const MegaArgs& a, int l) {
-  if (threadIdx.x != 32) return;
-  if (l >= a.L) {
-    prefetch_l2(a.out_norm, (uint32_t)a.D * 2);
-    return;
-  }
+  if (threadIdx.x != 32 || l >= a.L) return;
   const MegaLayer& ly = s_layers[l];
-  prefetch_l2(ly.attn_norm, (uint32_t)a.D * 2);
-  prefetch_l2(ly.ffn_norm, (uint32_t)a.D * 2);
   if (ly.q_norm) prefetch_l2(ly.q_norm, (uint32_t)a.HD * 2);
   if (ly.k_norm) prefetch_l2(ly.k_norm, (uint32_t)a.HD * 2);
 }
@@ -843,7 +946,7 @@ __device__ void attn_item(const MegaArgs& a, const MegaLayer& ly, int l, int kh,
 #pragma unroll
     for (int j = 0; j < V; j++) vb[(size_t)pos * HD + lane + 32 * j] = vv[j];
   }
-  __syncthreads();
+  csync();
   trace_mark(a, ph, MARK_INPUTS);
 
   float m[G], lsum[G], acc[G][V];
@@ -918,7 +1021,7 @@ __device__ void attn_item(const MegaArgs& a, const MegaLayer& ly, int l, int kh,
       m[g] = mn;
     }
   }
-  __syncthreads();  // the q/k warps' scratch use of wacc is over
+  csync();  // the q/k warps' scratch use of wacc is over
 #pragma unroll
   for (int g = 0; g < G; g++) {
     if (lane == 0) {
@@ -928,7 +1031,7 @@ __device__ void attn_item(const MegaArgs& a, const MegaLayer& ly, int l, int kh,
 #pragma unroll
     for (int v = 0; v < V; v++) wacc[((size_t)warp * G + g) * HD + lane * V + v] = acc[g][v];
   }
-  __syncthreads();
+  csync();
   const int nsplit = a.nsplit;
   float* part = a.attn_partial + (size_t)l * a.QHl * nsplit * (HD + 4);
   for (int ei = tid; ei < G * HD; ei += kThreads) {
@@ -954,14 +1057,14 @@ __device__ void attn_item(const MegaArgs& a, const MegaLayer& ly, int l, int kh,
     P[4 + dd] = A;
   }
   __threadfence();
-  __syncthreads();
+  csync();
   trace_mark(a, ph, MARK_STAGED);
   if (tid == 0) {
     int* ticket = a.attn_ticket + (size_t)l * a.KHl + kh;
     *is_last = (atomicAdd(ticket, 1) == nsplit - 1);
     if (*is_last) *ticket = 0;  // its next use is in a later step
   }
-  __syncthreads();
+  csync();
   if (!*is_last) return;
   __threadfence();
   // Merge: att = sum_j c_j acc_j / sum_j c_j l_j, c_j = exp(m_j - max m);
@@ -982,7 +1085,7 @@ __device__ void attn_item(const MegaArgs& a, const MegaLayer& ly, int l, int kh,
     ls = warp_sum(ls);
     if (lane == 0) Ls[g] = ls;
   }
-  __syncthreads();
+  csync();
   u64* att = a.ll + a.llo.att + (size_t)l * a.QHl * HD;
   for (int ei = tid; ei < G * HD; ei += kThreads) {
     const int g = ei / HD, dd = ei % HD;
@@ -999,7 +1102,7 @@ __device__ void attn_item(const MegaArgs& a, const MegaLayer& ly, int l, int kh,
     }
     ll_store(att + (size_t)(kh * G + g) * HD + dd, A / Ls[g], e);
   }
-  __syncthreads();
+  csync();
   trace_mark(a, ph, MARK_READY);
 }
 
@@ -1007,25 +1110,31 @@ __device__ void attn_item(const MegaArgs& a, const MegaLayer& ly, int l, int kh,
 // The kernel
 // ---------------------------------------------------------------------------
 template <int HD, int G>
-__global__ void __launch_bounds__(kThreads, 1)
-    k_mega_decode(const __grid_constant__ MegaArgs a, int buf_bytes) {
+__global__ void __launch_bounds__(kBlockThreads, 1)
+    k_mega_decode(const __grid_constant__ MegaArgs a, int buf_bytes, int parts) {
   extern __shared__ __align__(128) char dyn[];
   __shared__ float red[32];
   __shared__ float cbest_v[kWarps];
   __shared__ int cbest_i[kWarps];
-  __shared__ __align__(8) uint64_t ring_bar[kRing];
+  __shared__ __align__(8) uint64_t full_bar[kRing];
+  __shared__ __align__(8) uint64_t empty_bar[kRing];
+  __shared__ __align__(8) uint64_t gain_bar[2];
+  __shared__ __align__(16) float mv_red[2 * kWarps * kMaxChunkRows];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  Ring r;
-  r.base = dyn;
-  r.bar = ring_bar;
-  r.buf_bytes = buf_bytes;
-  r.g = 0;
-  r.cur = {0, 0, 0};
+  const int D32 = (a.D + 31) / 32 * 32;
   float* xraw = reinterpret_cast<float*>(dyn + (size_t)kRing * buf_bytes);  // [D]
-  float* xs = xraw + ((a.D + 31) / 32) * 32;  // matvec input / attention scratch
-  for (int i = threadIdx.x; i < a.L; i += kThreads) s_layers[i] = a.layers[i];
+  uint16_t* gain_buf = reinterpret_cast<uint16_t*>(xraw + D32);              // [2][D]
+  // Matvec input (bf16 parts) or attention scratch (floats).
+  float* xs = reinterpret_cast<float*>(gain_buf + 2 * D32);
+  uint16_t* xq = reinterpret_cast<uint16_t*>(xs);
+  for (int i = threadIdx.x; i < a.L; i += kBlockThreads) s_layers[i] = a.layers[i];
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kRing; i++) mbar_init(&ring_bar[i], 1);
+    for (int i = 0; i < kRing; i++) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], kWarps);
+    }
+    mbar_init(&gain_bar[0], 1);
+    mbar_init(&gain_bar[1], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -1035,8 +1144,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     s_slices[threadIdx.x] = cta_slice(weight_phase(a, wp), buf_bytes);
   }
   __syncthreads();
-  if (threadIdx.x == 0)
-    for (int i = 0; i < kRing; i++) cursor_issue(a, r.cur, dyn + (size_t)i * buf_bytes, &ring_bar[i]);
+  if (warp == kWarps) {
+    produce(a, dyn, buf_bytes, full_bar, empty_bar);
+    return;
+  }
+  Ring r;
+  r.base = dyn;
+  r.full = full_bar;
+  r.empty = empty_bar;
+  r.buf_bytes = buf_bytes;
+  r.g = 0;
+  r.nred = 0;
+  r.red = mv_red;
+  Gains gs;
+  gs.buf[0] = gain_buf;
+  gs.buf[1] = gain_buf + D32;
+  gs.bar = gain_bar;
+  gs.n[0] = gs.n[1] = 0;
+  gains_fill(gs, 0, s_layers[0].attn_norm, a.D);
+  gains_fill(gs, 1, s_layers[0].ffn_norm, a.D);
   int ph = 0;  // phase counter (trace only)
   int pos = __ldcg(a.pos);
   int token = __ldcg(a.tok);
@@ -1059,11 +1185,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_kv<HD>(a, l, pos);
       prefetch_gains(a, l + 1);
       if (l == 0)
-        stage_embedding(a, token, ly.attn_norm, xs, xraw, red);
+        stage_embedding(a, token, gs, 0, xq, parts, xraw, red);
       else
-        stage_norm_ll(a, x_o - 2 * (size_t)a.D + a.D, e, ly.attn_norm, a.D, xs, xraw, red, ph);
-      consume_phase(a, r, 4 * l + W_QKV, xs,
-                    Out{a.ll + a.llo.qkv + (size_t)l * a.QKVl, nullptr, e}, red, bv, bi, ph);
+        stage_norm_ll(a, x_o - 2 * (size_t)a.D + a.D, e, gs, 0, a.D, xq, parts, xraw, red, ph);
+      gains_fill(gs, 0, l + 1 < a.L ? s_layers[l + 1].attn_norm : a.out_norm, a.D);
+      consume_phase(a, r, 4 * l + W_QKV, xq, parts,
+                    Out{a.ll + a.llo.qkv + (size_t)l * a.QKVl, nullptr, e}, bv, bi, ph);
       ph++;
       // ATTN
       trace_mark(a, ph, MARK_BEGIN);
@@ -1072,47 +1199,60 @@ __global__ void __launch_bounds__(kThreads, 1)
       ph++;
       // O + residual
       trace_mark(a, ph, MARK_BEGIN);
-      stage_plain_ll(a, a.ll + a.llo.att + (size_t)l * QD, e, QD, xs, ph);
+      stage_plain_ll(a, a.ll + a.llo.att + (size_t)l * QD, e, QD, xq, parts, ph);
       {
         const size_t part0 = a.llo.xpart + (size_t)(l * 2 + 0) * a.world * a.D;
-        consume_phase(a, r, 4 * l + W_O, xs, Out{x_o, xraw, e, part0 + (size_t)a.rank * a.D},
-                      red, bv, bi, ph);
+        consume_phase(a, r, 4 * l + W_O, xq, parts,
+                      Out{x_o, xraw, e, part0 + (size_t)a.rank * a.D}, bv, bi, ph);
         if (a.world > 1)
-          tp_reduce_rows(a, xraw, part0, x_o, 2 * s_slices[W_O].pb, 2 * s_slices[W_O].pe, e);
+          tp_reduce_rows(a, xraw, part0, x_o, s_slices[W_O].rb, s_slices[W_O].re, e);
       }
       ph++;
       // gate/up + SwiGLU
       trace_mark(a, ph, MARK_BEGIN);
-      stage_norm_ll(a, x_o, e, ly.ffn_norm, a.D, xs, xraw, red, ph);
-      consume_phase(a, r, 4 * l + W_GU, xs, Out{a.ll + a.llo.h + (size_t)l * a.Fl, nullptr, e},
-                    red, bv, bi, ph);
+      stage_norm_ll(a, x_o, e, gs, 1, a.D, xq, parts, xraw, red, ph);
+      if (l + 1 < a.L)
+        gains_fill(gs, 1, s_layers[l + 1].ffn_norm, a.D);
+      else if (s + 1 < a.steps)
+        gains_fill(gs, 1, s_layers[0].ffn_norm, a.D);
+      consume_phase(a, r, 4 * l + W_GU, xq, parts,
+                    Out{a.ll + a.llo.h + (size_t)l * a.Fl, nullptr, e}, bv, bi, ph);
       ph++;
       // down + residual
       trace_mark(a, ph, MARK_BEGIN);
-      stage_plain_ll(a, a.ll + a.llo.h + (size_t)l * a.Fl, e, a.Fl, xs, ph);
+      stage_plain_ll(a, a.ll + a.llo.h + (size_t)l * a.Fl, e, a.Fl, xq, parts, ph);
       {
         const size_t part0 = a.llo.xpart + (size_t)(l * 2 + 1) * a.world * a.D;
-        consume_phase(a, r, 4 * l + W_DOWN, xs, Out{x_d, xraw, e, part0 + (size_t)a.rank * a.D},
-                      red, bv, bi, ph);
+        consume_phase(a, r, 4 * l + W_DOWN, xq, parts,
+                      Out{x_d, xraw, e, part0 + (size_t)a.rank * a.D}, bv, bi, ph);
         if (a.world > 1)
-          tp_reduce_rows(a, xraw, part0, x_d, 2 * s_slices[W_DOWN].pb, 2 * s_slices[W_DOWN].pe,
+          tp_reduce_rows(a, xraw, part0, x_d, s_slices[W_DOWN].rb, s_slices[W_DOWN].re,
                          e);
       }
       ph++;
     }
     // LM head with per-CTA argmax
     trace_mark(a, ph, MARK_BEGIN);
-    prefetch_gains(a, 0);  // next step's layer 0
-    stage_norm_ll(a, a.ll + a.llo.x + (size_t)(a.L - 1) * 2 * a.D + a.D, e, a.out_norm, a.D, xs,
+    stage_norm_ll(a, a.ll + a.llo.x + (size_t)(a.L - 1) * 2 * a.D + a.D, e, gs, 0, a.D, xq, parts,
                   xraw, red, ph);
+    if (s + 1 < a.steps) gains_fill(gs, 0, s_layers[0].attn_norm, a.D);
     bv = -INFINITY;
     bi = 0x7FFFFFFF;
-    consume_phase(a, r, 4 * a.L, xs, Out{nullptr, nullptr, e}, red, bv, bi, ph);
+    consume_phase(a, r, 4 * a.L, xq, parts, Out{nullptr, nullptr, e}, bv, bi, ph);
+    // Warp argmax (ties: lower index), then the warps' in order.
+    for (int o = 16; o > 0; o >>= 1) {
+      const float v2 = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
+      const int i2 = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+      if (v2 > bv || (v2 == bv && i2 < bi)) {
+        bv = v2;
+        bi = i2;
+      }
+    }
     if (lane == 0) {
       cbest_v[warp] = bv;
       cbest_i[warp] = bi;
     }
-    __syncthreads();
+    csync();
     if (threadIdx.x == 0) {
       float v = cbest_v[0];
       int i = cbest_i[0];
@@ -1164,7 +1304,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (lane == 0) cbest_i[0] = (i == 0x7FFFFFFF) ? 0 : i;
     }
-    __syncthreads();
+    csync();
     token = cbest_i[0];
     // Every CTA has published its partial after writing this step's K/V
     // rows (and a fence): the next step's attention reads them after this
@@ -1174,7 +1314,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       a.gen[step] = token;
     step++;
     pos++;
-    __syncthreads();
+    csync();
   }
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     *a.tok = token;
@@ -1209,12 +1349,40 @@ size_t select_attn_floats(int HD, int G) {
 }
 
 // Activation region, rounded to 128 bytes: the residual copy xraw [D]
-// (rounded to 32 floats), then the matvec input or the attention scratch.
-size_t act_bytes(int D, int QD, int Fl, int HD, int G) {
-  size_t k = (size_t)std::max(D, std::max(QD, Fl));
-  k = std::max(k, select_attn_floats(HD, G));
-  k += (size_t)(D + 31) / 32 * 32;
-  return (k * sizeof(float) + 127) / 128 * 128;
+// (rounded to 32 floats), two bf16 gain vectors [D] (same rounding), then
+// the matvec input (`parts` bf16 arrays of K + 32 columns) or the attention
+// scratch.
+size_t act_bytes(int D, int QD, int Fl, int HD, int G, int parts) {
+  const size_t kmax = (size_t)std::max(D, std::max(QD, Fl));
+  size_t bytes = std::max((size_t)parts * 2 * (kmax + 32), select_attn_floats(HD, G) * 4);
+  bytes += (size_t)(D + 31) / 32 * 32 * (4 + 2 * 2);  // xraw, two gain vectors
+  return (bytes + 127) / 128 * 128;
+}
+
+// Dynamic shared memory a CTA may take: the device's opt-in limit less the
+// kernel's static shared memory, rounded down to 1 KB.
+size_t smem_budget(int HD, int G) {
+  static size_t cached[3][4] = {};
+  const int hi = HD == 32 ? 0 : HD == 64 ? 1 : 2;
+  const int gi = G == 1 ? 0 : G == 2 ? 1 : G == 4 ? 2 : 3;
+  if (!cached[hi][gi]) {
+    cudaFuncAttributes fa;
+    SG_CUDA(cudaFuncGetAttributes(&fa, select(HD, G)));
+    int dev = 0, optin = 0;
+    SG_CUDA(cudaGetDevice(&dev));
+    SG_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    const size_t lim = (size_t)optin > fa.sharedSizeBytes ? (size_t)optin - fa.sharedSizeBytes : 0;
+    cached[hi][gi] = lim / 1024 * 1024;
+  }
+  return cached[hi][gi];
+}
+
+// Three activation parts (fp32-faithful) when the weight buffers keep at
+// least 40 KB each (64 rows by 256 columns and more); two (x to about
+// 2^-16) otherwise.
+int act_parts(int D, int QD, int Fl, int HD, int G) {
+  return act_bytes(D, QD, Fl, HD, G, 3) + (size_t)kRing * 40 * 1024 <= smem_budget(HD, G) ? 3
+                                                                                          : 2;
 }
 
 }  // namespace
@@ -1231,17 +1399,21 @@ MegaFlagged mega_flagged_layout(int D, int QKVl, int QD, int Fl, int L, int grid
   return f;
 }
 
-// Ring buffers take what the activations leave of the budget.
+// Ring buffers take what the activations leave of the budget. Every row
+// length (D, QD, Fl) must be a multiple of 32 columns.
 size_t mega_smem_bytes(int D, int QD, int Fl, int HD, int G) {
-  if (D > kNormRegs * kThreads) return 0;
-  const size_t act = act_bytes(D, QD, Fl, HD, G);
-  if (act + (size_t)kRing * 8 * 1024 > kSmemBudget) return 0;
-  size_t buf = (kSmemBudget - act) / kRing / 1024 * 1024;
+  if (!select(HD, G)) return 0;
+  if (D > kNormMaxK) return 0;
+  if (D % 32 || QD % 32 || Fl % 32) return 0;
+  const size_t act = act_bytes(D, QD, Fl, HD, G, act_parts(D, QD, Fl, HD, G));
+  const size_t budget = smem_budget(HD, G);
+  if (act + (size_t)kRing * 16 * 1024 > budget) return 0;
+  size_t buf = (budget - act) / kRing / 1024 * 1024;
   return (size_t)kRing * buf + act;
 }
 
 static int buffer_bytes(size_t smem, int D, int QD, int Fl, int HD, int G) {
-  return (int)((smem - act_bytes(D, QD, Fl, HD, G)) / kRing);
+  return (int)((smem - act_bytes(D, QD, Fl, HD, G, act_parts(D, QD, Fl, HD, G))) / kRing);
 }
 
 void mega_configure(size_t smem) {
@@ -1255,7 +1427,7 @@ int mega_grid(size_t smem, int HD, int G) {
   void* k = select(HD, G);
   if (!k || smem == 0) return 0;
   int per_sm = 0;
-  SG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, smem));
+  SG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kBlockThreads, smem));
   if (per_sm < 1) return 0;
   int dev, sms;
   SG_CUDA(cudaGetDevice(&dev));
@@ -1279,10 +1451,11 @@ void mega_decode(const MegaArgs& a, int grid, size_t smem, cudaStream_t s) {
   if (a.nsplit > kMaxSplits) SG_DIE("megakernel: too many attention splits");
   if (a.L > kMaxLayers) SG_DIE("megakernel: too many layers");
   int buf = buffer_bytes(smem, a.D, a.QHl * a.HD, a.Fl, a.HD, a.G);
-  if (buf < 8 * 1024 || buf % 16) SG_DIE("megakernel: weight buffers too small");
+  if (buf < 16 * 1024 || buf % 1024) SG_DIE("megakernel: weight buffers too small");
+  int parts = act_parts(a.D, a.QHl * a.HD, a.Fl, a.HD, a.G);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(kBlockThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -1290,7 +1463,7 @@ void mega_decode(const MegaArgs& a, int grid, size_t smem, cudaStream_t s) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  void* args[] = {(void*)&a, (void*)&buf};
+  void* args[] = {(void*)&a, (void*)&buf, (void*)&parts};
   SG_CUDA(cudaLaunchKernelExC(&cfg, k, args));
 }
 

@@ -20,9 +20,10 @@
 // Warp roles (6 warps): 0 TMA producer, 1 MMA issuer (one elected thread
 // each), 2..5 epilogue (each reads the 32 TMEM lanes of its quarter with
 // tcgen05.ld, applies STORE / ADD / SwiGLU and writes C coalesced along r).
-// Launched with programmatic dependent launch: the weight tiles of the first
-// stages are requested before griddepcontrol.wait, i.e. while the kernel
-// that produces the activations is still finishing.
+// Launched with programmatic dependent launch: for weights no earlier kernel
+// writes, the tiles of the first stages are requested before
+// griddepcontrol.wait, i.e. while the kernel that produces the activations
+// is still finishing.
 // Every wait is bounded: a timeout sets *err and the CTA finishes without
 // touching C further; the host reports the error.
 #include "common.cuh"
@@ -174,6 +175,8 @@ struct TcParams {
   int ldc;
   int epi;     // EPI_STORE / EPI_ADD / EPI_SWIGLU (C has N/2 columns)
   int* err;
+  int w_early; // 1: no earlier kernel writes W, its first tiles may load
+               // before the dependency wait
 };
 
 template <int BN>
@@ -213,10 +216,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   pdl_trigger();
 
   if (warp == 0) {
-    // TMA producer (one thread). Weights are not written by earlier kernels:
-    // the first stages' weight tiles go out before the dependency wait.
+    // TMA producer (one thread). When no earlier kernel writes the weights
+    // (w_early), the first stages' weight tiles go out before the
+    // dependency wait.
     if (lane == 0) {
-      const int pre = nk < STAGES ? nk : STAGES;
+      const int pre = p.w_early ? (nk < STAGES ? nk : STAGES) : 0;
       for (int kb = 0; kb < pre; kb++) {
         const uint32_t fb = saddr(&full_bar[kb]);
         mbar_expect_tx(fb, C::kStageBytes);
@@ -227,8 +231,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = kb % STAGES;
         const uint32_t st = sbase + s * C::kStageBytes;
         const uint32_t fb = saddr(&full_bar[s]);
-        if (kb >= STAGES) {
-          if (!mbar_wait(saddr(&empty_bar[s]), ((kb / STAGES) - 1) & 1, p.err)) break;
+        if (kb >= pre) {
+          if (kb >= STAGES &&
+              !mbar_wait(saddr(&empty_bar[s]), ((kb / STAGES) - 1) & 1, p.err))
+            break;
           mbar_expect_tx(fb, C::kStageBytes);
           tma_load_2d(st, &tmW, kb * BK, r0, fb);
         }
@@ -419,11 +425,11 @@ int tc_width(int rows, int T) {
 }
 
 void tc_gemm(const TcMap& w, const TcAct& a, int T, float* C, int ldc, Epilogue epi, int* err,
-             cudaStream_t s) {
+             cudaStream_t s, bool w_early) {
   if (w.K != a.hi[0].K) SG_DIE("tensor-core GEMM: K mismatch");
   if (T > a.hi[0].rows) SG_DIE("tensor-core GEMM: more tokens than the activation map holds");
   if (T <= 0) return;
-  const TcParams p{T, w.rows, w.K, C, ldc, (int)epi, err};
+  const TcParams p{T, w.rows, w.K, C, ldc, (int)epi, err, w_early ? 1 : 0};
   const int bn = tc_width(w.rows, T);
   if (bn == 128)
     launch_bn<128>(w, a, 2, p, s);

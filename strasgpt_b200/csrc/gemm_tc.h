@@ -40,9 +40,12 @@ void tc_split(const float* x, int ldx, int T, int K, uint16_t* hi, uint16_t* lo,
 // C[t][r] (op)= sum_k (A_hi + A_lo)[t][k] W[r][k] for t < T, r < w.rows.
 // For EPI_SWIGLU, w holds gate/up rows interleaved and C has w.rows/2
 // columns. `err` (device int, zero at rest) is set if a pipeline wait times
-// out; the caller checks it.
+// out; the caller checks it. `w_early`: no kernel launched before this one
+// on the stream writes w (model weights), so its first tiles may be
+// requested before the wait for that kernel; false when an earlier kernel
+// produces w (dequantised experts, caller-owned buffers).
 void tc_gemm(const TcMap& w, const TcAct& a, int T, float* C, int ldc, Epilogue epi, int* err,
-             cudaStream_t s);
+             cudaStream_t s, bool w_early = true);
 
 // Token-tile width tc_gemm uses for `rows` weight rows and T tokens.
 int tc_width(int rows, int T);

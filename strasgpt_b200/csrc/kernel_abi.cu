@@ -64,7 +64,7 @@ int strasgpt_k_gemm_tc(const float* a, int lda, uint16_t* a_hi,
   sg::tc_make_map(&mw, w, n, k);
   sg::tc_make_act(&act, a_hi, a_lo, m, k);
   sg::tc_split(a, lda, m, k, a_hi, a_lo, s);
-  sg::tc_gemm(mw, act, m, c, ldc, epilogue(epi), err, s);
+  sg::tc_gemm(mw, act, m, c, ldc, epilogue(epi), err, s, false);
   SG_CUDA(cudaGetLastError());
   return 0;
 }

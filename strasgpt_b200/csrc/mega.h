@@ -67,14 +67,18 @@ struct MegaArgs {
   int steps;
   int write_logits;
   // Optional (null = off): per phase and CTA, kMegaTraceWidth %globaltimer
-  // stamps [phase][cta][w]: stage start, inputs complete, input staged,
-  // first weight chunk ready, phase consumed, last chunk computed, next copy
-  // issued; for the first `trace_phases` phases of the launch.
+  // records [phase][cta][w]: stage start, inputs complete, input staged,
+  // first weight chunk ready, phase consumed, then the phase's ns spent
+  // waiting for weight buffers, on its chunks in total, on warp 0's dot
+  // products, and on the cross-warp sums and epilogues, then the times the
+  // RMSNorm sum of squares was complete, the normalised input written and
+  // the staging barrier passed, and the gains were resident; for the first
+  // `trace_phases` phases.
   unsigned long long* trace;
   int trace_phases;
 };
 
-constexpr int kMegaTraceWidth = 7;
+constexpr int kMegaTraceWidth = 13;
 
 // Dynamic shared memory the megakernel needs for these dimensions.
 size_t mega_smem_bytes(int D, int QD, int Fl, int HD, int G);

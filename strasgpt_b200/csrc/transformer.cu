@@ -905,12 +905,13 @@ struct Runner {
           sg::moe_gather_split(s->xn, D, s->moe_perm + off, k, n, s->a_hi, s->a_lo, st);
         });
         launch(FAM_OTHER, 0, [&] {
-          sg::tc_gemm(s->tc_w[4 * w->L + 1], s->in[0], n, s->h, F, sg::EPI_SWIGLU, s->tc_err, st);
+          sg::tc_gemm(s->tc_w[4 * w->L + 1], s->in[0], n, s->h, F, sg::EPI_SWIGLU, s->tc_err, st,
+                      false);
         });
         launch(FAM_OTHER, 0, [&] { sg::tc_split(s->h, F, n, F, s->a_hi, s->a_lo, st); });
         launch(FAM_OTHER, 0, [&] {
           sg::tc_gemm(s->tc_w[4 * w->L + 2], s->in[2], n, s->moe_y + (size_t)off * D, D,
-                      sg::EPI_STORE, s->tc_err, st);
+                      sg::EPI_STORE, s->tc_err, st, false);
         });
       }
       off += n;
