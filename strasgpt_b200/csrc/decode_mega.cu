@@ -681,8 +681,8 @@ __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const uint16_t
   const Slice s = s_slices[phs.kind];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, c = lane & 3;
-  const uint4* xq4 = reinterpret_cast<const uint4*>(xq) + (size_t)g * (xq_stride(phs.K) / 8);
-  const bool has_x = g < parts;
+  const int xps = xq_stride(phs.K) / 8;  // uint4 per activation part
+  const uint4* xq4 = reinterpret_cast<const uint4*>(xq);
   const bool tr = a.trace != nullptr;
   unsigned long long t_wait = 0, t_dot = 0, t_red = 0, t0 = 0;
   for (int ci = 0; ci < s.nchunks; ci++) {
@@ -697,9 +697,19 @@ __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const uint16_t
     if (ci == 0) trace_mark(a, ph, MARK_READY);
     const Chunk ch = slice_chunk(s, phs, ci);
     const int nr = ch.r1 - ch.r0;
-    const int ng = (nr + 15) >> 4;
     const int stride = row_stride(ch.k1 - ch.k0);
     const int nkb = (ch.k1 - ch.k0) >> 5;
+    // Folded chunk (at most 8 whole rows): fragment rows 8..15 are the same
+    // rows over the second half of the columns, and B carries the parts of
+    // both halves (columns p and parts + p), so each warp walks half as many
+    // 32-column blocks.
+    const bool fold = nr <= 8 && ch.first_seg && ch.last_seg && (nkb & 1) == 0;
+    const int nkw = fold ? nkb >> 1 : nkb;  // blocks walked
+    const int ng = fold ? 1 : (nr + 15) >> 4;
+    const int xhalf = fold && g >= parts;    // B column g: part g - parts, second half
+    const bool has_x = g < (fold ? 2 * parts : parts);
+    const uint4* xsrc = xq4 + (size_t)(g - xhalf * parts) * xps +
+                        (size_t)(((ch.k0 >> 5) + xhalf * nkw) * 4 + c);
     float acc[kMaxChunkRows / 16][2][4];
 #pragma unroll
     for (int q = 0; q < kMaxChunkRows / 16; q++)
@@ -711,13 +721,18 @@ __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const uint16_t
     // group q (rows past the chunk read its last row), 8 columns at
     // 8 (lane / 16) of the 16-column step.
     const uint32_t bbase = smem_addr(r.base + (size_t)b * r.buf_bytes) + (uint32_t)((lane >> 4) * 16);
+    const int m = (lane & 7) + ((lane >> 3) & 1) * 8;  // fragment row of this lane's address
     uint32_t lrow[kMaxChunkRows / 16];
+    if (fold) {
+      lrow[0] = bbase + (uint32_t)(min(m & 7, nr - 1) * stride + (m >> 3) * nkw * 64);
+    } else {
 #pragma unroll
-    for (int q = 0; q < kMaxChunkRows / 16; q++)
-      lrow[q] = bbase + (uint32_t)(min(q * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, nr - 1) * stride);
-    for (int kb = warp; kb < nkb; kb += kWarps) {
+      for (int q = 0; q < kMaxChunkRows / 16; q++)
+        lrow[q] = bbase + (uint32_t)(min(q * 16 + m, nr - 1) * stride);
+    }
+    for (int kb = warp; kb < nkw; kb += kWarps) {
       uint4 xb = make_uint4(0u, 0u, 0u, 0u);
-      if (has_x) xb = xq4[(size_t)(((ch.k0 >> 5) + kb) * 4 + c)];
+      if (has_x) xb = xsrc[(size_t)kb * 4];
 #pragma unroll
       for (int q = 0; q < kMaxChunkRows / 16; q++) {
         if (q < ng) {
@@ -736,8 +751,29 @@ __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const uint16_t
     // sums go to (or, for later column segments, add to) its red row.
     float* red = r.red + (size_t)(r.nred & 1) * kWarps * kMaxChunkRows;
     float* wred = red + warp * kMaxChunkRows;
+    if (fold) {
+      // Row g: columns 0..parts-1 of fragment row g (first half) plus
+      // columns parts..2 parts-1 of fragment row g + 8 (second half).
+      const float c0 = acc[0][0][0] + acc[0][1][0], c1 = acc[0][0][1] + acc[0][1][1];
+      const float c2 = acc[0][0][2] + acc[0][1][2], c3 = acc[0][0][3] + acc[0][1][3];
+      const float n1c0 = __shfl_down_sync(0xFFFFFFFFu, c0, 1);
+      const float n1c1 = __shfl_down_sync(0xFFFFFFFFu, c1, 1);
+      const float n1c3 = __shfl_down_sync(0xFFFFFFFFu, c3, 1);
+      const float n1c2 = __shfl_down_sync(0xFFFFFFFFu, c2, 1);
+      const float n2c2 = __shfl_down_sync(0xFFFFFFFFu, c2, 2);
+      const float n2c3 = __shfl_down_sync(0xFFFFFFFFu, c3, 2);
+      if (c == 0) {
+        // parts == 3: first half = C[g][0..2], second = C[g+8][3..5];
+        // parts == 2: first half = C[g][0..1], second = C[g+8][2..3].
+        const float v = (parts == 3) ? ((c0 + c1) + n1c0) + (n1c3 + (n2c2 + n2c3))
+                                     : (c0 + c1) + (n1c2 + n1c3);
+        (void)n1c1;
+        wred[g] = v;
+      }
+    }
 #pragma unroll
     for (int q = 0; q < kMaxChunkRows / 16; q++) {
+      if (fold) break;
       if (q < ng) {
         const float c0 = acc[q][0][0] + acc[q][1][0], c1 = acc[q][0][1] + acc[q][1][1];
         const float c2 = acc[q][0][2] + acc[q][1][2], c3 = acc[q][0][3] + acc[q][1][3];
@@ -1021,6 +1057,7 @@ __device__ void attn_item(const MegaArgs& a, const MegaLayer& ly, int l, int kh,
       m[g] = mn;
     }
   }
+  trace_mark(a, ph, MARK_NORMED);  // attention: scores and P.V done
   csync();  // the q/k warps' scratch use of wacc is over
 #pragma unroll
   for (int g = 0; g < G; g++) {
@@ -1056,6 +1093,7 @@ __device__ void attn_item(const MegaArgs& a, const MegaLayer& ly, int l, int kh,
     }
     P[4 + dd] = A;
   }
+  trace_mark(a, ph, MARK_SCALED);  // attention: split record written
   __threadfence();
   csync();
   trace_mark(a, ph, MARK_STAGED);
