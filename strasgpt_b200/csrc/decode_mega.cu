@@ -838,6 +838,25 @@ __device__ void tp_reduce_rows(const MegaArgs& a, const float* xraw, size_t part
 // ---------------------------------------------------------------------------
 // Attention
 // ---------------------------------------------------------------------------
+// Lane `lane`'s V values of one cache row (elements lane * V .. + V - 1),
+// one vector load from L2.
+template <int V>
+__device__ __forceinline__ void load_vrow(const float* row, int lane, float* out) {
+  if constexpr (V == 4) {
+    const float4 t = __ldcg(reinterpret_cast<const float4*>(row) + lane);
+    out[0] = t.x;
+    out[1] = t.y;
+    out[2] = t.z;
+    out[3] = t.w;
+  } else if constexpr (V == 2) {
+    const float2 t = __ldcg(reinterpret_cast<const float2*>(row) + lane);
+    out[0] = t.x;
+    out[1] = t.y;
+  } else {
+    out[0] = __ldcg(row + lane);
+  }
+}
+
 // The per-lane factors head_norm_rope needs for position `pos` (rope table
 // entries and norm gains), loaded before the head's values are waited for.
 template <int HD>
@@ -963,7 +982,19 @@ __device__ void attn_item(const MegaArgs& a, const MegaLayer& ly, int l, int kh,
   const u64* qkv = a.ll + a.llo.qkv + (size_t)l * a.QKVl;
 
   // The cache rows below `pos` were written in earlier steps (made visible
-  // by the fence at the top of the step).
+  // by the fence at the top of the step): the K rows of the warp's first 8
+  // positions go into registers before the wait for this step's q, k and v.
+  const int j = lane >> 2, qd = lane & 3;
+  const int base0 = s_begin + warp * 8;
+  float4 kv[QF];
+  {
+    const int s = base0 + j;
+    if (s < pos) {
+      const float4* kr = reinterpret_cast<const float4*>(kb + (size_t)s * HD);
+#pragma unroll
+      for (int i = 0; i < QF; i++) kv[i] = __ldcg(kr + qd + 4 * i);
+    }
+  }
   if (warp < G) {
     HeadFactors<HD> f;
     load_head_factors<HD>(a, ly.q_norm, pos, f);
@@ -993,16 +1024,17 @@ __device__ void attn_item(const MegaArgs& a, const MegaLayer& ly, int l, int kh,
 #pragma unroll
     for (int v = 0; v < V; v++) acc[g][v] = 0.f;
   }
-  const int j = lane >> 2, qd = lane & 3;
   const float div = sqrtf((float)HD);
-  for (int base = s_begin + warp * 8; base < s_end; base += kPosPerPass) {
+  for (int base = base0; base < s_end; base += kPosPerPass) {
     const int s = base + j;
     const bool valid = s < s_end;
     float d[G];
 #pragma unroll
     for (int g = 0; g < G; g++) d[g] = 0.f;
-    float4 kv[QF];
-    if (valid) {
+    // K rows not loaded yet: all of them after the first pass, the row at
+    // `pos` (appended above) in the first.
+    const int lo = (base == base0) ? pos : base;
+    if (valid && s >= lo) {
       const float4* kr = reinterpret_cast<const float4*>(kb + (size_t)s * HD);
 #pragma unroll
       for (int i = 0; i < QF; i++) kv[i] = __ldcg(kr + qd + 4 * i);
@@ -1011,9 +1043,12 @@ __device__ void attn_item(const MegaArgs& a, const MegaLayer& ly, int l, int kh,
 #pragma unroll
     for (int jj = 0; jj < 8; jj++) {
       const int sj = base + jj;
+      if (sj < s_end) {
+        load_vrow<V>(vb + (size_t)sj * HD, lane, vv[jj]);
+      } else {
 #pragma unroll
-      for (int v = 0; v < V; v++)
-        vv[jj][v] = (sj < s_end) ? __ldcg(vb + (size_t)sj * HD + lane * V + v) : 0.f;
+        for (int v = 0; v < V; v++) vv[jj][v] = 0.f;
+      }
     }
     if (valid) {
 #pragma unroll
@@ -1104,42 +1139,50 @@ __device__ void attn_item(const MegaArgs& a, const MegaLayer& ly, int l, int kh,
   }
   csync();
   if (!*is_last) return;
+  trace_mark(a, ph, MARK_SYNCED);  // attention: this CTA merges
   __threadfence();
   // Merge: att = sum_j c_j acc_j / sum_j c_j l_j, c_j = exp(m_j - max m);
-  // splits without positions have m = -inf.
-  for (int g = warp; g < G; g += kWarps) {
-    const float* P0 = part + (size_t)(kh * G + g) * nsplit * (HD + 4);
-    float mloc = -INFINITY;
-    for (int jx = lane; jx < nsplit; jx += 32)
-      mloc = fmaxf(mloc, __ldcg(P0 + (size_t)jx * (HD + 4)));
-    const float M = warp_max(mloc);
-    float ls = 0.f;
-    for (int jx = lane; jx < nsplit; jx += 32) {
-      const float mj = __ldcg(P0 + (size_t)jx * (HD + 4));
-      const float c = (mj == -INFINITY) ? 0.f : expf(mj - M);
-      cw[g * kMaxSplits + jx] = c;
-      ls += c * __ldcg(P0 + (size_t)jx * (HD + 4) + 1);
-    }
-    ls = warp_sum(ls);
-    if (lane == 0) Ls[g] = ls;
-  }
-  csync();
+  // splits without positions have m = -inf. Each thread merges one output
+  // element and loads the m, l and acc words of up to kMergeBatch splits at
+  // once (one L2 round trip per batch); later batches rescale the running
+  // sums to the new maximum.
+  constexpr int kMergeBatch = 16;
   u64* att = a.ll + a.llo.att + (size_t)l * a.QHl * HD;
   for (int ei = tid; ei < G * HD; ei += kThreads) {
     const int g = ei / HD, dd = ei % HD;
-    const float* P0 = part + (size_t)(kh * G + g) * nsplit * (HD + 4) + 4 + dd;
-    float A = 0.f;
-    for (int j0 = 0; j0 < nsplit; j0 += 8) {
-      float pv[8];  // the loads of a batch go out together
+    const float* P0 = part + (size_t)(kh * G + g) * nsplit * (HD + 4);
+    float M = -INFINITY, Ls = 0.f, A = 0.f;
+    for (int j0 = 0; j0 < nsplit; j0 += kMergeBatch) {
+      float mj[kMergeBatch], lj[kMergeBatch], aj[kMergeBatch];
 #pragma unroll
-      for (int u = 0; u < 8; u++)
-        pv[u] = (j0 + u < nsplit) ? __ldcg(P0 + (size_t)(j0 + u) * (HD + 4)) : 0.f;
+      for (int u = 0; u < kMergeBatch; u++) {
+        const float* Pj = P0 + (size_t)(j0 + u) * (HD + 4);
+        const bool in = j0 + u < nsplit;
+        mj[u] = in ? __ldcg(Pj) : -INFINITY;
+        lj[u] = in ? __ldcg(Pj + 1) : 0.f;
+        aj[u] = in ? __ldcg(Pj + 4 + dd) : 0.f;
+      }
+      float Mb = M;
 #pragma unroll
-      for (int u = 0; u < 8; u++)
-        if (j0 + u < nsplit) A = fmaf(cw[g * kMaxSplits + j0 + u], pv[u], A);
+      for (int u = 0; u < kMergeBatch; u++) Mb = fmaxf(Mb, mj[u]);
+      if (Mb == -INFINITY) continue;
+      if (M != -INFINITY && M != Mb) {
+        const float r = expf(M - Mb);
+        Ls *= r;
+        A *= r;
+      }
+      M = Mb;
+#pragma unroll
+      for (int u = 0; u < kMergeBatch; u++) {
+        if (mj[u] == -INFINITY) continue;
+        const float c = expf(mj[u] - M);
+        Ls += c * lj[u];
+        A = fmaf(c, aj[u], A);
+      }
     }
-    ll_store(att + (size_t)(kh * G + g) * HD + dd, A / Ls[g], e);
+    ll_store(att + (size_t)(kh * G + g) * HD + dd, A / Ls, e);
   }
+  trace_mark(a, ph, MARK_GAINS);  // attention: merged output stored
   csync();
   trace_mark(a, ph, MARK_READY);
 }
@@ -1212,6 +1255,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   u64* am = a.ll + a.llo.am;
   const int nam = a.world * (int)gridDim.x;  // argmax partials of all ranks
 
+  prefetch_kv<HD>(a, 0, pos);
   for (int s = 0; s < a.steps; s++) {
     const unsigned e = a.epoch + (unsigned)s;
     for (int l = 0; l < a.L; l++) {
@@ -1220,7 +1264,12 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
       u64* x_d = x_o + a.D;                              // after down
       // QKV
       trace_mark(a, ph, MARK_BEGIN);
-      prefetch_kv<HD>(a, l, pos);
+      // The next layer's cache rows, a layer ahead of their use (this
+      // layer's were requested during the previous one).
+      if (l + 1 < a.L)
+        prefetch_kv<HD>(a, l + 1, pos);
+      else if (s + 1 < a.steps)
+        prefetch_kv<HD>(a, 0, pos + 1);
       prefetch_gains(a, l + 1);
       if (l == 0)
         stage_embedding(a, token, gs, 0, xq, parts, xraw, red);
