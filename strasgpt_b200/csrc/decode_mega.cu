@@ -950,17 +950,15 @@ __device__ void prefetch_gains(const MegaArgs& a, int l) {
 
 template <int HD, int G>
 constexpr int attn_floats() {
-  // qs [G][HD], wm/wl [kWarps][G], wacc [kWarps][G][HD], merge weights
-  // [G][kMaxSplits], denominators [G], last-CTA flag.
-  return G * HD + 2 * kWarps * G + kWarps * G * HD + G * kMaxSplits + G + 4;
+  // qs [G][HD], wm/wl [kWarps][G], wacc [kWarps][G][HD].
+  return G * HD + 2 * kWarps * G + kWarps * G * HD;
 }
 
 // One attention item: kv head kh, cache split sp, at position pos. Its q,
 // k and v come from the flagged qkv vector of layer l (epoch e). The split
 // holding `pos` appends this step's k and v to the cache. The split record
-// [m, l, -, -, acc[HD]] of each of the G query heads goes to attn_partial;
-// the last split of the kv head to finish (ticket) merges the records and
-// publishes the heads' attention output in the flagged att vector.
+// [m, l, acc[HD]] of each of the G query heads goes out as flagged words
+// (rec vector); merge_item combines the records of a kv head.
 template <int HD, int G>
 __device__ void attn_item(const MegaArgs& a, const MegaLayer& ly, int l, int kh, int sp,
                           int pos, unsigned e, float* sm, int ph) {
@@ -970,9 +968,6 @@ __device__ void attn_item(const MegaArgs& a, const MegaLayer& ly, int l, int kh,
   float* wm = qs + G * HD;             // [kWarps][G]
   float* wl = wm + kWarps * G;         // [kWarps][G]
   float* wacc = wl + kWarps * G;       // [kWarps][G][HD]
-  float* cw = wacc + kWarps * G * HD;  // [G][kMaxSplits]
-  float* Ls = cw + G * kMaxSplits;     // [G]
-  int* is_last = reinterpret_cast<int*>(Ls + G);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const size_t layer_off = (size_t)l * a.KHl * a.ctx * HD;
   float* kb = a.kc + layer_off + (size_t)kh * a.ctx * HD;
@@ -1104,8 +1099,8 @@ __device__ void attn_item(const MegaArgs& a, const MegaLayer& ly, int l, int kh,
     for (int v = 0; v < V; v++) wacc[((size_t)warp * G + g) * HD + lane * V + v] = acc[g][v];
   }
   csync();
-  const int nsplit = a.nsplit;
-  float* part = a.attn_partial + (size_t)l * a.QHl * nsplit * (HD + 4);
+  // The split record of each query head, as flagged words.
+  u64* rec = a.ll + a.llo.rec + (((size_t)l * a.KHl + kh) * a.nsplit + sp) * G * (HD + 2);
   for (int ei = tid; ei < G * HD; ei += kThreads) {
     const int g = ei / HD, dd = ei % HD;
     float M = -INFINITY;
@@ -1120,48 +1115,79 @@ __device__ void attn_item(const MegaArgs& a, const MegaLayer& ly, int l, int kh,
         A += wacc[((size_t)w * G + g) * HD + dd] * c;
       }
     }
-    // Split record: [m, l, -, -, acc[HD]] (16-byte aligned acc).
-    float* P = part + ((size_t)(kh * G + g) * nsplit + sp) * (HD + 4);
+    u64* R = rec + (size_t)g * (HD + 2);
     if (dd == 0) {
-      P[0] = M;
-      P[1] = L;
+      ll_store(R, M, e);
+      ll_store(R + 1, L, e);
     }
-    P[4 + dd] = A;
+    ll_store(R + 2 + dd, A, e);
   }
   trace_mark(a, ph, MARK_SCALED);  // attention: split record written
-  __threadfence();
-  csync();
+  csync();  // the scratch (qs, wm, wl, wacc) is free for the next item
   trace_mark(a, ph, MARK_STAGED);
-  if (tid == 0) {
-    int* ticket = a.attn_ticket + (size_t)l * a.KHl + kh;
-    *is_last = (atomicAdd(ticket, 1) == nsplit - 1);
-    if (*is_last) *ticket = 0;  // its next use is in a later step
-  }
-  csync();
-  if (!*is_last) return;
-  trace_mark(a, ph, MARK_SYNCED);  // attention: this CTA merges
-  __threadfence();
-  // Merge: att = sum_j c_j acc_j / sum_j c_j l_j, c_j = exp(m_j - max m);
-  // splits without positions have m = -inf. Each thread merges one output
-  // element and loads the m, l and acc words of up to kMergeBatch splits at
-  // once (one L2 round trip per batch); later batches rescale the running
-  // sums to the new maximum.
-  constexpr int kMergeBatch = 16;
-  u64* att = a.ll + a.llo.att + (size_t)l * a.QHl * HD;
-  for (int ei = tid; ei < G * HD; ei += kThreads) {
-    const int g = ei / HD, dd = ei % HD;
-    const float* P0 = part + (size_t)(kh * G + g) * nsplit * (HD + 4);
-    float M = -INFINITY, Ls = 0.f, A = 0.f;
-    for (int j0 = 0; j0 < nsplit; j0 += kMergeBatch) {
-      float mj[kMergeBatch], lj[kMergeBatch], aj[kMergeBatch];
+}
+
+// Waits for the flagged words m, l and acc[dd] of `count` split records
+// (at most N) starting at base, `stride` words apart, and returns their
+// values; all loads of a round go out together.
+template <int N>
+__device__ __forceinline__ void ll_gather_rec(const MegaArgs& a, const u64* base, int stride,
+                                              int count, int dd, unsigned e, float* m, float* l,
+                                              float* acc) {
+  u64 w[3 * N];
 #pragma unroll
-      for (int u = 0; u < kMergeBatch; u++) {
-        const float* Pj = P0 + (size_t)(j0 + u) * (HD + 4);
-        const bool in = j0 + u < nsplit;
-        mj[u] = in ? __ldcg(Pj) : -INFINITY;
-        lj[u] = in ? __ldcg(Pj + 1) : 0.f;
-        aj[u] = in ? __ldcg(Pj + 4 + dd) : 0.f;
-      }
+  for (int u = 0; u < N; u++) {
+    const u64* R = base + (size_t)u * stride;
+    const bool in = u < count;
+    w[3 * u] = in ? ll_load(R) : ((u64)e << 32 | __float_as_uint(-INFINITY));
+    w[3 * u + 1] = in ? ll_load(R + 1) : ((u64)e << 32);
+    w[3 * u + 2] = in ? ll_load(R + 2 + dd) : ((u64)e << 32);
+  }
+  unsigned long long pending = 0;
+#pragma unroll
+  for (int i = 0; i < 3 * N; i++)
+    if (!ll_ready(w[i], e)) pending |= 1ull << i;
+  Spin sp;
+  while (pending) {
+    if (!spin_on(a, sp)) break;
+#pragma unroll
+    for (int u = 0; u < N; u++) {
+      const u64* R = base + (size_t)u * stride;
+      if (pending & (1ull << (3 * u))) w[3 * u] = ll_load(R);
+      if (pending & (1ull << (3 * u + 1))) w[3 * u + 1] = ll_load(R + 1);
+      if (pending & (1ull << (3 * u + 2))) w[3 * u + 2] = ll_load(R + 2 + dd);
+    }
+#pragma unroll
+    for (int i = 0; i < 3 * N; i++)
+      if ((pending & (1ull << i)) && ll_ready(w[i], e)) pending &= ~(1ull << i);
+  }
+#pragma unroll
+  for (int u = 0; u < N; u++) {
+    m[u] = ll_value(w[3 * u]);
+    l[u] = ll_value(w[3 * u + 1]);
+    acc[u] = ll_value(w[3 * u + 2]);
+  }
+}
+
+// The attention output of kv head kh (its G query heads) at position pos:
+// att = sum_j c_j acc_j / sum_j c_j l_j over the splits holding positions
+// (c_j = exp(m_j - max m); splits of the kv head with positions <= pos).
+// Each thread merges one output element and waits for the words of up to
+// kMergeBatch splits at once; later batches rescale the running sums.
+template <int HD, int G>
+__device__ void merge_item(const MegaArgs& a, int l, int kh, int pos, unsigned e) {
+  constexpr int kMergeBatch = 12;
+  const int nact = min(a.nsplit, pos / a.split_len + 1);
+  const int stride = G * (HD + 2);
+  const u64* rec0 = a.ll + a.llo.rec + ((size_t)l * a.KHl + kh) * a.nsplit * stride;
+  u64* att = a.ll + a.llo.att + (size_t)l * a.QHl * HD;
+  for (int ei = threadIdx.x; ei < G * HD; ei += kThreads) {
+    const int g = ei / HD, dd = ei % HD;
+    float M = -INFINITY, Ls = 0.f, A = 0.f;
+    for (int j0 = 0; j0 < nact; j0 += kMergeBatch) {
+      float mj[kMergeBatch], lj[kMergeBatch], aj[kMergeBatch];
+      ll_gather_rec<kMergeBatch>(a, rec0 + (size_t)j0 * stride + (size_t)g * (HD + 2), stride,
+                                 nact - j0, dd, e, mj, lj, aj);
       float Mb = M;
 #pragma unroll
       for (int u = 0; u < kMergeBatch; u++) Mb = fmaxf(Mb, mj[u]);
@@ -1182,9 +1208,6 @@ __device__ void attn_item(const MegaArgs& a, const MegaLayer& ly, int l, int kh,
     }
     ll_store(att + (size_t)(kh * G + g) * HD + dd, A / Ls, e);
   }
-  trace_mark(a, ph, MARK_GAINS);  // attention: merged output stored
-  csync();
-  trace_mark(a, ph, MARK_READY);
 }
 
 // ---------------------------------------------------------------------------
@@ -1283,6 +1306,13 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
       trace_mark(a, ph, MARK_BEGIN);
       for (int it = blockIdx.x; it < attn_items; it += gridDim.x)
         attn_item<HD, G>(a, ly, l, it % a.KHl, it / a.KHl, pos, e, xs, ph);
+      // The merge of kv head kh runs on CTA (attn_items + kh) mod grid,
+      // idle during attention when the grid has room.
+      for (int kh = 0; kh < a.KHl; kh++)
+        if ((attn_items + kh) % (int)gridDim.x == (int)blockIdx.x) {
+          merge_item<HD, G>(a, l, kh, pos, e);
+          trace_mark(a, ph, MARK_READY);
+        }
       ph++;
       // O + residual
       trace_mark(a, ph, MARK_BEGIN);
@@ -1474,7 +1504,8 @@ int act_parts(int D, int QD, int Fl, int HD, int G) {
 
 }  // namespace
 
-MegaFlagged mega_flagged_layout(int D, int QKVl, int QD, int Fl, int L, int grid, int world) {
+MegaFlagged mega_flagged_layout(int D, int QKVl, int QD, int Fl, int L, int grid, int world,
+                                int nsplit, int HD) {
   MegaFlagged f;
   f.x = 0;
   f.qkv = f.x + (size_t)L * 2 * D;
@@ -1482,7 +1513,9 @@ MegaFlagged mega_flagged_layout(int D, int QKVl, int QD, int Fl, int L, int grid
   f.h = f.att + (size_t)L * QD;
   f.xpart = f.h + (size_t)L * Fl;
   f.am = f.xpart + (world > 1 ? (size_t)L * 2 * world * D : 0);
-  f.total = f.am + 2 * (size_t)world * grid;
+  f.rec = f.am + 2 * (size_t)world * grid;
+  // QD / HD query heads, each with one record per split.
+  f.total = f.rec + (size_t)L * (QD / HD) * nsplit * (HD + 2);
   return f;
 }
 

@@ -31,10 +31,12 @@ struct MegaFlagged {
   size_t h;      // [L][Fl]       SwiGLU output
   size_t xpart;  // [L][2][N][D]  every rank's partial o_proj / down rows (N > 1)
   size_t am;     // [2][N][grid]  per-CTA argmax value / global index of every rank
+  size_t rec;    // [L][KHl][nsplit][G][HD+2]  attention split records (m, l, acc)
   size_t total;
 };
 
-MegaFlagged mega_flagged_layout(int D, int QKVl, int QD, int Fl, int L, int grid, int world);
+MegaFlagged mega_flagged_layout(int D, int QKVl, int QD, int Fl, int L, int grid, int world,
+                                int nsplit, int HD);
 
 struct MegaArgs {
   int D, HD, QHl, KHl, G, Fl, Vl, L, QKVl, ctx;
@@ -48,8 +50,6 @@ struct MegaArgs {
   float* logits;            // [Vl]
   float* kc;                // [L][KHl][ctx][HD]
   float* vc;
-  float* attn_partial;      // [L][QHl][nsplit][HD+4]
-  int* attn_ticket;         // [L][KHl], zero at rest
   int nsplit, split_len;
   unsigned long long* ll;   // flagged vectors (layout: MegaFlagged)
   MegaFlagged llo;

@@ -569,10 +569,8 @@ void alloc_state(const W_t* w, const transformer_configuration_t* c, S_t* s) {
     s->mega_grid = sg::mega_grid(s->mega_smem, w->HD, w->G);
     if (s->mega_grid <= 0) s->use_mega = false;
   }
-  int max_split = s->nsplit;
   if (s->use_mega) {
     sg::mega_split(s->ctx, w->KHl, s->mega_grid, &s->mega_nsplit, &s->mega_split_len);
-    max_split = std::max(max_split, s->mega_nsplit);
     std::vector<sg::MegaLayer> ml(w->L);
     for (int l = 0; l < w->L; l++) {
       const Layer& y = w->layer[l];
@@ -593,7 +591,7 @@ void alloc_state(const W_t* w, const transformer_configuration_t* c, S_t* s) {
     // Flagged hand-off vectors, zero (epoch 0: never written) at rest. Under
     // tensor parallelism they live in the exchange buffer the ranks map.
     s->mega_llo = sg::mega_flagged_layout(w->D, w->QKVl, w->QHl * w->HD, w->Fl, w->L,
-                                          s->mega_grid, w->world);
+                                          s->mega_grid, w->world, s->mega_nsplit, w->HD);
     if (w->world == 1) {
       s->mega_ll = (unsigned long long*)dalloc(s->allocs, s->mega_llo.total * 8, nullptr);
       SG_CUDA(cudaMemset(s->mega_ll, 0, s->mega_llo.total * 8));
@@ -605,12 +603,11 @@ void alloc_state(const W_t* w, const transformer_configuration_t* c, S_t* s) {
                  s->use_mega ? s->mega_llo.total * 8 : 0);
     if (s->use_mega) s->mega_ll = (unsigned long long*)(s->tp.local + s->tp.extra_off);
   }
-  // Split records and tickets: one set for the per-op decode kernel, one
-  // per layer for the persistent kernel.
-  const size_t layers_of_records = s->use_mega ? (size_t)w->L : 1;
-  s->attn_partial = F32(layers_of_records * w->QHl * max_split * (HD + 4));
-  s->attn_ticket = I32(layers_of_records * w->KHl);
-  SG_CUDA(cudaMemset(s->attn_ticket, 0, layers_of_records * w->KHl * 4));
+  // Split records and tickets of the per-op decode kernel (the persistent
+  // kernel keeps its records among its flagged vectors).
+  s->attn_partial = F32((size_t)w->QHl * s->nsplit * (HD + 4));
+  s->attn_ticket = I32(w->KHl);
+  SG_CUDA(cudaMemset(s->attn_ticket, 0, (size_t)w->KHl * 4));
   s->am_val = F32(1024);
   s->am_idx = I32(1024);
   s->am_ticket = I32(1);
@@ -826,7 +823,6 @@ struct Runner {
     a.pair_stride = (int)c->rope_pair_stride;
     a.logits = s->logits;
     a.kc = s->kc; a.vc = s->vc;
-    a.attn_partial = s->attn_partial; a.attn_ticket = s->attn_ticket;
     a.nsplit = s->mega_nsplit; a.split_len = s->mega_split_len;
     a.ll = s->mega_ll; a.llo = s->mega_llo; a.epoch = s->mega_epoch;
     a.rank = w->rank; a.world = w->world;
