@@ -28,7 +28,7 @@
 // pairs, so a CTA's weights for the whole launch form a fixed list of
 // chunks (up to 64 rows by a column range, one shared-memory buffer each).
 // A ninth warp is the producer: it walks that list and, for each of the
-// kRing buffers, waits until the consumers have released the buffer (empty
+// ring buffers, waits until the consumers have released the buffer (empty
 // mbarrier), then copies the chunk's rows into it with one cp.async.bulk per
 // row (into its own CTA's buffer only), completion counted on the buffer's
 // full mbarrier. Rows sit kPad bytes further apart than in memory, so the
@@ -66,7 +66,7 @@ constexpr int kBlockThreads = kThreads + 32;  // + the producer warp
 constexpr int kPosPerPass = kWarps * 8;  // cache rows per CTA pass
 constexpr int kMaxChunkRows = 64;        // rows per weight chunk (4 fragments)
 constexpr int kPad = 16;                 // extra bytes per row in a buffer
-constexpr int kRing = 2;                 // weight buffers per CTA
+constexpr int kMaxRing = 4;              // weight buffers per CTA (at most)
 constexpr int kMaxSplits = 64;
 constexpr int kTpMaxWorld = 8;
 constexpr unsigned long long kTimeoutNs = 2000000000ULL;
@@ -337,8 +337,10 @@ __device__ __forceinline__ Slice cta_slice(const Phase& ph, int buf_bytes) {
   const int n = s.re - s.rb;
   // Whole rows, as many as the slice has up to kMaxChunkRows and what a
   // buffer holds, when that is at least 16 rows (or the whole slice); else
-  // up to kMaxChunkRows rows by equal column segments (multiples of 256
-  // columns).
+  // row segments of kSegCols columns (each row segment is one bulk copy:
+  // long segments keep the copy count per byte low), as many rows as a
+  // buffer holds, the columns split into equal segments (multiples of 256).
+  constexpr int kSegCols = 1024;
   const int want = min(kMaxChunkRows, max(n, 2));
   const int whole = min(want, (buf_bytes / row_stride(ph.K)) & ~1);
   if (whole >= min(16, want)) {
@@ -346,8 +348,8 @@ __device__ __forceinline__ Slice cta_slice(const Phase& ph, int buf_bytes) {
     s.kseg = ph.K;
     s.spp = 1;
   } else {
-    s.rows = min(want, (buf_bytes / row_stride(256)) & ~1);
-    const int kmax = ((buf_bytes / s.rows - kPad) / 2) / 256 * 256;
+    const int kmax = min(kSegCols, ph.K);
+    s.rows = max(2, min(want, (buf_bytes / row_stride(kmax)) & ~1));
     s.spp = (ph.K + kmax - 1) / kmax;
     s.kseg = ((ph.K + s.spp - 1) / s.spp + 255) / 256 * 256;
   }
@@ -409,11 +411,11 @@ __device__ void wait_bar(const MegaArgs& a, uint64_t* bar, unsigned parity,
 }
 
 // The producer warp: copies every chunk of the launch, in the consumers'
-// order, into the ring. Chunk g goes to buffer g % kRing once the consumer
+// order, into the ring. Chunk g goes to buffer g % nbuf once the consumer
 // warps have released that buffer's previous chunk (empty[b]); its rows land
 // row_stride(k1 - k0) bytes apart. Stops issuing once the error flag is set;
 // before returning it waits (bounded) until its copies have landed.
-__device__ void produce(const MegaArgs& a, char* base, int buf_bytes, uint64_t* full,
+__device__ void produce(const MegaArgs& a, char* base, int buf_bytes, int nbuf, uint64_t* full,
                         uint64_t* empty) {
   const int lane = threadIdx.x & 31;
   Cursor c = {0, 0, 0};
@@ -421,9 +423,9 @@ __device__ void produce(const MegaArgs& a, char* base, int buf_bytes, uint64_t* 
   for (;;) {
     cursor_skip_empty(a, c);
     if (c.step >= a.steps) break;
-    const int b = (int)(g % kRing);
-    if (g >= (unsigned)kRing) {
-      if (lane == 0) wait_bar(a, empty + b, (g / kRing - 1) & 1, true, 128);
+    const int b = (int)(g % nbuf);
+    if (g >= (unsigned)nbuf) {
+      if (lane == 0) wait_bar(a, empty + b, (g / nbuf - 1) & 1, true, 128);
       __syncwarp();
     }
     if (*(volatile int*)a.err) break;
@@ -442,8 +444,8 @@ __device__ void produce(const MegaArgs& a, char* base, int buf_bytes, uint64_t* 
   }
   // The last use of each buffer: its copy has landed (or the wait ran out).
   if (lane == 0)
-    for (unsigned i = (g > (unsigned)kRing ? g - kRing : 0); i < g; i++)
-      wait_bar(a, full + i % kRing, (i / kRing) & 1, false);
+    for (unsigned i = (g > (unsigned)nbuf ? g - nbuf : 0); i < g; i++)
+      wait_bar(a, full + i % nbuf, (i / nbuf) & 1, false);
   __syncwarp();
 }
 
@@ -609,8 +611,9 @@ __device__ void stage_embedding(const MegaArgs& a, int token, Gains& gs, int gi,
 // ---------------------------------------------------------------------------
 struct Ring {
   char* base;      // buffer b starts at base + b * buf_bytes
-  uint64_t* full;  // [kRing]: the chunk in buffer b has landed
-  uint64_t* empty; // [kRing]: the consumer warps are done with buffer b
+  uint64_t* full;  // [nbuf]: the chunk in buffer b has landed
+  uint64_t* empty; // [nbuf]: the consumer warps are done with buffer b
+  int nbuf;
   int buf_bytes;
   unsigned g;      // chunks consumed so far
   unsigned nred;   // cross-warp reductions so far (selects the red half)
@@ -686,9 +689,9 @@ __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const uint16_t
   const bool tr = a.trace != nullptr;
   unsigned long long t_wait = 0, t_dot = 0, t_red = 0, t0 = 0;
   for (int ci = 0; ci < s.nchunks; ci++) {
-    const int b = (int)(r.g % kRing);
+    const int b = (int)(r.g % r.nbuf);
     if (tr) t0 = now_ns();
-    wait_bar(a, r.full + b, (r.g / kRing) & 1);
+    wait_bar(a, r.full + b, (r.g / r.nbuf) & 1);
     if (tr) {
       const unsigned long long t1 = now_ns();
       t_wait += t1 - t0;
@@ -1215,25 +1218,25 @@ __device__ void merge_item(const MegaArgs& a, int l, int kh, int pos, unsigned e
 // ---------------------------------------------------------------------------
 template <int HD, int G>
 __global__ void __launch_bounds__(kBlockThreads, 1)
-    k_mega_decode(const __grid_constant__ MegaArgs a, int buf_bytes, int parts) {
+    k_mega_decode(const __grid_constant__ MegaArgs a, int buf_bytes, int nbuf, int parts) {
   extern __shared__ __align__(128) char dyn[];
   __shared__ float red[32];
   __shared__ float cbest_v[kWarps];
   __shared__ int cbest_i[kWarps];
-  __shared__ __align__(8) uint64_t full_bar[kRing];
-  __shared__ __align__(8) uint64_t empty_bar[kRing];
+  __shared__ __align__(8) uint64_t full_bar[kMaxRing];
+  __shared__ __align__(8) uint64_t empty_bar[kMaxRing];
   __shared__ __align__(8) uint64_t gain_bar[2];
   __shared__ __align__(16) float mv_red[2 * kWarps * kMaxChunkRows];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int D32 = (a.D + 31) / 32 * 32;
-  float* xraw = reinterpret_cast<float*>(dyn + (size_t)kRing * buf_bytes);  // [D]
+  float* xraw = reinterpret_cast<float*>(dyn + (size_t)nbuf * buf_bytes);  // [D]
   uint16_t* gain_buf = reinterpret_cast<uint16_t*>(xraw + D32);              // [2][D]
   // Matvec input (bf16 parts) or attention scratch (floats).
   float* xs = reinterpret_cast<float*>(gain_buf + 2 * D32);
   uint16_t* xq = reinterpret_cast<uint16_t*>(xs);
   for (int i = threadIdx.x; i < a.L; i += kBlockThreads) s_layers[i] = a.layers[i];
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kRing; i++) {
+    for (int i = 0; i < nbuf; i++) {
       mbar_init(&full_bar[i], 1);
       mbar_init(&empty_bar[i], kWarps);
     }
@@ -1249,13 +1252,14 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   }
   __syncthreads();
   if (warp == kWarps) {
-    produce(a, dyn, buf_bytes, full_bar, empty_bar);
+    produce(a, dyn, buf_bytes, nbuf, full_bar, empty_bar);
     return;
   }
   Ring r;
   r.base = dyn;
   r.full = full_bar;
   r.empty = empty_bar;
+  r.nbuf = nbuf;
   r.buf_bytes = buf_bytes;
   r.g = 0;
   r.nred = 0;
@@ -1494,12 +1498,23 @@ size_t smem_budget(int HD, int G) {
   return cached[hi][gi];
 }
 
-// Three activation parts (fp32-faithful) when the weight buffers keep at
-// least 40 KB each (64 rows by 256 columns and more); two (x to about
-// 2^-16) otherwise.
+// Weight buffers of the ring (STRASGPT_MEGA_RING, 2..4; default 2).
+int ring_count() {
+  static int n = 0;
+  if (!n) {
+    const char* v = getenv("STRASGPT_MEGA_RING");
+    n = v ? atoi(v) : 2;
+    if (n < 2) n = 2;
+    if (n > kMaxRing) n = kMaxRing;
+  }
+  return n;
+}
+
+// Three activation parts (fp32-faithful) when the weight ring keeps at
+// least 128 KB; two (x to about 2^-17, as in the tensor-core prefill)
+// otherwise, so that large models keep enough weight bytes in flight.
 int act_parts(int D, int QD, int Fl, int HD, int G) {
-  return act_bytes(D, QD, Fl, HD, G, 3) + (size_t)kRing * 40 * 1024 <= smem_budget(HD, G) ? 3
-                                                                                          : 2;
+  return act_bytes(D, QD, Fl, HD, G, 3) + (size_t)128 * 1024 <= smem_budget(HD, G) ? 3 : 2;
 }
 
 }  // namespace
@@ -1527,13 +1542,14 @@ size_t mega_smem_bytes(int D, int QD, int Fl, int HD, int G) {
   if (D % 32 || QD % 32 || Fl % 32) return 0;
   const size_t act = act_bytes(D, QD, Fl, HD, G, act_parts(D, QD, Fl, HD, G));
   const size_t budget = smem_budget(HD, G);
-  if (act + (size_t)kRing * 16 * 1024 > budget) return 0;
-  size_t buf = (budget - act) / kRing / 1024 * 1024;
-  return (size_t)kRing * buf + act;
+  const int nbuf = ring_count();
+  if (act + (size_t)nbuf * 16 * 1024 > budget) return 0;
+  size_t buf = (budget - act) / nbuf / 1024 * 1024;
+  return (size_t)nbuf * buf + act;
 }
 
 static int buffer_bytes(size_t smem, int D, int QD, int Fl, int HD, int G) {
-  return (int)((smem - act_bytes(D, QD, Fl, HD, G, act_parts(D, QD, Fl, HD, G))) / kRing);
+  return (int)((smem - act_bytes(D, QD, Fl, HD, G, act_parts(D, QD, Fl, HD, G))) / ring_count());
 }
 
 void mega_configure(size_t smem) {
@@ -1583,7 +1599,8 @@ void mega_decode(const MegaArgs& a, int grid, size_t smem, cudaStream_t s) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  void* args[] = {(void*)&a, (void*)&buf, (void*)&parts};
+  int nbuf = ring_count();
+  void* args[] = {(void*)&a, (void*)&buf, (void*)&nbuf, (void*)&parts};
   SG_CUDA(cudaLaunchKernelExC(&cfg, k, args));
 }
 
