@@ -1513,7 +1513,14 @@ int ring_count() {
 // Three activation parts (fp32-faithful) when the weight ring keeps at
 // least 128 KB; two (x to about 2^-17, as in the tensor-core prefill)
 // otherwise, so that large models keep enough weight bytes in flight.
+// STRASGPT_MEGA_PARTS=2 or 3 overrides the choice (when the ring still
+// fits).
 int act_parts(int D, int QD, int Fl, int HD, int G) {
+  const char* v = getenv("STRASGPT_MEGA_PARTS");
+  if (v && (atoi(v) == 2 || atoi(v) == 3) &&
+      act_bytes(D, QD, Fl, HD, G, atoi(v)) + (size_t)ring_count() * 16 * 1024 <=
+          smem_budget(HD, G))
+    return atoi(v);
   return act_bytes(D, QD, Fl, HD, G, 3) + (size_t)128 * 1024 <= smem_budget(HD, G) ? 3 : 2;
 }
 

@@ -122,3 +122,20 @@ def test_golden_fixtures_cover_every_tiny_config():
         cfg = configs.get(name)
         assert g["logits"].shape == (cfg.steps + 1, cfg.vocab)
         assert len(meta["tokens"]) == cfg.steps + 1
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["t_llama", "t_qwen", "t_untied", "t_gqa8"])
+def test_device_greedy_loop_two_activation_parts(cuda, name, monkeypatch):
+    """The persistent decode kernel with the activation split into two bf16
+    parts (the choice for models whose FFN width leaves too little shared
+    memory for three): greedy ids still equal the golden ones."""
+    from strasgpt_b200 import Transformer
+    monkeypatch.setenv("STRASGPT_MEGA_PARTS", "2")
+    cfg = configs.get(name)
+    meta, _ = load_golden(name)
+    m = Transformer(model_dir(cfg))
+    toks, tm = m.generate_greedy(synth.prompt_tokens(cfg), cfg.steps)
+    assert tm.decode_launches == 1  # the persistent kernel ran
+    assert list(toks) == meta["tokens"]
+    m.free()
