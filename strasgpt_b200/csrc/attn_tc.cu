@@ -1,0 +1,305 @@
+// Causal GQA attention of a prefill chunk on the tensor cores
+// (source/transformer.c:1375-1422: s = q.k / sqrtf(HD) over positions
+// [0, pos], max-subtracted expf softmax, att = sum p v).
+//
+// One CTA = one kv head and 64 rows, a row being one (query, q head of the
+// group) pair (64 / G queries x G heads), so every K/V tile is shared by the
+// whole group. Four warps, 16 rows each. The reference's operands are fp32;
+// the tensor cores take bf16, so each operand is split as x = hi + lo
+// (hi = bf16(x), lo = bf16(x - hi), about 17 significant bits, as in the
+// tensor-core projections) and every product takes three mma.sync
+// m16n8k16 (hi.hi + hi.lo + lo.hi) with fp32 accumulators:
+//   S = Q K^T   Q fragments from shared memory (ldmatrix), K rows as the
+//               col-major B operand (ldmatrix of [key][hd] tiles);
+//   online softmax on the S accumulators (rows g and g + 8 of a lane);
+//   O += P V    P re-packed from the S accumulators into A fragments, V as
+//               the B operand (ldmatrix.trans of [key][hd] tiles).
+// K/V tiles of 64 keys are read from the fp32 cache, split and stored in
+// shared memory with rows padded by 16 bytes (conflict-free ldmatrix).
+#include "common.cuh"
+#include "kernels.h"
+
+#include <math.h>
+
+namespace sg {
+namespace {
+
+constexpr int kRowsTc = 64;  // rows per CTA
+constexpr int kKeysTc = 64;  // keys per tile
+
+template <int HD>
+struct TcAttn {
+  static constexpr int LD = HD + 8;  // bf16 elements per shared-memory row
+  static constexpr size_t kBytes = (size_t)(2 * kRowsTc + 4 * kKeysTc) * LD * 2;
+};
+
+__device__ __forceinline__ uint32_t saddr(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+// fp32 -> bf16 bits, round to nearest even (finite inputs).
+__device__ __forceinline__ uint32_t bf16_bits(float f) {
+  uint32_t u = __float_as_uint(f);
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return u >> 16;
+}
+
+// (hi, lo) bf16 bits of x.
+__device__ __forceinline__ void split2(float x, uint32_t& hi, uint32_t& lo) {
+  hi = bf16_bits(x);
+  lo = bf16_bits(x - __uint_as_float(hi << 16));
+}
+
+// Four fp32 values -> hi and lo halves as 8-byte stores.
+__device__ __forceinline__ void store_split4(uint16_t* hi, uint16_t* lo, float4 v) {
+  uint32_t h0, h1, h2, h3, l0, l1, l2, l3;
+  split2(v.x, h0, l0);
+  split2(v.y, h1, l1);
+  split2(v.z, h2, l2);
+  split2(v.w, h3, l3);
+  *reinterpret_cast<uint2*>(hi) = make_uint2(h0 | (h1 << 16), h2 | (h3 << 16));
+  *reinterpret_cast<uint2*>(lo) = make_uint2(l0 | (l1 << 16), l2 | (l3 << 16));
+}
+
+__device__ __forceinline__ void ldsm4(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm4t(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void mma(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <int HD>
+__global__ void __launch_bounds__(128) k_attn_prefill_tc(AttnPrefillArgs a) {
+  constexpr int LD = TcAttn<HD>::LD;
+  constexpr int KS = HD / 16;  // k16 steps of q.k
+  constexpr int NH = HD / 8;   // n8 tiles of the output
+  extern __shared__ __align__(16) uint16_t sm[];
+  uint16_t* Qh = sm;
+  uint16_t* Ql = Qh + kRowsTc * LD;
+  uint16_t* Kh = Ql + kRowsTc * LD;
+  uint16_t* Kl = Kh + kKeysTc * LD;
+  uint16_t* Vh = Kl + kKeysTc * LD;
+  uint16_t* Vl = Vh + kKeysTc * LD;
+  const int kh = blockIdx.x, G = a.G, qt = kRowsTc / G, t0 = blockIdx.y * qt;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g8 = lane >> 2, c = lane & 3;
+  pdl_trigger();
+  pdl_wait();
+
+  // Q tile: row r = (query t0 + r / G, head r % G).
+  const float4* q4 = reinterpret_cast<const float4*>(a.q);
+  for (int i = tid; i < kRowsTc * (HD / 4); i += 128) {
+    const int r = i / (HD / 4), d4 = i % (HD / 4);
+    const int t = t0 + r / G, g = r % G;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (t < a.T) v = q4[((size_t)(t * a.KHl + kh) * G + g) * (HD / 4) + d4];
+    store_split4(Qh + r * LD + d4 * 4, Ql + r * LD + d4 * 4, v);
+  }
+
+  // This lane's rows (g8 and g8 + 8 of the warp's 16) and their positions.
+  const int rA = 16 * warp + g8, rB = rA + 8;
+  const int tA = t0 + rA / G, tB = t0 + rB / G;
+  const int posA = (tA < a.T) ? a.pos0 + tA : -1;  // -1: no keys
+  const int posB = (tB < a.T) ? a.pos0 + tB : -1;
+  float mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;
+  float o[NH][4];
+#pragma unroll
+  for (int n = 0; n < NH; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  const int tl = min(t0 + qt, a.T) - 1;
+  const int kend = a.pos0 + tl + 1;  // keys [0, kend) for this CTA
+  const float div = sqrtf((float)HD);
+  const float4* kc4 = reinterpret_cast<const float4*>(a.k_cache + (size_t)kh * a.ctx * HD);
+  const float4* vc4 = reinterpret_cast<const float4*>(a.v_cache + (size_t)kh * a.ctx * HD);
+
+  // ldmatrix lane addresses (element offsets within a tile):
+  //  A (Q rows of this warp): row (lane % 16), column 8 (lane / 16);
+  //  B (K, two n8 tiles): key (lane % 8) + 8 (lane / 16), column 8 ((lane / 8) % 2);
+  //  B (V, transposed, two n8 tiles): key (lane % 8) + 8 ((lane / 8) % 2), column 8 (lane / 16).
+  const int qoff = (16 * warp + (lane & 15)) * LD + (lane >> 4) * 8;
+  const int koff = ((lane & 7) + (lane >> 4) * 8) * LD + ((lane >> 3) & 1) * 8;
+  const int voff = ((lane & 7) + ((lane >> 3) & 1) * 8) * LD + (lane >> 4) * 8;
+
+  for (int k0 = 0; k0 < kend; k0 += kKeysTc) {
+    __syncthreads();  // Q written / the previous tile's K and V consumed
+    for (int i = tid; i < kKeysTc * (HD / 4); i += 128) {
+      const int key = i / (HD / 4), d4 = i % (HD / 4);
+      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+      if (k0 + key < kend) {
+        kv = __ldcg(kc4 + (size_t)(k0 + key) * (HD / 4) + d4);
+        vv = __ldcg(vc4 + (size_t)(k0 + key) * (HD / 4) + d4);
+      }
+      store_split4(Kh + key * LD + d4 * 4, Kl + key * LD + d4 * 4, kv);
+      store_split4(Vh + key * LD + d4 * 4, Vl + key * LD + d4 * 4, vv);
+    }
+    __syncthreads();
+
+    // S = Q K^T: 16 rows x 64 keys per warp (8 n8 tiles).
+    float s[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; n++) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < KS; ks++) {
+      uint32_t ah[4], al[4];
+      ldsm4(saddr(Qh + qoff + ks * 16), ah);
+      ldsm4(saddr(Ql + qoff + ks * 16), al);
+#pragma unroll
+      for (int n = 0; n < 8; n += 2) {
+        uint32_t bh[4], bl[4];
+        ldsm4(saddr(Kh + koff + n * 8 * LD + ks * 16), bh);
+        ldsm4(saddr(Kl + koff + n * 8 * LD + ks * 16), bl);
+        mma(s[n], ah, bh[0], bh[1]);
+        mma(s[n], ah, bl[0], bl[1]);
+        mma(s[n], al, bh[0], bh[1]);
+        mma(s[n + 1], ah, bh[2], bh[3]);
+        mma(s[n + 1], ah, bl[2], bl[3]);
+        mma(s[n + 1], al, bh[2], bh[3]);
+      }
+    }
+
+    // Scale, causal mask, online softmax (rows A and B of this lane; the
+    // four lanes of a row hold its 64 keys).
+    float mxA = -INFINITY, mxB = -INFINITY;
+#pragma unroll
+    for (int n = 0; n < 8; n++) {
+      const int key = k0 + n * 8 + 2 * c;
+      s[n][0] = (key <= posA) ? s[n][0] / div : -INFINITY;
+      s[n][1] = (key + 1 <= posA) ? s[n][1] / div : -INFINITY;
+      s[n][2] = (key <= posB) ? s[n][2] / div : -INFINITY;
+      s[n][3] = (key + 1 <= posB) ? s[n][3] / div : -INFINITY;
+      mxA = fmaxf(mxA, fmaxf(s[n][0], s[n][1]));
+      mxB = fmaxf(mxB, fmaxf(s[n][2], s[n][3]));
+    }
+    mxA = fmaxf(mxA, __shfl_xor_sync(0xFFFFFFFFu, mxA, 1));
+    mxA = fmaxf(mxA, __shfl_xor_sync(0xFFFFFFFFu, mxA, 2));
+    mxB = fmaxf(mxB, __shfl_xor_sync(0xFFFFFFFFu, mxB, 1));
+    mxB = fmaxf(mxB, __shfl_xor_sync(0xFFFFFFFFu, mxB, 2));
+    const float nA = fmaxf(mA, mxA), nB = fmaxf(mB, mxB);
+    // A row with no key so far keeps m = -inf and contributes nothing.
+    const float cA = (nA == -INFINITY) ? 1.f : expf(mA - nA);
+    const float cB = (nB == -INFINITY) ? 1.f : expf(mB - nB);
+    mA = nA;
+    mB = nB;
+    lA *= cA;
+    lB *= cB;
+#pragma unroll
+    for (int n = 0; n < NH; n++) {
+      o[n][0] *= cA;
+      o[n][1] *= cA;
+      o[n][2] *= cB;
+      o[n][3] *= cB;
+    }
+#pragma unroll
+    for (int n = 0; n < 8; n++) {
+      s[n][0] = (s[n][0] == -INFINITY) ? 0.f : expf(s[n][0] - nA);
+      s[n][1] = (s[n][1] == -INFINITY) ? 0.f : expf(s[n][1] - nA);
+      s[n][2] = (s[n][2] == -INFINITY) ? 0.f : expf(s[n][2] - nB);
+      s[n][3] = (s[n][3] == -INFINITY) ? 0.f : expf(s[n][3] - nB);
+      lA += s[n][0] + s[n][1];
+      lB += s[n][2] + s[n][3];
+    }
+
+    // O += P V: k16 step j = keys 16 j .. 16 j + 15 (S tiles 2j, 2j + 1).
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      uint32_t ph[4], pl[4];
+      {
+        uint32_t h0, l0, h1, l1;
+        split2(s[2 * j][0], h0, l0);
+        split2(s[2 * j][1], h1, l1);
+        ph[0] = h0 | (h1 << 16);
+        pl[0] = l0 | (l1 << 16);
+        split2(s[2 * j][2], h0, l0);
+        split2(s[2 * j][3], h1, l1);
+        ph[1] = h0 | (h1 << 16);
+        pl[1] = l0 | (l1 << 16);
+        split2(s[2 * j + 1][0], h0, l0);
+        split2(s[2 * j + 1][1], h1, l1);
+        ph[2] = h0 | (h1 << 16);
+        pl[2] = l0 | (l1 << 16);
+        split2(s[2 * j + 1][2], h0, l0);
+        split2(s[2 * j + 1][3], h1, l1);
+        ph[3] = h0 | (h1 << 16);
+        pl[3] = l0 | (l1 << 16);
+      }
+#pragma unroll
+      for (int n = 0; n < NH; n += 2) {
+        uint32_t bh[4], bl[4];
+        ldsm4t(saddr(Vh + voff + j * 16 * LD + n * 8), bh);
+        ldsm4t(saddr(Vl + voff + j * 16 * LD + n * 8), bl);
+        mma(o[n], ph, bh[0], bh[1]);
+        mma(o[n], ph, bl[0], bl[1]);
+        mma(o[n], pl, bh[0], bh[1]);
+        mma(o[n + 1], ph, bh[2], bh[3]);
+        mma(o[n + 1], ph, bl[2], bl[3]);
+        mma(o[n + 1], pl, bh[2], bh[3]);
+      }
+    }
+  }
+
+  // Row sums over the four lanes of a row, then att = O / l.
+  lA += __shfl_xor_sync(0xFFFFFFFFu, lA, 1);
+  lA += __shfl_xor_sync(0xFFFFFFFFu, lA, 2);
+  lB += __shfl_xor_sync(0xFFFFFFFFu, lB, 1);
+  lB += __shfl_xor_sync(0xFFFFFFFFu, lB, 2);
+  const int gA = rA % G, gB = rB % G;
+  if (tA < a.T) {
+    float* out = a.att + ((size_t)(tA * a.KHl + kh) * G + gA) * HD;
+#pragma unroll
+    for (int n = 0; n < NH; n++)
+      *reinterpret_cast<float2*>(out + n * 8 + 2 * c) = make_float2(o[n][0] / lA, o[n][1] / lA);
+  }
+  if (tB < a.T) {
+    float* out = a.att + ((size_t)(tB * a.KHl + kh) * G + gB) * HD;
+#pragma unroll
+    for (int n = 0; n < NH; n++)
+      *reinterpret_cast<float2*>(out + n * 8 + 2 * c) = make_float2(o[n][2] / lB, o[n][3] / lB);
+  }
+}
+
+template <int HD>
+void launch_hd(const AttnPrefillArgs& a, cudaStream_t s) {
+  const int qt = kRowsTc / a.G;
+  dim3 grid(a.KHl, (a.T + qt - 1) / qt);
+  launch(k_attn_prefill_tc<HD>, grid, dim3(128), TcAttn<HD>::kBytes, s, a);
+}
+
+}  // namespace
+
+bool attn_prefill_tc_supported(const AttnPrefillArgs& a) {
+  return (a.HD == 32 || a.HD == 64 || a.HD == 128) && a.G >= 1 && a.G <= kRowsTc &&
+         kRowsTc % a.G == 0;
+}
+
+void attn_prefill_tc(const AttnPrefillArgs& a, cudaStream_t s) {
+  if (!attn_prefill_tc_supported(a)) SG_DIE("attn_prefill_tc: unsupported head_dim / group");
+  if (a.HD == 128)
+    launch_hd<128>(a, s);
+  else if (a.HD == 64)
+    launch_hd<64>(a, s);
+  else
+    launch_hd<32>(a, s);
+}
+
+void attn_prefill_tc_configure() {
+  SG_CUDA(cudaFuncSetAttribute(k_attn_prefill_tc<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)TcAttn<32>::kBytes));
+  SG_CUDA(cudaFuncSetAttribute(k_attn_prefill_tc<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)TcAttn<64>::kBytes));
+  SG_CUDA(cudaFuncSetAttribute(k_attn_prefill_tc<128>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)TcAttn<128>::kBytes));
+}
+
+}  // namespace sg

@@ -20,6 +20,12 @@
 
 namespace sg {
 
+// Boolean setting from the environment: "0" is false, anything else true.
+bool env_flag(const char* name, bool dflt) {
+  const char* e = getenv(name);
+  return e ? e[0] != '0' : dflt;
+}
+
 bool pdl_enabled() {
   static int v = -1;
   if (v < 0) {
@@ -867,6 +873,10 @@ static void attn_prefill_hd(const AttnPrefillArgs& a, cudaStream_t s) {
 }
 
 void attn_prefill(const AttnPrefillArgs& a, cudaStream_t s) {
+  if (attn_prefill_tc_supported(a) && env_flag("STRASGPT_ATTN_TC", true)) {
+    attn_prefill_tc(a, s);
+    return;
+  }
   if (a.HD == 64)
     attn_prefill_hd<64>(a, s);
   else if (a.HD == 128)
@@ -1424,6 +1434,7 @@ void gpu_sleep_cycles(long long cycles, cudaStream_t s) {
 // than 48 KB. Called once per device before any launch (and before any
 // stream capture).
 void configure_kernels() {
+  attn_prefill_tc_configure();
   const int big = 200 * 1024;
 #define SG_SMEM(fn) \
   SG_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, big))

@@ -83,6 +83,11 @@ struct AttnPrefillArgs {
   float* att;
 };
 void attn_prefill(const AttnPrefillArgs& a, cudaStream_t s);
+// The same on the tensor cores (attn_tc.cu): operands split into bf16 hi/lo
+// halves, three mma.sync per product; attn_prefill uses it when supported.
+bool attn_prefill_tc_supported(const AttnPrefillArgs& a);
+void attn_prefill_tc(const AttnPrefillArgs& a, cudaStream_t s);
+void attn_prefill_tc_configure();
 
 // Greedy argmax over rows [0, n): first index of the strict maximum, as
 // source/sampler.c:92-102. Writes *out_token, stores it at

@@ -167,10 +167,14 @@ def test_gemm_tc(cuda, m, n, k, epi):
     (24, 2, 2, 64, 64, 0), (77, 2, 8, 32, 128, 10), (512, 8, 2, 128, 640, 0),
     (100, 1, 4, 128, 800, 600), (40, 2, 16, 64, 64, 3), (2, 1, 1, 128, 16, 5),
     (130, 2, 64, 64, 192, 0)])
-def test_attn_prefill(cuda, t, kh, g, hd, ctx, pos0):
+@pytest.mark.parametrize("tc", [True, False])
+def test_attn_prefill(cuda, t, kh, g, hd, ctx, pos0, tc, monkeypatch):
     """Causal GQA attention of a chunk against a float64 softmax
-    (source/transformer.c:1375-1422)."""
+    (source/transformer.c:1375-1422), on the tensor cores (operands split
+    into bf16 hi/lo halves: the projections' TC_REL bound) and on the CUDA
+    cores (STRASGPT_ATTN_TC=0)."""
     torch = cuda
+    monkeypatch.setenv("STRASGPT_ATTN_TC", "1" if tc else "0")
     gen = torch.Generator(device="cuda").manual_seed(t * 7 + g + hd + pos0)
     q = torch.randn(t, kh * g, hd, device="cuda", generator=gen)
     kc = torch.randn(kh, ctx, hd, device="cuda", generator=gen)
@@ -187,7 +191,8 @@ def test_attn_prefill(cuda, t, kh, g, hd, ctx, pos0):
     pos = pos0 + torch.arange(t, device="cuda").view(t, 1, 1, 1)
     s = s.masked_fill(torch.arange(n, device="cuda").view(1, 1, 1, n) > pos, float("-inf"))
     want = torch.einsum("tkgn,knd->tkgd", torch.softmax(s, dim=-1), v).reshape(t, kh * g, hd)
-    close(att, want, f"attn_prefill t={t} kh={kh} g={g} hd={hd} pos0={pos0}")
+    close(att, want, f"attn_prefill tc={tc} t={t} kh={kh} g={g} hd={hd} pos0={pos0}",
+          rel=TC_REL if tc else 1e-5)
 
 
 @pytest.mark.gpu
