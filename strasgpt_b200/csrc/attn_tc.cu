@@ -30,35 +30,47 @@ constexpr int kKeysTc = 64;  // keys per tile
 template <int HD>
 struct TcAttn {
   static constexpr int LD = HD + 8;  // bf16 elements per shared-memory row
-  static constexpr size_t kBytes = (size_t)(2 * kRowsTc + 4 * kKeysTc) * LD * 2;
+  // bf16 Q hi/lo, K hi/lo, V hi/lo, then the fp32 K and V rows of the next
+  // tile (filled by cp.async while the current tile is multiplied).
+  static constexpr size_t kBf16Bytes = (size_t)(2 * kRowsTc + 4 * kKeysTc) * LD * 2;
+  static constexpr size_t kBytes = kBf16Bytes + (size_t)2 * kKeysTc * HD * 4;
 };
 
 __device__ __forceinline__ uint32_t saddr(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
 }
 
-// fp32 -> bf16 bits, round to nearest even (finite inputs).
-__device__ __forceinline__ uint32_t bf16_bits(float f) {
-  uint32_t u = __float_as_uint(f);
-  u += 0x7FFFu + ((u >> 16) & 1u);
-  return u >> 16;
-}
-
-// (hi, lo) bf16 bits of x.
-__device__ __forceinline__ void split2(float x, uint32_t& hi, uint32_t& lo) {
-  hi = bf16_bits(x);
-  lo = bf16_bits(x - __uint_as_float(hi << 16));
+// Two fp32 values -> their bf16 (round to nearest even) hi halves and the
+// bf16 of what they leave (lo), each pair packed as one word, x0 in the low
+// 16 bits (the hardware conversion cvt.rn.bf16x2.f32 puts its first source
+// in the high half).
+__device__ __forceinline__ void split_pair(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(x1), "f"(x0));
+  const float r0 = x0 - __uint_as_float(hi << 16);
+  const float r1 = x1 - __uint_as_float(hi & 0xFFFF0000u);
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(r1), "f"(r0));
 }
 
 // Four fp32 values -> hi and lo halves as 8-byte stores.
 __device__ __forceinline__ void store_split4(uint16_t* hi, uint16_t* lo, float4 v) {
-  uint32_t h0, h1, h2, h3, l0, l1, l2, l3;
-  split2(v.x, h0, l0);
-  split2(v.y, h1, l1);
-  split2(v.z, h2, l2);
-  split2(v.w, h3, l3);
-  *reinterpret_cast<uint2*>(hi) = make_uint2(h0 | (h1 << 16), h2 | (h3 << 16));
-  *reinterpret_cast<uint2*>(lo) = make_uint2(l0 | (l1 << 16), l2 | (l3 << 16));
+  uint32_t h0, h1, l0, l1;
+  split_pair(v.x, v.y, h0, l0);
+  split_pair(v.z, v.w, h1, l1);
+  *reinterpret_cast<uint2*>(hi) = make_uint2(h0, h1);
+  *reinterpret_cast<uint2*>(lo) = make_uint2(l0, l1);
+}
+
+// 16-byte asynchronous copy global -> shared; src_bytes 0 fills zeros.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(saddr(dst)), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
 __device__ __forceinline__ void ldsm4(uint32_t addr, uint32_t* r) {
@@ -93,19 +105,56 @@ __global__ void __launch_bounds__(128) k_attn_prefill_tc(AttnPrefillArgs a) {
   uint16_t* Kl = Kh + kKeysTc * LD;
   uint16_t* Vh = Kl + kKeysTc * LD;
   uint16_t* Vl = Vh + kKeysTc * LD;
+  float* Kraw = reinterpret_cast<float*>(Vl + kKeysTc * LD);  // [kKeysTc][HD]
+  float* Vraw = Kraw + kKeysTc * HD;
   const int kh = blockIdx.x, G = a.G, qt = kRowsTc / G, t0 = blockIdx.y * qt;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g8 = lane >> 2, c = lane & 3;
+  constexpr int kVecPerThread = kKeysTc * (HD / 4) / 128;  // float4 per thread per tile
   pdl_trigger();
   pdl_wait();
 
-  // Q tile: row r = (query t0 + r / G, head r % G).
+  const int tl = min(t0 + qt, a.T) - 1;
+  const int kend = a.pos0 + tl + 1;  // keys [0, kend) for this CTA
+  const float* kbase = a.k_cache + (size_t)kh * a.ctx * HD;
+  const float* vbase = a.v_cache + (size_t)kh * a.ctx * HD;
+  // fp32 K and V rows [k0, k0 + kKeysTc) -> Kraw, Vraw (zeros past kend).
+  auto fetch = [&](int k0) {
+#pragma unroll
+    for (int u = 0; u < kVecPerThread; u++) {
+      const int i = tid + u * 128;
+      const int key = i / (HD / 4), d4 = i % (HD / 4);
+      const bool in = k0 + key < kend;
+      const size_t off = in ? (size_t)(k0 + key) * HD + d4 * 4 : 0;
+      cp_async16(Kraw + key * HD + d4 * 4, kbase + off, in ? 16 : 0);
+      cp_async16(Vraw + key * HD + d4 * 4, vbase + off, in ? 16 : 0);
+    }
+    cp_async_commit();
+  };
+  fetch(0);
+
+  // Q tile: row r = (query t0 + r / G, head r % G); all loads of a batch
+  // go out before the values are split.
   const float4* q4 = reinterpret_cast<const float4*>(a.q);
-  for (int i = tid; i < kRowsTc * (HD / 4); i += 128) {
-    const int r = i / (HD / 4), d4 = i % (HD / 4);
-    const int t = t0 + r / G, g = r % G;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (t < a.T) v = q4[((size_t)(t * a.KHl + kh) * G + g) * (HD / 4) + d4];
-    store_split4(Qh + r * LD + d4 * 4, Ql + r * LD + d4 * 4, v);
+  constexpr int kQBatch = 8;
+  for (int i0 = tid; i0 < kRowsTc * (HD / 4); i0 += kQBatch * 128) {
+    float4 v[kQBatch];
+#pragma unroll
+    for (int u = 0; u < kQBatch; u++) {
+      const int i = i0 + u * 128;
+      const int r = i / (HD / 4), d4 = i % (HD / 4);
+      const int t = t0 + r / G, g = r % G;
+      v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (i < kRowsTc * (HD / 4) && t < a.T)
+        v[u] = q4[((size_t)(t * a.KHl + kh) * G + g) * (HD / 4) + d4];
+    }
+#pragma unroll
+    for (int u = 0; u < kQBatch; u++) {
+      const int i = i0 + u * 128;
+      if (i < kRowsTc * (HD / 4)) {
+        const int r = i / (HD / 4), d4 = i % (HD / 4);
+        store_split4(Qh + r * LD + d4 * 4, Ql + r * LD + d4 * 4, v[u]);
+      }
+    }
   }
 
   // This lane's rows (g8 and g8 + 8 of the warp's 16) and their positions.
@@ -117,11 +166,7 @@ __global__ void __launch_bounds__(128) k_attn_prefill_tc(AttnPrefillArgs a) {
   float o[NH][4];
 #pragma unroll
   for (int n = 0; n < NH; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-  const int tl = min(t0 + qt, a.T) - 1;
-  const int kend = a.pos0 + tl + 1;  // keys [0, kend) for this CTA
   const float div = sqrtf((float)HD);
-  const float4* kc4 = reinterpret_cast<const float4*>(a.k_cache + (size_t)kh * a.ctx * HD);
-  const float4* vc4 = reinterpret_cast<const float4*>(a.v_cache + (size_t)kh * a.ctx * HD);
 
   // ldmatrix lane addresses (element offsets within a tile):
   //  A (Q rows of this warp): row (lane % 16), column 8 (lane / 16);
@@ -132,39 +177,54 @@ __global__ void __launch_bounds__(128) k_attn_prefill_tc(AttnPrefillArgs a) {
   const int voff = ((lane & 7) + ((lane >> 3) & 1) * 8) * LD + (lane >> 4) * 8;
 
   for (int k0 = 0; k0 < kend; k0 += kKeysTc) {
-    __syncthreads();  // Q written / the previous tile's K and V consumed
-    for (int i = tid; i < kKeysTc * (HD / 4); i += 128) {
+    // This tile's fp32 rows have landed (each thread waits for its own
+    // copies; the barrier makes all of them visible) and the previous
+    // tile's bf16 K and V are consumed.
+    cp_async_wait_all();
+    __syncthreads();
+#pragma unroll 4
+    for (int u = 0; u < kVecPerThread; u++) {
+      const int i = tid + u * 128;
       const int key = i / (HD / 4), d4 = i % (HD / 4);
-      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-      if (k0 + key < kend) {
-        kv = __ldcg(kc4 + (size_t)(k0 + key) * (HD / 4) + d4);
-        vv = __ldcg(vc4 + (size_t)(k0 + key) * (HD / 4) + d4);
-      }
+      const float4 kv = *reinterpret_cast<const float4*>(Kraw + key * HD + d4 * 4);
+      const float4 vv = *reinterpret_cast<const float4*>(Vraw + key * HD + d4 * 4);
       store_split4(Kh + key * LD + d4 * 4, Kl + key * LD + d4 * 4, kv);
       store_split4(Vh + key * LD + d4 * 4, Vl + key * LD + d4 * 4, vv);
     }
     __syncthreads();
+    // The next tile's rows stream in while this one is multiplied.
+    if (k0 + kKeysTc < kend) fetch(k0 + kKeysTc);
 
     // S = Q K^T: 16 rows x 64 keys per warp (8 n8 tiles).
     float s[8][4];
 #pragma unroll
     for (int n = 0; n < 8; n++) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+    // Per k16 step: every fragment first, then the three products of all
+    // eight tiles in turn (eight independent accumulation chains).
 #pragma unroll
     for (int ks = 0; ks < KS; ks++) {
-      uint32_t ah[4], al[4];
+      uint32_t ah[4], al[4], bh[4][4], bl[4][4];
       ldsm4(saddr(Qh + qoff + ks * 16), ah);
       ldsm4(saddr(Ql + qoff + ks * 16), al);
 #pragma unroll
-      for (int n = 0; n < 8; n += 2) {
-        uint32_t bh[4], bl[4];
-        ldsm4(saddr(Kh + koff + n * 8 * LD + ks * 16), bh);
-        ldsm4(saddr(Kl + koff + n * 8 * LD + ks * 16), bl);
-        mma(s[n], ah, bh[0], bh[1]);
-        mma(s[n], ah, bl[0], bl[1]);
-        mma(s[n], al, bh[0], bh[1]);
-        mma(s[n + 1], ah, bh[2], bh[3]);
-        mma(s[n + 1], ah, bl[2], bl[3]);
-        mma(s[n + 1], al, bh[2], bh[3]);
+      for (int n = 0; n < 4; n++) {
+        ldsm4(saddr(Kh + koff + n * 16 * LD + ks * 16), bh[n]);
+        ldsm4(saddr(Kl + koff + n * 16 * LD + ks * 16), bl[n]);
+      }
+#pragma unroll
+      for (int n = 0; n < 4; n++) {
+        mma(s[2 * n], ah, bh[n][0], bh[n][1]);
+        mma(s[2 * n + 1], ah, bh[n][2], bh[n][3]);
+      }
+#pragma unroll
+      for (int n = 0; n < 4; n++) {
+        mma(s[2 * n], ah, bl[n][0], bl[n][1]);
+        mma(s[2 * n + 1], ah, bl[n][2], bl[n][3]);
+      }
+#pragma unroll
+      for (int n = 0; n < 4; n++) {
+        mma(s[2 * n], al, bh[n][0], bh[n][1]);
+        mma(s[2 * n + 1], al, bh[n][2], bh[n][3]);
       }
     }
 
@@ -214,36 +274,36 @@ __global__ void __launch_bounds__(128) k_attn_prefill_tc(AttnPrefillArgs a) {
 #pragma unroll
     for (int j = 0; j < 4; j++) {
       uint32_t ph[4], pl[4];
-      {
-        uint32_t h0, l0, h1, l1;
-        split2(s[2 * j][0], h0, l0);
-        split2(s[2 * j][1], h1, l1);
-        ph[0] = h0 | (h1 << 16);
-        pl[0] = l0 | (l1 << 16);
-        split2(s[2 * j][2], h0, l0);
-        split2(s[2 * j][3], h1, l1);
-        ph[1] = h0 | (h1 << 16);
-        pl[1] = l0 | (l1 << 16);
-        split2(s[2 * j + 1][0], h0, l0);
-        split2(s[2 * j + 1][1], h1, l1);
-        ph[2] = h0 | (h1 << 16);
-        pl[2] = l0 | (l1 << 16);
-        split2(s[2 * j + 1][2], h0, l0);
-        split2(s[2 * j + 1][3], h1, l1);
-        ph[3] = h0 | (h1 << 16);
-        pl[3] = l0 | (l1 << 16);
-      }
+      split_pair(s[2 * j][0], s[2 * j][1], ph[0], pl[0]);
+      split_pair(s[2 * j][2], s[2 * j][3], ph[1], pl[1]);
+      split_pair(s[2 * j + 1][0], s[2 * j + 1][1], ph[2], pl[2]);
+      split_pair(s[2 * j + 1][2], s[2 * j + 1][3], ph[3], pl[3]);
+      // Output tiles in groups of eight: fragments first, then the three
+      // products of the group in turn.
 #pragma unroll
-      for (int n = 0; n < NH; n += 2) {
-        uint32_t bh[4], bl[4];
-        ldsm4t(saddr(Vh + voff + j * 16 * LD + n * 8), bh);
-        ldsm4t(saddr(Vl + voff + j * 16 * LD + n * 8), bl);
-        mma(o[n], ph, bh[0], bh[1]);
-        mma(o[n], ph, bl[0], bl[1]);
-        mma(o[n], pl, bh[0], bh[1]);
-        mma(o[n + 1], ph, bh[2], bh[3]);
-        mma(o[n + 1], ph, bl[2], bl[3]);
-        mma(o[n + 1], pl, bh[2], bh[3]);
+      for (int n0 = 0; n0 < NH; n0 += 8) {
+        constexpr int kPairs = (NH < 8 ? NH : 8) / 2;
+        uint32_t bh[kPairs][4], bl[kPairs][4];
+#pragma unroll
+        for (int q = 0; q < kPairs; q++) {
+          ldsm4t(saddr(Vh + voff + j * 16 * LD + (n0 + 2 * q) * 8), bh[q]);
+          ldsm4t(saddr(Vl + voff + j * 16 * LD + (n0 + 2 * q) * 8), bl[q]);
+        }
+#pragma unroll
+        for (int q = 0; q < kPairs; q++) {
+          mma(o[n0 + 2 * q], ph, bh[q][0], bh[q][1]);
+          mma(o[n0 + 2 * q + 1], ph, bh[q][2], bh[q][3]);
+        }
+#pragma unroll
+        for (int q = 0; q < kPairs; q++) {
+          mma(o[n0 + 2 * q], ph, bl[q][0], bl[q][1]);
+          mma(o[n0 + 2 * q + 1], ph, bl[q][2], bl[q][3]);
+        }
+#pragma unroll
+        for (int q = 0; q < kPairs; q++) {
+          mma(o[n0 + 2 * q], pl, bh[q][0], bh[q][1]);
+          mma(o[n0 + 2 * q + 1], pl, bh[q][2], bh[q][3]);
+        }
       }
     }
   }
