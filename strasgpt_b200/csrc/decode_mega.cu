@@ -260,10 +260,21 @@ __device__ __forceinline__ void trace_mark(const MegaArgs& a, int ph, int slot) 
 // ---------------------------------------------------------------------------
 // Weight phases and the per-CTA chunk schedule
 // ---------------------------------------------------------------------------
-enum WKind { W_QKV = 0, W_O = 1, W_GU = 2, W_DOWN = 3, W_LM = 4 };
+enum WKind {
+  W_QKV = 0,
+  W_O = 1,
+  W_GU = 2,
+  W_DOWN = 3,
+  W_LM = 4,
+  W_ROUTER = 5,  // MoE: router rows (bf16)
+  W_EGU = 6,     // MoE: gate/up rows of the selected experts (MXFP4)
+  W_EDOWN = 7    // MoE: down rows of the selected experts (MXFP4)
+};
+constexpr int kKinds = 8;
+constexpr int kMaxTopk = 8;
 
 struct Phase {
-  const uint16_t* W;
+  const uint16_t* W;  // bf16 rows (null for the MXFP4 expert phases)
   int K;       // row length (elements)
   int pairs;   // total row pairs of the phase
   int kind;
@@ -274,18 +285,34 @@ struct Phase {
 constexpr int kMaxLayers = 96;
 __shared__ MegaLayer s_layers[kMaxLayers];
 
-// Weight phase `wp` of a step: 4 per layer (QKV, O, GU, DOWN), then LM.
+// Weight phases per layer: dense QKV, O, GU, DOWN; mixture of experts QKV,
+// O, ROUTER, EGU, EDOWN. The LM head follows the last layer.
+__device__ __forceinline__ int phases_per_layer(const MegaArgs& a) { return a.moe ? 5 : 4; }
+
+__device__ __forceinline__ int phase_kind(const MegaArgs& a, int wp) {
+  const int P = phases_per_layer(a);
+  if (wp == P * a.L) return W_LM;
+  const int i = wp % P;
+  if (!a.moe || i < 2) return i;
+  return i == 2 ? W_ROUTER : (i == 3 ? W_EGU : W_EDOWN);
+}
+
+// MXFP4 rows in a buffer: the codes (K / 2 bytes) then the scales (K / 32
+// bytes, rounded up to 16).
+__device__ __host__ __forceinline__ int mx_scale_bytes(int K) { return (K / 32 + 15) / 16 * 16; }
+__device__ __host__ __forceinline__ int mx_row_bytes(int K) { return K / 2 + mx_scale_bytes(K); }
+
+// Weight phase `wp` of a step.
 __device__ __forceinline__ Phase weight_phase(const MegaArgs& a, int wp) {
   Phase p;
-  if (wp == 4 * a.L) {
+  p.kind = phase_kind(a, wp);
+  if (p.kind == W_LM) {
     p.W = a.out_w;
     p.K = a.D;
     p.pairs = a.Vl / 2;
-    p.kind = W_LM;
     return p;
   }
-  const MegaLayer& ly = s_layers[wp >> 2];
-  p.kind = wp & 3;
+  const MegaLayer& ly = s_layers[wp / phases_per_layer(a)];
   switch (p.kind) {
     case W_QKV:
       p.W = ly.wqkv;
@@ -302,9 +329,24 @@ __device__ __forceinline__ Phase weight_phase(const MegaArgs& a, int wp) {
       p.K = a.D;
       p.pairs = a.Fl;
       break;
-    default:
+    case W_DOWN:
       p.W = ly.wd;
       p.K = a.Fl;
+      p.pairs = a.D / 2;
+      break;
+    case W_ROUTER:
+      p.W = ly.router;
+      p.K = a.D;
+      p.pairs = a.E / 2;
+      break;
+    case W_EGU:  // pair (slot j, f): gate row f and up row f of expert j
+      p.W = nullptr;
+      p.K = a.D;
+      p.pairs = a.topk * a.Fe;
+      break;
+    default:  // W_EDOWN: output rows, one chunk per selected expert
+      p.W = nullptr;
+      p.K = a.Fe;
       p.pairs = a.D / 2;
       break;
   }
@@ -313,9 +355,10 @@ __device__ __forceinline__ Phase weight_phase(const MegaArgs& a, int wp) {
 
 // One chunk: rows [r0, r1) of the phase's matrix over columns [k0, k1): up
 // to kMaxChunkRows rows, whole when they fit a buffer, else a column segment
-// (a row group then spans several chunks).
+// (a row group then spans several chunks). For W_EDOWN the segments are the
+// selected experts (seg = slot).
 struct Chunk {
-  int r0, r1, k0, k1;
+  int r0, r1, k0, k1, seg;
   bool first_seg, last_seg;
 };
 
@@ -329,19 +372,51 @@ struct Slice {
 
 __device__ __forceinline__ int row_stride(int cols) { return 2 * cols + kPad; }
 
-__device__ __forceinline__ Slice cta_slice(const Phase& ph, int buf_bytes) {
+// EGU chunk ci of a slice: pairs [p0, p0 + np), at most rows / 2 pairs and
+// never across a selected-expert boundary (a multiple of Fe), so that each
+// chunk's gate and up rows are contiguous runs of one expert.
+__device__ __forceinline__ void egu_chunk(int pb, int pe, int R, int Fe, int ci, int& p0,
+                                          int& np) {
+  int p = pb;
+  for (int i = 0;; i++) {
+    const int n = min(R, min(pe, (p / Fe + 1) * Fe) - p);
+    if (i == ci || p + n >= pe) {
+      p0 = p;
+      np = n;
+      return;
+    }
+    p += n;
+  }
+}
+
+__device__ __forceinline__ Slice cta_slice(const Phase& ph, int buf_bytes, int topk, int Fe) {
   Slice s;
   const long long np = ph.pairs;
   s.rb = 2 * (int)(np * blockIdx.x / gridDim.x);
   s.re = 2 * (int)(np * (blockIdx.x + 1) / gridDim.x);
   const int n = s.re - s.rb;
+  const int want = min(kMaxChunkRows, max(n, 2));
+  if (ph.kind == W_EGU || ph.kind == W_EDOWN) {
+    // Whole MXFP4 rows; the down rows once per selected expert; gate/up
+    // chunks end at expert boundaries.
+    s.rows = max(2, min(want, (buf_bytes / mx_row_bytes(ph.K)) & ~1));
+    s.kseg = ph.K;
+    s.spp = (ph.kind == W_EDOWN) ? topk : 1;
+    if (ph.kind == W_EDOWN) {
+      s.nchunks = ((n + s.rows - 1) / s.rows) * s.spp;
+    } else {
+      s.nchunks = 0;
+      for (int p = s.rb / 2; p < s.re / 2; s.nchunks++)
+        p += min(s.rows / 2, min(s.re / 2, (p / Fe + 1) * Fe) - p);
+    }
+    return s;
+  }
   // Whole rows, as many as the slice has up to kMaxChunkRows and what a
   // buffer holds, when that is at least 16 rows (or the whole slice); else
   // row segments of kSegCols columns (each row segment is one bulk copy:
   // long segments keep the copy count per byte low), as many rows as a
   // buffer holds, the columns split into equal segments (multiples of 256).
   constexpr int kSegCols = 1024;
-  const int want = min(kMaxChunkRows, max(n, 2));
   const int whole = min(want, (buf_bytes / row_stride(ph.K)) & ~1);
   if (whole >= min(16, want)) {
     s.rows = whole;
@@ -362,8 +437,14 @@ __device__ __forceinline__ Chunk slice_chunk(const Slice& s, const Phase& ph, in
   const int grp = ci / s.spp, seg = ci % s.spp;
   c.r0 = s.rb + grp * s.rows;
   c.r1 = min(c.r0 + s.rows, s.re);
-  c.k0 = seg * s.kseg;
-  c.k1 = min(c.k0 + s.kseg, ph.K);
+  c.seg = seg;
+  if (ph.kind == W_EDOWN) {
+    c.k0 = 0;
+    c.k1 = ph.K;
+  } else {
+    c.k0 = seg * s.kseg;
+    c.k1 = min(c.k0 + s.kseg, ph.K);
+  }
   c.first_seg = (seg == 0);
   c.last_seg = (seg == s.spp - 1);
   return c;
@@ -374,16 +455,16 @@ struct Cursor {
   int step, wp, ci;
 };
 
-// This CTA's slice of each weight-phase kind (QKV, O, GU, DOWN, LM); every
-// layer has the same shapes, so they are computed once per launch.
-__shared__ Slice s_slices[5];
+// This CTA's slice of each weight-phase kind; every layer has the same
+// shapes, so they are computed once per launch.
+__shared__ Slice s_slices[kKinds];
 
 __device__ void cursor_skip_empty(const MegaArgs& a, Cursor& c) {
+  const int last = phases_per_layer(a) * a.L;
   while (c.step < a.steps) {
-    const int kind = (c.wp == 4 * a.L) ? W_LM : (c.wp & 3);
-    if (c.ci < s_slices[kind].nchunks) return;
+    if (c.ci < s_slices[phase_kind(a, c.wp)].nchunks) return;
     c.ci = 0;
-    if (++c.wp > 4 * a.L) {
+    if (++c.wp > last) {
       c.wp = 0;
       c.step++;
     }
@@ -415,11 +496,63 @@ __device__ void wait_bar(const MegaArgs& a, uint64_t* bar, unsigned parity,
 // warps have released that buffer's previous chunk (empty[b]); its rows land
 // row_stride(k1 - k0) bytes apart. Stops issuing once the error flag is set;
 // before returning it waits (bounded) until its copies have landed.
+__device__ void expert_select(const MegaArgs& a, int l, unsigned e, int* sel, float* w);
+
+__device__ __forceinline__ bool expert_owned(const MegaArgs& a, int ex) {
+  return ex >= a.e_begin && ex < a.e_end;
+}
+
+// The producer's copy of the expert choice of the layer being streamed.
+__shared__ int s_psel[kMaxTopk];
+
+// An MXFP4 expert chunk in a buffer: the codes of its rows back to back,
+// then their scales (rows of mx_scale_bytes). EGU chunk of np pairs (slot j,
+// outputs f0 .. f0 + np): gate codes, up codes, gate scales, up scales;
+// EDOWN chunk (slot ch.seg, output rows r0 .. r1): codes, scales. Each run
+// is contiguous in memory, one bulk copy; experts this rank does not own
+// are not copied.
+__device__ void produce_mx(const MegaArgs& a, const Phase& ph, const Slice& sl, const Chunk& ch,
+                           int ci, int l, char* buf, uint64_t* bar) {
+  const int lane = threadIdx.x & 31;
+  const int cb = ph.K / 2, sb = mx_scale_bytes(ph.K);
+  const MegaLayer& ly = s_layers[l];
+  if (ph.kind == W_EGU) {
+    int p0, np;
+    egu_chunk(sl.rb / 2, sl.re / 2, sl.rows / 2, a.Fe, ci, p0, np);
+    const int j = p0 / a.Fe, f0 = p0 % a.Fe;
+    const bool own = expert_owned(a, s_psel[j]);
+    if (lane == 0) {
+      mbar_expect_tx(bar, own ? (unsigned)(2 * np * (cb + sb)) : 0u);
+      if (own) {
+        const size_t row = (size_t)(s_psel[j] - a.e_begin) * a.Fe + f0;
+        bulk_copy(buf, ly.gate_c + row * cb, (unsigned)(np * cb), bar);
+        bulk_copy(buf + (size_t)np * cb, ly.up_c + row * cb, (unsigned)(np * cb), bar);
+        bulk_copy(buf + (size_t)2 * np * cb, ly.gate_s + row * sb, (unsigned)(np * sb), bar);
+        bulk_copy(buf + (size_t)2 * np * cb + (size_t)np * sb, ly.up_s + row * sb,
+                  (unsigned)(np * sb), bar);
+      }
+    }
+  } else {
+    const int nr = ch.r1 - ch.r0, j = ch.seg;
+    const bool own = expert_owned(a, s_psel[j]);
+    if (lane == 0) {
+      mbar_expect_tx(bar, own ? (unsigned)(nr * (cb + sb)) : 0u);
+      if (own) {
+        const size_t row = (size_t)(s_psel[j] - a.e_begin) * a.D + ch.r0;
+        bulk_copy(buf, ly.down_c + row * cb, (unsigned)(nr * cb), bar);
+        bulk_copy(buf + (size_t)nr * cb, ly.down_s + row * sb, (unsigned)(nr * sb), bar);
+      }
+    }
+  }
+  __syncwarp();
+}
+
 __device__ void produce(const MegaArgs& a, char* base, int buf_bytes, int nbuf, uint64_t* full,
                         uint64_t* empty) {
   const int lane = threadIdx.x & 31;
   Cursor c = {0, 0, 0};
   unsigned g = 0;
+  int psel_key = -1;  // (step, layer) of s_psel
   for (;;) {
     cursor_skip_empty(a, c);
     if (c.step >= a.steps) break;
@@ -431,9 +564,22 @@ __device__ void produce(const MegaArgs& a, char* base, int buf_bytes, int nbuf, 
     if (*(volatile int*)a.err) break;
     const Phase ph = weight_phase(a, c.wp);
     const Chunk ch = slice_chunk(s_slices[ph.kind], ph, c.ci);
+    char* buf = base + (size_t)b * buf_bytes;
+    if (ph.kind == W_EGU || ph.kind == W_EDOWN) {
+      // The expert rows depend on this step's router output of the layer.
+      const int l = c.wp / phases_per_layer(a);
+      if (psel_key != c.step * a.L + l) {
+        expert_select(a, l, a.epoch + (unsigned)c.step, s_psel, nullptr);
+        psel_key = c.step * a.L + l;
+        if (*(volatile int*)a.err) break;  // the choice may be incomplete
+      }
+      produce_mx(a, ph, s_slices[ph.kind], ch, c.ci, l, buf, full + b);
+      c.ci++;
+      g++;
+      continue;
+    }
     const int nr = ch.r1 - ch.r0, w = ch.k1 - ch.k0;
     const int stride = row_stride(w);
-    char* buf = base + (size_t)b * buf_bytes;
     if (lane == 0) mbar_expect_tx(full + b, (unsigned)(nr * w * 2));
     __syncwarp();
     const uint16_t* src = ph.W + (size_t)ch.r0 * ph.K + ch.k0;
@@ -524,10 +670,12 @@ __device__ __forceinline__ const uint16_t* gains_ready(const MegaArgs& a, Gains&
 }
 
 // xq = rmsnorm(x) * gains from the flagged vector src (epoch e); the raw
-// values also go to xraw[K]. Thread t owns k = t + u * 256. The loops are
-// kept short: this code runs once per phase, from a cold instruction cache.
+// values also go to xraw[K] (and the normalised ones, as fp32, to xf when
+// set). Thread t owns k = t + u * 256. The loops are kept short: this code
+// runs once per phase, from a cold instruction cache.
 __device__ void stage_norm_ll(const MegaArgs& a, const u64* src, unsigned e, Gains& gs, int gi,
-                              int K, uint16_t* xq, int parts, float* xraw, float* red, int ph) {
+                              int K, uint16_t* xq, int parts, float* xraw, float* red, int ph,
+                              float* xf = nullptr) {
   const int tid = threadIdx.x;
   float ss = 0.f;
   for (int b = 0; b * kThreads < K; b += kNormBatch) {
@@ -549,8 +697,11 @@ __device__ void stage_norm_ll(const MegaArgs& a, const u64* src, unsigned e, Gai
   const float inv = 1.0f / sqrtf(ss + a.eps);
   const uint16_t* g = gains_ready(a, gs, gi);
   trace_mark(a, ph, MARK_GAINS);
-  for (int k = tid; k < K; k += kThreads)
-    xq_put(xq, K, parts, k, (xraw[k] * inv) * bf16_to_f32(g[k]));
+  for (int k = tid; k < K; k += kThreads) {
+    const float v = (xraw[k] * inv) * bf16_to_f32(g[k]);
+    xq_put(xq, K, parts, k, v);
+    if (xf) xf[k] = v;  // fp32 copy for the MXFP4 expert rows
+  }
   trace_mark(a, ph, MARK_SCALED);
   csync();
   trace_mark(a, ph, MARK_SYNCED);
@@ -634,11 +785,13 @@ __device__ __forceinline__ void pair_epilogue(const MegaArgs& a, const Out& o, i
   const int r0 = 2 * pair;
   switch (kind) {
     case W_QKV:
+    case W_ROUTER:
       ll_store(o.dst + r0, y0, o.e);
       ll_store(o.dst + r0 + 1, y1, o.e);
       break;
     case W_O:
     case W_DOWN:
+    case W_EDOWN:
       if (a.world > 1) {
         // This rank's partial sums go to every rank; the owner of the rows
         // adds them up in rank order (tp_reduce_rows).
@@ -820,6 +973,234 @@ __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const uint16_t
   trace_put(a, ph, SUM_COMPUTE, t_dot + t_red);
   trace_put(a, ph, SUM_DOT, t_dot);
   trace_put(a, ph, SUM_REDUCE, t_red);
+}
+
+// ---------------------------------------------------------------------------
+// Mixture of experts
+// ---------------------------------------------------------------------------
+// Expert choice for layer l from its router logits (flagged vector rl,
+// epoch e), as the per-op router (kernels.cu moe_topk): topk rounds of the
+// warp argmax (ties -> lower index), then the softmax over the chosen
+// logits in choice order. One warp; lane 0 writes sel[topk] and, when w is
+// set, w[topk]; the warp is synchronised on return.
+__device__ void expert_select(const MegaArgs& a, int l, unsigned e, int* sel, float* w) {
+  const int lane = threadIdx.x & 31;
+  float v[4];  // E <= 128
+  ll_gather<4>(a, a.ll + a.llo.rl + (size_t)l * a.E, lane, 32, a.E, e, v);
+#pragma unroll
+  for (int u = 0; u < 4; u++)
+    if (lane + 32 * u >= a.E) v[u] = -INFINITY;
+  float chosen[kMaxTopk];
+  int ci[kMaxTopk];
+  for (int s = 0; s < a.topk; s++) {
+    float best = -INFINITY;
+    int bi = 0x7FFFFFFF;
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int ex = lane + 32 * u;
+      if (ex < a.E && (v[u] > best || (v[u] == best && ex < bi))) {
+        best = v[u];
+        bi = ex;
+      }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      const float v2 = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+      const int i2 = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+      if (v2 > best || (v2 == best && i2 < bi)) {
+        best = v2;
+        bi = i2;
+      }
+    }
+    chosen[s] = best;
+    ci[s] = bi;
+#pragma unroll
+    for (int u = 0; u < 4; u++)
+      if (lane + 32 * u == bi) v[u] = -INFINITY;
+  }
+  if (lane == 0) {
+    const float mx = chosen[0];
+    float ex[kMaxTopk], sum = 0.f;
+    for (int s = 0; s < a.topk; s++) {
+      ex[s] = expf(chosen[s] - mx);
+      sum += ex[s];
+    }
+    for (int s = 0; s < a.topk; s++) {
+      sel[s] = ci[s];
+      if (w) w[s] = ex[s] / sum;
+    }
+  }
+  __syncwarp();
+}
+
+// e2m1 values (OCP microscaling), low nibble first; pairs of values per
+// code byte in shared memory.
+__device__ const float kMxE2M1[16] = {0.0f,  0.5f,  1.0f,  1.5f,  2.0f,  3.0f,  4.0f,  6.0f,
+                                      -0.0f, -0.5f, -1.0f, -1.5f, -2.0f, -3.0f, -4.0f, -6.0f};
+__shared__ float2 s_mx_lut[256];
+
+// 2^(e - 127) for an e8m0 scale byte (e = 0: 2^-127, a denormal).
+__device__ __forceinline__ float mx_scale(uint32_t e) {
+  return e == 0 ? __uint_as_float(0x00400000u) : __uint_as_float(e << 23);
+}
+
+// Partial dot of 8 codes (one 32-bit word, low nibble first) with 8
+// activations, as the per-op kernel (kernels.cu mxfp4_dot8).
+__device__ __forceinline__ float mx_dot8(uint32_t c, float4 xa, float4 xb) {
+  const float2 p0 = s_mx_lut[c & 0xFF];
+  const float2 p1 = s_mx_lut[(c >> 8) & 0xFF];
+  const float2 p2 = s_mx_lut[(c >> 16) & 0xFF];
+  const float2 p3 = s_mx_lut[c >> 24];
+  float t = p0.x * xa.x;
+  t = fmaf(p0.y, xa.y, t);
+  t = fmaf(p1.x, xa.z, t);
+  t = fmaf(p1.y, xa.w, t);
+  t = fmaf(p2.x, xb.x, t);
+  t = fmaf(p2.y, xb.y, t);
+  t = fmaf(p3.x, xb.z, t);
+  t = fmaf(p3.y, xb.w, t);
+  return t;
+}
+
+// Warp dots of two MXFP4 rows (codes c0/c1, scales s0/s1 in shared memory;
+// K elements) with x (fp32, shared memory): lane l takes the 8 codes at
+// bytes 4 (l % 4) of blocks l / 4 + 8 p, the block scale multiplying its
+// partial sum, as the per-op kernel (kernels.cu mxfp4_row_dot) does. With
+// c1 null only the first row is computed.
+__device__ __forceinline__ void mx_rows_dot(const uint8_t* c0, const uint8_t* s0,
+                                            const uint8_t* c1, const uint8_t* s1, int K,
+                                            const float* x, float& y0, float& y1) {
+  const int lane = threadIdx.x & 31, bl = lane >> 2, q = lane & 3, nb = K / 32;
+  float a0 = 0.f, a1 = 0.f;
+#pragma unroll 2
+  for (int b = bl; b < nb; b += 8) {
+    const float4* xv = reinterpret_cast<const float4*>(x + b * 32 + q * 8);
+    const float4 xa = xv[0], xb = xv[1];
+    const uint32_t w0 = *reinterpret_cast<const uint32_t*>(c0 + b * 16 + q * 4);
+    a0 = fmaf(mx_dot8(w0, xa, xb), mx_scale(s0[b]), a0);
+    if (c1) {
+      const uint32_t w1 = *reinterpret_cast<const uint32_t*>(c1 + b * 16 + q * 4);
+      a1 = fmaf(mx_dot8(w1, xa, xb), mx_scale(s1[b]), a1);
+    }
+  }
+  y0 = warp_sum(a0);
+  y1 = c1 ? warp_sum(a1) : 0.f;
+}
+
+// Gate/up of the selected experts: warp w takes the chunk's pairs w, w + 8,
+// ... (gate row and up row of expert sel[j], output f) and publishes
+// swiglu(gate . x, up . x) in the flagged vector hm (experts this rank does
+// not own: nothing).
+__device__ void consume_mx_gu(const MegaArgs& a, Ring& r, int l, const float* xf, const int* sel,
+                              unsigned e, int ph) {
+  trace_mark(a, ph, MARK_STAGED);
+  const Slice s = s_slices[W_EGU];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int cb = a.D / 2, sb = mx_scale_bytes(a.D);
+  u64* hm = a.ll + a.llo.hm + (size_t)l * a.topk * a.Fe;
+  const bool tr = a.trace != nullptr;
+  unsigned long long t_wait = 0, t0 = 0;
+  for (int ci = 0; ci < s.nchunks; ci++) {
+    const int b = (int)(r.g % r.nbuf);
+    if (tr) t0 = now_ns();
+    wait_bar(a, r.full + b, (r.g / r.nbuf) & 1);
+    if (tr) t_wait += now_ns() - t0;
+    if (ci == 0) trace_mark(a, ph, MARK_READY);
+    int p0, np;
+    egu_chunk(s.rb / 2, s.re / 2, s.rows / 2, a.Fe, ci, p0, np);
+    const int j = p0 / a.Fe, f0 = p0 % a.Fe;
+    if (expert_owned(a, sel[j])) {
+      const uint8_t* buf = reinterpret_cast<const uint8_t*>(r.base + (size_t)b * r.buf_bytes);
+      const uint8_t* gsc = buf + (size_t)2 * np * cb;
+      for (int i = warp; i < np; i += kWarps) {
+        float g, u;
+        mx_rows_dot(buf + (size_t)i * cb, gsc + (size_t)i * sb, buf + (size_t)(np + i) * cb,
+                    gsc + (size_t)(np + i) * sb, a.D, xf, g, u);
+        if (lane == 0) ll_store(hm + (size_t)j * a.Fe + f0 + i, swiglu(g, u), e);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(r.empty + b);
+    r.g++;
+  }
+  csync();  // xf (the normalised x) is read no more
+  trace_mark(a, ph, MARK_CONSUMED);
+  trace_put(a, ph, SUM_WAIT, t_wait);
+}
+
+// xf[j][f] = the selected experts' SwiGLU outputs (flagged vector hm,
+// epoch e) for the experts this rank owns.
+__device__ void stage_moe_h(const MegaArgs& a, int l, unsigned e, const int* sel, float* xf,
+                            int ph) {
+  constexpr int B = 16;
+  for (int j = 0; j < a.topk; j++) {
+    if (!expert_owned(a, sel[j])) continue;
+    const u64* src = a.ll + a.llo.hm + ((size_t)l * a.topk + j) * a.Fe;
+    for (int base = threadIdx.x; base < a.Fe; base += B * kThreads) {
+      float v[B];
+      ll_gather<B>(a, src, base, kThreads, a.Fe, e, v);
+#pragma unroll
+      for (int u = 0; u < B; u++) {
+        const int k = base + u * kThreads;
+        if (k < a.Fe) xf[(size_t)j * a.Fe + k] = v[u];
+      }
+    }
+  }
+  trace_mark(a, ph, MARK_INPUTS);
+  csync();
+}
+
+// Down rows of the selected experts: one chunk per (row group, expert j);
+// warp w takes rows w, w + 8, ... and adds w_j (down_j[row] . h_j) to the
+// row's sum in choice order; after the last expert, thread t finishes row
+// pair t (residual add, or the tensor-parallel push).
+__device__ void consume_mx_down(const MegaArgs& a, Ring& r, const float* xf, const int* sel,
+                                const float* selw, const Out& o, float& bv, int& bi, int ph) {
+  trace_mark(a, ph, MARK_STAGED);
+  const Slice s = s_slices[W_EDOWN];
+  const Phase phs = {nullptr, a.Fe, a.D / 2, W_EDOWN};
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int cb = a.Fe / 2, sb = mx_scale_bytes(a.Fe);
+  const bool tr = a.trace != nullptr;
+  unsigned long long t_wait = 0, t0 = 0;
+  for (int ci = 0; ci < s.nchunks; ci++) {
+    const int b = (int)(r.g % r.nbuf);
+    if (tr) t0 = now_ns();
+    wait_bar(a, r.full + b, (r.g / r.nbuf) & 1);
+    if (tr) t_wait += now_ns() - t0;
+    if (ci == 0) trace_mark(a, ph, MARK_READY);
+    const Chunk ch = slice_chunk(s, phs, ci);
+    const int nr = ch.r1 - ch.r0, j = ch.seg;
+    const bool own = expert_owned(a, sel[j]);
+    const float wj = selw[j];
+    const uint8_t* buf = reinterpret_cast<const uint8_t*>(r.base + (size_t)b * r.buf_bytes);
+    float* red = r.red + (size_t)(r.nred & 1) * kWarps * kMaxChunkRows;
+    // Two rows per warp pass (shared activation loads, two chains).
+    for (int ri = 2 * warp; ri < nr; ri += 2 * kWarps) {
+      float d0 = 0.f, d1 = 0.f;
+      if (own) {
+        const bool two = ri + 1 < nr;
+        mx_rows_dot(buf + (size_t)ri * cb, buf + (size_t)nr * cb + (size_t)ri * sb,
+                    two ? buf + (size_t)(ri + 1) * cb : nullptr,
+                    buf + (size_t)nr * cb + (size_t)(ri + 1) * sb, a.Fe, xf + (size_t)j * a.Fe,
+                    d0, d1);
+      }
+      if (lane == 0) {
+        red[ri] = (ch.first_seg ? 0.f : red[ri]) + wj * d0;
+        if (ri + 1 < nr) red[ri + 1] = (ch.first_seg ? 0.f : red[ri + 1]) + wj * d1;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(r.empty + b);
+    if (ch.last_seg) {
+      r.nred++;
+      csync();
+      if (tid < (nr >> 1))
+        pair_epilogue(a, o, W_EDOWN, (ch.r0 >> 1) + tid, red[2 * tid], red[2 * tid + 1], bv, bi);
+    }
+    r.g++;
+  }
+  trace_mark(a, ph, MARK_CONSUMED);
+  trace_put(a, ph, SUM_WAIT, t_wait);
 }
 
 // Tensor parallelism: rows [r0, r1) of the residual (this CTA's rows of the
@@ -1231,10 +1612,17 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   const int D32 = (a.D + 31) / 32 * 32;
   float* xraw = reinterpret_cast<float*>(dyn + (size_t)nbuf * buf_bytes);  // [D]
   uint16_t* gain_buf = reinterpret_cast<uint16_t*>(xraw + D32);              // [2][D]
+  // MoE: fp32 expert inputs (the normalised x, then the selected experts'
+  // SwiGLU outputs [topk][Fe]).
+  float* xf = reinterpret_cast<float*>(gain_buf + 2 * D32);
   // Matvec input (bf16 parts) or attention scratch (floats).
-  float* xs = reinterpret_cast<float*>(gain_buf + 2 * D32);
+  float* xs = xf + (a.moe ? (max(a.D, a.topk * a.Fe) + 31) / 32 * 32 : 0);
   uint16_t* xq = reinterpret_cast<uint16_t*>(xs);
+  __shared__ int s_csel[kMaxTopk];
+  __shared__ float s_cselw[kMaxTopk];
   for (int i = threadIdx.x; i < a.L; i += kBlockThreads) s_layers[i] = a.layers[i];
+  for (int i = threadIdx.x; i < 256; i += kBlockThreads)
+    s_mx_lut[i] = make_float2(kMxE2M1[i & 0xF], kMxE2M1[i >> 4]);
   if (threadIdx.x == 0) {
     for (int i = 0; i < nbuf; i++) {
       mbar_init(&full_bar[i], 1);
@@ -1245,10 +1633,25 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  if (threadIdx.x < 5) {
-    // Layer 0's phases stand for every layer (same shapes).
-    const int wp = (threadIdx.x == W_LM) ? 4 * a.L : threadIdx.x;
-    s_slices[threadIdx.x] = cta_slice(weight_phase(a, wp), buf_bytes);
+  if (threadIdx.x < kKinds) {
+    // Layer 0's phases stand for every layer (same shapes); kinds the model
+    // does not have get no chunks.
+    const int k = threadIdx.x, P = phases_per_layer(a);
+    int wp = -1;
+    if (k == W_LM)
+      wp = P * a.L;
+    else if (k == W_QKV || k == W_O)
+      wp = k;
+    else if (!a.moe && (k == W_GU || k == W_DOWN))
+      wp = k;
+    else if (a.moe && k >= W_ROUTER)
+      wp = k - W_ROUTER + 2;
+    if (wp >= 0) {
+      s_slices[k] = cta_slice(weight_phase(a, wp), buf_bytes, a.topk, a.Fe);
+    } else {
+      Slice z = {0, 0, 2, 0, 1, 0};
+      s_slices[k] = z;
+    }
   }
   __syncthreads();
   if (warp == kWarps) {
@@ -1276,6 +1679,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   int token = __ldcg(a.tok);
   int step = __ldcg(a.step);
   const int QD = a.QHl * a.HD;
+  const int P = phases_per_layer(a);
   const int attn_items = a.KHl * a.nsplit;
   float bv = -INFINITY;
   int bi = 0x7FFFFFFF;
@@ -1303,7 +1707,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
       else
         stage_norm_ll(a, x_o - 2 * (size_t)a.D + a.D, e, gs, 0, a.D, xq, parts, xraw, red, ph);
       gains_fill(gs, 0, l + 1 < a.L ? s_layers[l + 1].attn_norm : a.out_norm, a.D);
-      consume_phase(a, r, 4 * l + W_QKV, xq, parts,
+      consume_phase(a, r, P * l + 0, xq, parts,
                     Out{a.ll + a.llo.qkv + (size_t)l * a.QKVl, nullptr, e}, bv, bi, ph);
       ph++;
       // ATTN
@@ -1323,34 +1727,53 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
       stage_plain_ll(a, a.ll + a.llo.att + (size_t)l * QD, e, QD, xq, parts, ph);
       {
         const size_t part0 = a.llo.xpart + (size_t)(l * 2 + 0) * a.world * a.D;
-        consume_phase(a, r, 4 * l + W_O, xq, parts,
+        consume_phase(a, r, P * l + 1, xq, parts,
                       Out{x_o, xraw, e, part0 + (size_t)a.rank * a.D}, bv, bi, ph);
         if (a.world > 1)
           tp_reduce_rows(a, xraw, part0, x_o, s_slices[W_O].rb, s_slices[W_O].re, e);
       }
       ph++;
-      // gate/up + SwiGLU
+      // FFN input: RMSNorm of x_o (for MoE also kept as fp32 in xf)
       trace_mark(a, ph, MARK_BEGIN);
-      stage_norm_ll(a, x_o, e, gs, 1, a.D, xq, parts, xraw, red, ph);
+      stage_norm_ll(a, x_o, e, gs, 1, a.D, xq, parts, xraw, red, ph, a.moe ? xf : nullptr);
       if (l + 1 < a.L)
         gains_fill(gs, 1, s_layers[l + 1].ffn_norm, a.D);
       else if (s + 1 < a.steps)
         gains_fill(gs, 1, s_layers[0].ffn_norm, a.D);
-      consume_phase(a, r, 4 * l + W_GU, xq, parts,
-                    Out{a.ll + a.llo.h + (size_t)l * a.Fl, nullptr, e}, bv, bi, ph);
-      ph++;
-      // down + residual
-      trace_mark(a, ph, MARK_BEGIN);
-      stage_plain_ll(a, a.ll + a.llo.h + (size_t)l * a.Fl, e, a.Fl, xq, parts, ph);
-      {
-        const size_t part0 = a.llo.xpart + (size_t)(l * 2 + 1) * a.world * a.D;
-        consume_phase(a, r, 4 * l + W_DOWN, xq, parts,
-                      Out{x_d, xraw, e, part0 + (size_t)a.rank * a.D}, bv, bi, ph);
+      const size_t part_d = a.llo.xpart + (size_t)(l * 2 + 1) * a.world * a.D;
+      if (a.moe) {
+        // router logits, then every CTA picks the experts
+        consume_phase(a, r, P * l + 2, xq, parts,
+                      Out{a.ll + a.llo.rl + (size_t)l * a.E, nullptr, e}, bv, bi, ph);
+        if (warp == 0) expert_select(a, l, e, s_csel, s_cselw);
+        csync();
+        ph++;
+        // gate/up + SwiGLU of the selected experts
+        trace_mark(a, ph, MARK_BEGIN);
+        consume_mx_gu(a, r, l, xf, s_csel, e, ph);
+        ph++;
+        // down of the selected experts, weighted sum + residual
+        trace_mark(a, ph, MARK_BEGIN);
+        stage_moe_h(a, l, e, s_csel, xf, ph);
+        consume_mx_down(a, r, xf, s_csel, s_cselw,
+                        Out{x_d, xraw, e, part_d + (size_t)a.rank * a.D}, bv, bi, ph);
         if (a.world > 1)
-          tp_reduce_rows(a, xraw, part0, x_d, s_slices[W_DOWN].rb, s_slices[W_DOWN].re,
-                         e);
+          tp_reduce_rows(a, xraw, part_d, x_d, s_slices[W_EDOWN].rb, s_slices[W_EDOWN].re, e);
+        ph++;
+      } else {
+        // gate/up + SwiGLU
+        consume_phase(a, r, P * l + 2, xq, parts,
+                      Out{a.ll + a.llo.h + (size_t)l * a.Fl, nullptr, e}, bv, bi, ph);
+        ph++;
+        // down + residual
+        trace_mark(a, ph, MARK_BEGIN);
+        stage_plain_ll(a, a.ll + a.llo.h + (size_t)l * a.Fl, e, a.Fl, xq, parts, ph);
+        consume_phase(a, r, P * l + 3, xq, parts,
+                      Out{x_d, xraw, e, part_d + (size_t)a.rank * a.D}, bv, bi, ph);
+        if (a.world > 1)
+          tp_reduce_rows(a, xraw, part_d, x_d, s_slices[W_DOWN].rb, s_slices[W_DOWN].re, e);
+        ph++;
       }
-      ph++;
     }
     // LM head with per-CTA argmax
     trace_mark(a, ph, MARK_BEGIN);
@@ -1359,7 +1782,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     if (s + 1 < a.steps) gains_fill(gs, 0, s_layers[0].attn_norm, a.D);
     bv = -INFINITY;
     bi = 0x7FFFFFFF;
-    consume_phase(a, r, 4 * a.L, xq, parts, Out{nullptr, nullptr, e}, bv, bi, ph);
+    consume_phase(a, r, P * a.L, xq, parts, Out{nullptr, nullptr, e}, bv, bi, ph);
     // Warp argmax (ties: lower index), then the warps' in order.
     for (int o = 16; o > 0; o >>= 1) {
       const float v2 = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
@@ -1473,10 +1896,17 @@ size_t select_attn_floats(int HD, int G) {
 // (rounded to 32 floats), two bf16 gain vectors [D] (same rounding), then
 // the matvec input (`parts` bf16 arrays of K + 32 columns) or the attention
 // scratch.
-size_t act_bytes(int D, int QD, int Fl, int HD, int G, int parts) {
+// fp32 expert inputs of a mixture of experts (none for a dense model): the
+// normalised x [D], then the selected experts' outputs [topk][Fe].
+int moe_xf_floats(int D, int topk, int Fe) {
+  return topk ? (std::max(D, topk * Fe) + 31) / 32 * 32 : 0;
+}
+
+size_t act_bytes(int D, int QD, int Fl, int HD, int G, int parts, int xf_floats = 0) {
   const size_t kmax = (size_t)std::max(D, std::max(QD, Fl));
   size_t bytes = std::max((size_t)parts * 2 * (kmax + 32), select_attn_floats(HD, G) * 4);
   bytes += (size_t)(D + 31) / 32 * 32 * (4 + 2 * 2);  // xraw, two gain vectors
+  bytes += (size_t)xf_floats * 4;
   return (bytes + 127) / 128 * 128;
 }
 
@@ -1515,19 +1945,42 @@ int ring_count() {
 // otherwise, so that large models keep enough weight bytes in flight.
 // STRASGPT_MEGA_PARTS=2 or 3 overrides the choice (when the ring still
 // fits).
-int act_parts(int D, int QD, int Fl, int HD, int G) {
+int act_parts(int D, int QD, int Fl, int HD, int G, int xf) {
   const char* v = getenv("STRASGPT_MEGA_PARTS");
   if (v && (atoi(v) == 2 || atoi(v) == 3) &&
-      act_bytes(D, QD, Fl, HD, G, atoi(v)) + (size_t)ring_count() * 16 * 1024 <=
+      act_bytes(D, QD, Fl, HD, G, atoi(v), xf) + (size_t)ring_count() * 16 * 1024 <=
           smem_budget(HD, G))
     return atoi(v);
-  return act_bytes(D, QD, Fl, HD, G, 3) + (size_t)128 * 1024 <= smem_budget(HD, G) ? 3 : 2;
+  return act_bytes(D, QD, Fl, HD, G, 3, xf) + (size_t)128 * 1024 <= smem_budget(HD, G) ? 3 : 2;
+}
+
+// dst[r][0 .. src_bytes) = src[r][...], dst[r][src_bytes .. dst_bytes) = 0.
+__global__ void k_pad_rows(const uint8_t* __restrict__ src, size_t rows, int src_bytes,
+                           int dst_bytes, uint8_t* __restrict__ dst) {
+  const size_t n = rows * (size_t)dst_bytes;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / dst_bytes;
+    const int c = (int)(i % dst_bytes);
+    dst[i] = c < src_bytes ? src[r * src_bytes + c] : 0;
+  }
 }
 
 }  // namespace
 
+void mega_pad_rows(const uint8_t* src, size_t rows, int src_bytes, int dst_bytes, uint8_t* dst,
+                   cudaStream_t s) {
+  if (rows == 0) return;
+  const size_t n = rows * (size_t)dst_bytes;
+  const int blocks = (int)std::min<size_t>((n + 255) / 256, 148 * 16);
+  k_pad_rows<<<blocks, 256, 0, s>>>(src, rows, src_bytes, dst_bytes, dst);
+  SG_CUDA(cudaGetLastError());
+}
+
+int mega_scale_row_bytes(int K) { return mx_scale_bytes(K); }
+
 MegaFlagged mega_flagged_layout(int D, int QKVl, int QD, int Fl, int L, int grid, int world,
-                                int nsplit, int HD) {
+                                int nsplit, int HD, int E, int topk, int Fe) {
   MegaFlagged f;
   f.x = 0;
   f.qkv = f.x + (size_t)L * 2 * D;
@@ -1537,17 +1990,20 @@ MegaFlagged mega_flagged_layout(int D, int QKVl, int QD, int Fl, int L, int grid
   f.am = f.xpart + (world > 1 ? (size_t)L * 2 * world * D : 0);
   f.rec = f.am + 2 * (size_t)world * grid;
   // QD / HD query heads, each with one record per split.
-  f.total = f.rec + (size_t)L * (QD / HD) * nsplit * (HD + 2);
+  f.rl = f.rec + (size_t)L * (QD / HD) * nsplit * (HD + 2);
+  f.hm = f.rl + (size_t)L * E;
+  f.total = f.hm + (size_t)L * topk * Fe;
   return f;
 }
 
 // Ring buffers take what the activations leave of the budget. Every row
 // length (D, QD, Fl) must be a multiple of 32 columns.
-size_t mega_smem_bytes(int D, int QD, int Fl, int HD, int G) {
+size_t mega_smem_bytes(int D, int QD, int Fl, int HD, int G, int topk, int Fe) {
   if (!select(HD, G)) return 0;
   if (D > kNormMaxK) return 0;
-  if (D % 32 || QD % 32 || Fl % 32) return 0;
-  const size_t act = act_bytes(D, QD, Fl, HD, G, act_parts(D, QD, Fl, HD, G));
+  if (D % 32 || QD % 32 || Fl % 32 || Fe % 32) return 0;
+  const int xf = moe_xf_floats(D, topk, Fe);
+  const size_t act = act_bytes(D, QD, Fl, HD, G, act_parts(D, QD, Fl, HD, G, xf), xf);
   const size_t budget = smem_budget(HD, G);
   const int nbuf = ring_count();
   if (act + (size_t)nbuf * 16 * 1024 > budget) return 0;
@@ -1555,8 +2011,9 @@ size_t mega_smem_bytes(int D, int QD, int Fl, int HD, int G) {
   return (size_t)nbuf * buf + act;
 }
 
-static int buffer_bytes(size_t smem, int D, int QD, int Fl, int HD, int G) {
-  return (int)((smem - act_bytes(D, QD, Fl, HD, G, act_parts(D, QD, Fl, HD, G))) / ring_count());
+static int buffer_bytes(size_t smem, int D, int QD, int Fl, int HD, int G, int xf) {
+  return (int)((smem - act_bytes(D, QD, Fl, HD, G, act_parts(D, QD, Fl, HD, G, xf), xf)) /
+               ring_count());
 }
 
 void mega_configure(size_t smem) {
@@ -1593,9 +2050,14 @@ void mega_decode(const MegaArgs& a, int grid, size_t smem, cudaStream_t s) {
   if (!k) SG_DIE("megakernel: unsupported head_dim / group");
   if (a.nsplit > kMaxSplits) SG_DIE("megakernel: too many attention splits");
   if (a.L > kMaxLayers) SG_DIE("megakernel: too many layers");
-  int buf = buffer_bytes(smem, a.D, a.QHl * a.HD, a.Fl, a.HD, a.G);
+  const int xf = moe_xf_floats(a.D, a.moe ? a.topk : 0, a.Fe);
+  int buf = buffer_bytes(smem, a.D, a.QHl * a.HD, a.Fl, a.HD, a.G, xf);
   if (buf < 16 * 1024 || buf % 1024) SG_DIE("megakernel: weight buffers too small");
-  int parts = act_parts(a.D, a.QHl * a.HD, a.Fl, a.HD, a.G);
+  if (a.moe && (a.topk < 1 || a.topk > kMaxTopk || a.E > 128 || a.E % 2))
+    SG_DIE("megakernel: unsupported expert count / top-k");
+  if (a.moe && 2 * mx_row_bytes(std::max(a.D, a.Fe)) > buf)
+    SG_DIE("megakernel: weight buffers too small for two expert rows");
+  int parts = act_parts(a.D, a.QHl * a.HD, a.Fl, a.HD, a.G, xf);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kBlockThreads);

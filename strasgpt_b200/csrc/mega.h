@@ -19,6 +19,17 @@ struct MegaLayer {
   const uint16_t* ffn_norm;
   const uint16_t* wgu;    // [2*Fl][D], gate/up rows interleaved
   const uint16_t* wd;     // [D][Fl]
+  // Mixture of experts (null for a dense layer): the router [E][D] bf16 and
+  // this rank's experts in MXFP4, codes [El][rows][K/2] (two per byte, low
+  // nibble first) and e8m0 scales [El][rows][S] with S = K/32 rounded up to
+  // 16 bytes (a row's scales start on a 16-byte boundary).
+  const uint16_t* router;
+  const uint8_t* gate_c;  // [El][Fe][D/2]
+  const uint8_t* up_c;
+  const uint8_t* down_c;  // [El][D][Fe/2]
+  const uint8_t* gate_s;  // [El][Fe][S(D)]
+  const uint8_t* up_s;
+  const uint8_t* down_s;  // [El][D][S(Fe)]
 };
 
 // Offsets (in 64-bit words) of the flagged vectors inside MegaArgs::ll.
@@ -32,11 +43,13 @@ struct MegaFlagged {
   size_t xpart;  // [L][2][N][D]  every rank's partial o_proj / down rows (N > 1)
   size_t am;     // [2][N][grid]  per-CTA argmax value / global index of every rank
   size_t rec;    // [L][KHl][nsplit][G][HD+2]  attention split records (m, l, acc)
+  size_t rl;     // [L][E]        router logits (MoE)
+  size_t hm;     // [L][topk][Fe] SwiGLU outputs of the selected experts (MoE)
   size_t total;
 };
 
 MegaFlagged mega_flagged_layout(int D, int QKVl, int QD, int Fl, int L, int grid, int world,
-                                int nsplit, int HD);
+                                int nsplit, int HD, int E, int topk, int Fe);
 
 struct MegaArgs {
   int D, HD, QHl, KHl, G, Fl, Vl, L, QKVl, ctx;
@@ -64,6 +77,9 @@ struct MegaArgs {
   int* gen;                 // generated tokens
   int gen_len;              // capacity of gen: writes at step >= gen_len are dropped
   int* err;                 // set non-zero when a wait times out
+  // Mixture of experts (moe != 0): E experts, topk chosen per token, expert
+  // FFN width Fe, this rank owning experts [e_begin, e_end).
+  int moe, E, topk, Fe, e_begin, e_end;
   int steps;
   int write_logits;
   // Optional (null = off): per phase and CTA, kMegaTraceWidth %globaltimer
@@ -80,13 +96,19 @@ struct MegaArgs {
 
 constexpr int kMegaTraceWidth = 13;
 
-// Dynamic shared memory the megakernel needs for these dimensions.
-size_t mega_smem_bytes(int D, int QD, int Fl, int HD, int G);
+// Dynamic shared memory the megakernel needs for these dimensions (for a
+// mixture of experts, Fl = 0, topk and Fe set; dense: topk = Fe = 0).
+size_t mega_smem_bytes(int D, int QD, int Fl, int HD, int G, int topk = 0, int Fe = 0);
 // Largest grid that is co-resident (one CTA per SM); 0 if not launchable.
 int mega_grid(size_t smem, int HD, int G);
 // Decode split used by the megakernel (split_len a multiple of 64).
 void mega_split(int ctx, int KHl, int grid, int* nsplit, int* split_len);
 void mega_configure(size_t smem);
+// Bytes of a row of e8m0 scales in the layout the kernel copies (K / 32
+// rounded up to 16), and the copy of [rows][src_bytes] into that layout.
+int mega_scale_row_bytes(int K);
+void mega_pad_rows(const uint8_t* src, size_t rows, int src_bytes, int dst_bytes, uint8_t* dst,
+                   cudaStream_t s);
 void mega_decode(const MegaArgs& a, int grid, size_t smem, cudaStream_t s);
 
 }  // namespace sg

@@ -555,13 +555,17 @@ void alloc_state(const W_t* w, const transformer_configuration_t* c, S_t* s) {
   SG_CUDA(cudaMemset(s->step, 0, 4));
   SG_CUDA(cudaMemset(s->gen, 0, ((size_t)s->ctx + 1) * 4));
   sg::attn_decode_split(s->ctx, w->KHl, &s->nsplit, &s->split_len);
-  // Megakernel decode: dense models, when a CTA fits on every SM (under
-  // tensor parallelism for the greedy loop; predict keeps the per-op path,
-  // which gathers the full logits).
-  s->use_mega = !w->moe && (w->Vl % 2 == 0) && w->L <= 96 && w->world <= 8 &&
-                w->D <= 8192 && env_int("STRASGPT_MEGA", 1) != 0;
+  // Megakernel decode (dense and mixture-of-experts models), when a CTA fits
+  // on every SM (under tensor parallelism for the greedy loop; predict keeps
+  // the per-op path, which gathers the full logits).
+  const bool moe_ok = !w->moe || (w->E % 2 == 0 && w->E <= 128 && w->topk >= 1 &&
+                                  w->topk <= 8 && w->F % 32 == 0 && w->D % 32 == 0);
+  const int mega_Fl = w->moe ? 0 : w->Fl;
+  s->use_mega = moe_ok && (w->Vl % 2 == 0) && w->L <= 96 && w->world <= 8 && w->D <= 8192 &&
+                env_int("STRASGPT_MEGA", 1) != 0;
   if (s->use_mega) {
-    s->mega_smem = sg::mega_smem_bytes(w->D, w->QHl * w->HD, w->Fl, w->HD, w->G);
+    s->mega_smem = sg::mega_smem_bytes(w->D, w->QHl * w->HD, mega_Fl, w->HD, w->G,
+                                       w->moe ? w->topk : 0, w->moe ? w->F : 0);
     if (s->mega_smem == 0) s->use_mega = false;
   }
   if (s->use_mega) {
@@ -572,17 +576,38 @@ void alloc_state(const W_t* w, const transformer_configuration_t* c, S_t* s) {
   if (s->use_mega) {
     sg::mega_split(s->ctx, w->KHl, s->mega_grid, &s->mega_nsplit, &s->mega_split_len);
     std::vector<sg::MegaLayer> ml(w->L);
+    const int sgD = sg::mega_scale_row_bytes(w->D), sgF = sg::mega_scale_row_bytes(w->F);
     for (int l = 0; l < w->L; l++) {
       const Layer& y = w->layer[l];
-      ml[l] = {y.attn_norm, y.wqkv, y.q_norm, y.k_norm, y.wo, y.ffn_norm, y.wgu, y.wd};
+      ml[l] = {y.attn_norm, y.wqkv, y.q_norm, y.k_norm, y.wo, y.ffn_norm, y.wgu, y.wd,
+               nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+      if (w->moe) {
+        // The expert scales again, each row on a 16-byte boundary (one bulk
+        // copy per row), next to the unchanged codes.
+        const size_t gu_rows = (size_t)w->El * w->F, d_rows = (size_t)w->El * w->D;
+        uint8_t* gs = (uint8_t*)dalloc(s->allocs, gu_rows * sgD, nullptr);
+        uint8_t* us = (uint8_t*)dalloc(s->allocs, gu_rows * sgD, nullptr);
+        uint8_t* ds = (uint8_t*)dalloc(s->allocs, d_rows * sgF, nullptr);
+        sg::mega_pad_rows(y.gate_s, gu_rows, w->D / 32, sgD, gs, 0);
+        sg::mega_pad_rows(y.up_s, gu_rows, w->D / 32, sgD, us, 0);
+        sg::mega_pad_rows(y.down_s, d_rows, w->F / 32, sgF, ds, 0);
+        ml[l].router = y.router;
+        ml[l].gate_c = y.gate_c;
+        ml[l].up_c = y.up_c;
+        ml[l].down_c = y.down_c;
+        ml[l].gate_s = gs;
+        ml[l].up_s = us;
+        ml[l].down_s = ds;
+      }
     }
+    SG_CUDA(cudaDeviceSynchronize());
     s->mega_layers = (sg::MegaLayer*)dalloc(s->allocs, sizeof(sg::MegaLayer) * w->L, nullptr);
     SG_CUDA(cudaMemcpy(s->mega_layers, ml.data(), sizeof(sg::MegaLayer) * w->L,
                        cudaMemcpyHostToDevice));
     s->err = I32(1);
     if (getenv("STRASGPT_MEGA_TRACE")) {
       // Phase timestamps of the first two decode steps of a launch.
-      s->trace_phases = 2 * (5 * w->L + 1);
+      s->trace_phases = 2 * ((w->moe ? 6 : 5) * w->L + 1);
       const size_t n = (size_t)s->trace_phases * s->mega_grid * sg::kMegaTraceWidth;
       s->trace = (unsigned long long*)dalloc(s->allocs, n * 8, nullptr);
       SG_CUDA(cudaMemset(s->trace, 0, n * 8));
@@ -590,8 +615,10 @@ void alloc_state(const W_t* w, const transformer_configuration_t* c, S_t* s) {
     SG_CUDA(cudaMemset(s->err, 0, 4));
     // Flagged hand-off vectors, zero (epoch 0: never written) at rest. Under
     // tensor parallelism they live in the exchange buffer the ranks map.
-    s->mega_llo = sg::mega_flagged_layout(w->D, w->QKVl, w->QHl * w->HD, w->Fl, w->L,
-                                          s->mega_grid, w->world, s->mega_nsplit, w->HD);
+    s->mega_llo = sg::mega_flagged_layout(w->D, w->QKVl, w->QHl * w->HD, mega_Fl, w->L,
+                                          s->mega_grid, w->world, s->mega_nsplit, w->HD,
+                                          w->moe ? w->E : 0, w->moe ? w->topk : 0,
+                                          w->moe ? w->F : 0);
     if (w->world == 1) {
       s->mega_ll = (unsigned long long*)dalloc(s->allocs, s->mega_llo.total * 8, nullptr);
       SG_CUDA(cudaMemset(s->mega_ll, 0, s->mega_llo.total * 8));
@@ -814,7 +841,10 @@ struct Runner {
   void mega(int steps, bool write_logits) {
     sg::MegaArgs a;
     a.D = w->D; a.HD = w->HD; a.QHl = w->QHl; a.KHl = w->KHl; a.G = w->G;
-    a.Fl = w->Fl; a.Vl = w->Vl; a.L = w->L; a.QKVl = w->QKVl; a.ctx = s->ctx;
+    a.Fl = w->moe ? 0 : w->Fl; a.Vl = w->Vl; a.L = w->L; a.QKVl = w->QKVl; a.ctx = s->ctx;
+    a.moe = w->moe ? 1 : 0;
+    a.E = w->moe ? w->E : 0; a.topk = w->moe ? w->topk : 0; a.Fe = w->moe ? w->F : 0;
+    a.e_begin = w->e_begin; a.e_end = w->e_end;
     a.eps = w->eps; a.layers = s->mega_layers;
     a.emb = w->emb; a.out_norm = w->out_norm; a.out_w = w->out_w;
     a.rope = s->rope;
