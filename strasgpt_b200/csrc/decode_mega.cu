@@ -302,6 +302,66 @@ __device__ __forceinline__ int phase_kind(const MegaArgs& a, int wp) {
 __device__ __host__ __forceinline__ int mx_scale_bytes(int K) { return (K / 32 + 15) / 16 * 16; }
 __device__ __host__ __forceinline__ int mx_row_bytes(int K) { return K / 2 + mx_scale_bytes(K); }
 
+// MXFP4 expert inputs in shared memory ("xm"): per vector of K values two
+// f16 arrays hi, mid with x * 2^s = hi + mid (hi the f16 rounding of
+// x * 2^s, mid that of what it leaves), s a power-of-two exponent per
+// 32-column block that puts the block's largest magnitude in [2^14, 2^15).
+// Array p of vector j starts at byte (2 j + p) * mx_x_vbytes(K) (64 mod 128,
+// so that the two arrays' 64-byte pieces of a block share no bank); after
+// all arrays, the inverse block scales 2^-s, floats [vectors][K / 32].
+__device__ __host__ __forceinline__ int mx_x_vbytes(int K) { return (2 * K + 127) / 128 * 128 + 64; }
+__device__ __host__ __forceinline__ int mx_x_bytes(int nvec, int K) {
+  return nvec * (2 * mx_x_vbytes(K) + K / 32 * 4);
+}
+// Floats of the xm region of a mixture of experts (none for a dense model):
+// the normalised x [D] (gate/up input), later the selected experts' SwiGLU
+// outputs [topk][Fe] (down input).
+__device__ __host__ __forceinline__ int moe_xf_floats(int D, int topk, int Fe) {
+  if (!topk) return 0;
+  const int b = mx_x_bytes(1, D) > mx_x_bytes(topk, Fe) ? mx_x_bytes(1, D) : mx_x_bytes(topk, Fe);
+  return (b / 4 + 31) / 32 * 32;
+}
+
+// 2^(e - 127) for an e8m0 scale byte (e = 0: 2^-127, a denormal).
+__device__ __forceinline__ float mx_scale(uint32_t e) {
+  return e == 0 ? __uint_as_float(0x00400000u) : __uint_as_float(e << 23);
+}
+
+__device__ __forceinline__ uint16_t f16_rn(float f) {
+  uint16_t h;
+  asm("cvt.rn.f16.f32 %0, %1;" : "=h"(h) : "f"(f));
+  return h;
+}
+__device__ __forceinline__ float f16_to_f32(uint16_t h) {
+  float f;
+  asm("cvt.f32.f16 %0, %1;" : "=f"(f) : "h"(h));
+  return f;
+}
+
+// Stores v (element k of vector j of an xm region for K columns) as its two
+// f16 parts. Called by the 32 lanes of a warp together, for the 32 columns
+// of one block (lane 0 at the block's first column): the block scale is the
+// warp's largest magnitude.
+__device__ __forceinline__ void xm_put_block(uint8_t* xm, int K, int nvec, int j, int k, float v) {
+  float m = fabsf(v);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+  int sh = 0;
+  if (m > 0.f) {
+    const int ex = (int)((__float_as_uint(m) >> 23) & 0xFF) - 127;
+    sh = min(max(14 - ex, -126), 126);
+  }
+  const float xs = v * __uint_as_float((uint32_t)(sh + 127) << 23);
+  const uint16_t hi = f16_rn(xs);
+  const uint16_t mid = f16_rn(xs - f16_to_f32(hi));
+  const int vb = mx_x_vbytes(K);
+  reinterpret_cast<uint16_t*>(xm + (size_t)(2 * j) * vb)[k] = hi;
+  reinterpret_cast<uint16_t*>(xm + (size_t)(2 * j + 1) * vb)[k] = mid;
+  if ((threadIdx.x & 31) == 0)
+    reinterpret_cast<float*>(xm + (size_t)nvec * 2 * vb)[j * (K / 32) + k / 32] =
+        __uint_as_float((uint32_t)(127 - sh) << 23);
+}
+
 // Weight phase `wp` of a step.
 __device__ __forceinline__ Phase weight_phase(const MegaArgs& a, int wp) {
   Phase p;
@@ -670,12 +730,12 @@ __device__ __forceinline__ const uint16_t* gains_ready(const MegaArgs& a, Gains&
 }
 
 // xq = rmsnorm(x) * gains from the flagged vector src (epoch e); the raw
-// values also go to xraw[K] (and the normalised ones, as fp32, to xf when
-// set). Thread t owns k = t + u * 256. The loops are kept short: this code
+// values also go to xraw[K] (and the normalised ones to the xm region, as
+// vector 0, when set). Thread t owns k = t + u * 256. The loops are kept short: this code
 // runs once per phase, from a cold instruction cache.
 __device__ void stage_norm_ll(const MegaArgs& a, const u64* src, unsigned e, Gains& gs, int gi,
                               int K, uint16_t* xq, int parts, float* xraw, float* red, int ph,
-                              float* xf = nullptr) {
+                              uint8_t* xm = nullptr) {
   const int tid = threadIdx.x;
   float ss = 0.f;
   for (int b = 0; b * kThreads < K; b += kNormBatch) {
@@ -700,7 +760,9 @@ __device__ void stage_norm_ll(const MegaArgs& a, const u64* src, unsigned e, Gai
   for (int k = tid; k < K; k += kThreads) {
     const float v = (xraw[k] * inv) * bf16_to_f32(g[k]);
     xq_put(xq, K, parts, k, v);
-    if (xf) xf[k] = v;  // fp32 copy for the MXFP4 expert rows
+    // MXFP4 expert input (K is then a multiple of 32: a warp's lanes hold
+    // one block)
+    if (xm) xm_put_block(xm, K, 1, 0, k, v);
   }
   trace_mark(a, ph, MARK_SCALED);
   csync();
@@ -1032,69 +1094,124 @@ __device__ void expert_select(const MegaArgs& a, int l, unsigned e, int* sel, fl
   __syncwarp();
 }
 
-// e2m1 values (OCP microscaling), low nibble first; pairs of values per
-// code byte in shared memory.
-__device__ const float kMxE2M1[16] = {0.0f,  0.5f,  1.0f,  1.5f,  2.0f,  3.0f,  4.0f,  6.0f,
-                                      -0.0f, -0.5f, -1.0f, -1.5f, -2.0f, -3.0f, -4.0f, -6.0f};
-__shared__ float2 s_mx_lut[256];
-
-// 2^(e - 127) for an e8m0 scale byte (e = 0: 2^-127, a denormal).
-__device__ __forceinline__ float mx_scale(uint32_t e) {
-  return e == 0 ? __uint_as_float(0x00400000u) : __uint_as_float(e << 23);
+// Four e2m1 pairs (the bytes of w, low byte first) as f16x2 words, the low
+// nibble of a byte in the low half (exact: every e2m1 value is an f16).
+__device__ __forceinline__ void e2m1x8_to_f16(uint32_t w, uint32_t* h) {
+  asm("{\n"
+      " .reg .b8 b0, b1, b2, b3;\n"
+      " mov.b32 {b0, b1, b2, b3}, %4;\n"
+      " cvt.rn.f16x2.e2m1x2 %0, b0;\n"
+      " cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+      " cvt.rn.f16x2.e2m1x2 %2, b2;\n"
+      " cvt.rn.f16x2.e2m1x2 %3, b3;\n"
+      "}"
+      : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+      : "r"(w));
 }
 
-// Partial dot of 8 codes (one 32-bit word, low nibble first) with 8
-// activations, as the per-op kernel (kernels.cu mxfp4_dot8).
-__device__ __forceinline__ float mx_dot8(uint32_t c, float4 xa, float4 xb) {
-  const float2 p0 = s_mx_lut[c & 0xFF];
-  const float2 p1 = s_mx_lut[(c >> 8) & 0xFF];
-  const float2 p2 = s_mx_lut[(c >> 16) & 0xFF];
-  const float2 p3 = s_mx_lut[c >> 24];
-  float t = p0.x * xa.x;
-  t = fmaf(p0.y, xa.y, t);
-  t = fmaf(p1.x, xa.z, t);
-  t = fmaf(p1.y, xa.w, t);
-  t = fmaf(p2.x, xb.x, t);
-  t = fmaf(p2.y, xb.y, t);
-  t = fmaf(p3.x, xb.z, t);
-  t = fmaf(p3.y, xb.w, t);
-  return t;
+// d += A (16x16 f16) * B (16x8 f16), fp32 accumulators; fragments as mma_bf16.
+__device__ __forceinline__ void mma_f16(float* d, uint32_t a0, uint32_t a1, uint32_t a2,
+                                        uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Warp dots of two MXFP4 rows (codes c0/c1, scales s0/s1 in shared memory;
-// K elements) with x (fp32, shared memory): lane l takes the 8 codes at
-// bytes 4 (l % 4) of blocks l / 4 + 8 p, the block scale multiplying its
-// partial sum, as the per-op kernel (kernels.cu mxfp4_row_dot) does. With
-// c1 null only the first row is computed.
-__device__ __forceinline__ void mx_rows_dot(const uint8_t* c0, const uint8_t* s0,
-                                            const uint8_t* c1, const uint8_t* s1, int K,
-                                            const float* x, float& y0, float& y1) {
-  const int lane = threadIdx.x & 31, bl = lane >> 2, q = lane & 3, nb = K / 32;
-  float a0 = 0.f, a1 = 0.f;
-#pragma unroll 2
-  for (int b = bl; b < nb; b += 8) {
-    const float4* xv = reinterpret_cast<const float4*>(x + b * 32 + q * 8);
-    const float4 xa = xv[0], xb = xv[1];
-    const uint32_t w0 = *reinterpret_cast<const uint32_t*>(c0 + b * 16 + q * 4);
-    a0 = fmaf(mx_dot8(w0, xa, xb), mx_scale(s0[b]), a0);
-    if (c1) {
-      const uint32_t w1 = *reinterpret_cast<const uint32_t*>(c1 + b * 16 + q * 4);
-      a1 = fmaf(mx_dot8(w1, xa, xb), mx_scale(s1[b]), a1);
+// One MXFP4 chunk on the tensor cores: rows [0, nr) (at most kMaxChunkRows;
+// codes at buf + i cb, scale bytes at buf + nr cb + i sb) times vector j of
+// the xm region (K columns). The products of a 32-column block are exact
+// in f16 x f16 -> fp32: lane 4g + c holds, from ldmatrix, the 32-bit code
+// word c (columns 8c .. 8c + 7) of rows g and g + 8 of a block, and those
+// eight columns are the lane's k slots of the block's two m16n8k16 steps;
+// B column n is x part min(n, 1) over the same columns (one 16-byte load).
+// Each block's accumulators are scaled by (weight block scale) x (x block
+// scale) into the row sums. Warp w walks block pairs w, w + 8, ... for every
+// 16-row group; lane 4g stores (first) or adds wgt x its row sums to
+// wred[row].
+__device__ __forceinline__ void mx_chunk_dot(const uint8_t* buf, int nr, int K, int cb, int sb,
+                                             const uint8_t* xm, int nvec, int j, float wgt,
+                                             bool first, float* wred) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, c = lane & 3;
+  const int nb = K >> 5, npair = (nb + 1) >> 1, ng = (nr + 15) >> 4;
+  const int vb = mx_x_vbytes(K);
+  const uint8_t* xp = xm + (size_t)(2 * j + min(g, 1)) * vb + c * 16;
+  const float* xsi = reinterpret_cast<const float*>(xm + (size_t)nvec * 2 * vb) + j * nb;
+  const uint8_t* scl = buf + (size_t)nr * cb;
+  // ldmatrix lane address: row (lane % 8) + 8 ((lane / 8) % 2) of group q
+  // (rows past the chunk read its last row), block + lane / 16.
+  const uint32_t bbase = smem_addr(buf) + (uint32_t)((lane >> 4) * 16);
+  const int m = (lane & 7) + ((lane >> 3) & 1) * 8;
+  float acc[kMaxChunkRows / 16][4];
+#pragma unroll
+  for (int q = 0; q < kMaxChunkRows / 16; q++)
+#pragma unroll
+    for (int i = 0; i < 4; i++) acc[q][i] = 0.f;
+  for (int kp = warp; kp < npair; kp += kWarps) {
+    const int b0 = 2 * kp;
+    const bool two = b0 + 1 < nb;
+    const uint4 x0 = *reinterpret_cast<const uint4*>(xp + (size_t)b0 * 64);
+    const uint4 x1 = two ? *reinterpret_cast<const uint4*>(xp + (size_t)(b0 + 1) * 64) : x0;
+    const float xs0 = xsi[b0], xs1 = two ? xsi[b0 + 1] : 0.f;
+#pragma unroll
+    for (int q = 0; q < kMaxChunkRows / 16; q++) {
+      if (q < ng) {
+        uint32_t w[4];
+        ldsm_x4(bbase + (uint32_t)(min(q * 16 + m, nr - 1) * cb + kp * 32), w);
+        const uint32_t sg =
+            *reinterpret_cast<const uint16_t*>(scl + min(q * 16 + g, nr - 1) * sb + b0);
+        const uint32_t s8 =
+            *reinterpret_cast<const uint16_t*>(scl + min(q * 16 + g + 8, nr - 1) * sb + b0);
+        uint32_t hg[4], h8[4];
+        float t[4] = {0.f, 0.f, 0.f, 0.f};
+        e2m1x8_to_f16(w[0], hg);
+        e2m1x8_to_f16(w[1], h8);
+        mma_f16(t, hg[0], h8[0], hg[1], h8[1], x0.x, x0.y);
+        mma_f16(t, hg[2], h8[2], hg[3], h8[3], x0.z, x0.w);
+        float fg = mx_scale(sg & 0xFF) * xs0, f8 = mx_scale(s8 & 0xFF) * xs0;
+        acc[q][0] = fmaf(t[0], fg, acc[q][0]);
+        acc[q][1] = fmaf(t[1], fg, acc[q][1]);
+        acc[q][2] = fmaf(t[2], f8, acc[q][2]);
+        acc[q][3] = fmaf(t[3], f8, acc[q][3]);
+        if (two) {
+          float u[4] = {0.f, 0.f, 0.f, 0.f};
+          e2m1x8_to_f16(w[2], hg);
+          e2m1x8_to_f16(w[3], h8);
+          mma_f16(u, hg[0], h8[0], hg[1], h8[1], x1.x, x1.y);
+          mma_f16(u, hg[2], h8[2], hg[3], h8[3], x1.z, x1.w);
+          fg = mx_scale(sg >> 8) * xs1;
+          f8 = mx_scale(s8 >> 8) * xs1;
+          acc[q][0] = fmaf(u[0], fg, acc[q][0]);
+          acc[q][1] = fmaf(u[1], fg, acc[q][1]);
+          acc[q][2] = fmaf(u[2], f8, acc[q][2]);
+          acc[q][3] = fmaf(u[3], f8, acc[q][3]);
+        }
+      }
     }
   }
-  y0 = warp_sum(a0);
-  y1 = c1 ? warp_sum(a1) : 0.f;
+  // Lane 4g: columns 0 and 1 (parts hi and mid) of rows g and g + 8.
+  if (c == 0) {
+#pragma unroll
+    for (int q = 0; q < kMaxChunkRows / 16; q++) {
+      const int r0 = q * 16 + g, r8 = r0 + 8;
+      if (r0 < nr) wred[r0] = (first ? 0.f : wred[r0]) + wgt * (acc[q][0] + acc[q][1]);
+      if (r8 < nr) wred[r8] = (first ? 0.f : wred[r8]) + wgt * (acc[q][2] + acc[q][3]);
+    }
+  }
 }
 
-// Gate/up of the selected experts: warp w takes the chunk's pairs w, w + 8,
-// ... (gate row and up row of expert sel[j], output f) and publishes
-// swiglu(gate . x, up . x) in the flagged vector hm (experts this rank does
-// not own: nothing).
-__device__ void consume_mx_gu(const MegaArgs& a, Ring& r, int l, const float* xf, const int* sel,
-                              unsigned e, int ph) {
+// Gate/up of the selected experts, one chunk of np (gate, up) row pairs of
+// expert sel[j] at a time (2 np rows: gate rows then up rows); after each
+// chunk the warps' row sums meet and thread i publishes swiglu(gate_i . x,
+// up_i . x) in the flagged vector hm (experts this rank does not own:
+// nothing). x is vector 0 of the xm region.
+__device__ void consume_mx_gu(const MegaArgs& a, Ring& r, int l, const uint8_t* xm,
+                              const int* sel, unsigned e, int ph) {
   trace_mark(a, ph, MARK_STAGED);
   const Slice s = s_slices[W_EGU];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int cb = a.D / 2, sb = mx_scale_bytes(a.D);
   u64* hm = a.ll + a.llo.hm + (size_t)l * a.topk * a.Fe;
   const bool tr = a.trace != nullptr;
@@ -1108,40 +1225,49 @@ __device__ void consume_mx_gu(const MegaArgs& a, Ring& r, int l, const float* xf
     int p0, np;
     egu_chunk(s.rb / 2, s.re / 2, s.rows / 2, a.Fe, ci, p0, np);
     const int j = p0 / a.Fe, f0 = p0 % a.Fe;
-    if (expert_owned(a, sel[j])) {
-      const uint8_t* buf = reinterpret_cast<const uint8_t*>(r.base + (size_t)b * r.buf_bytes);
-      const uint8_t* gsc = buf + (size_t)2 * np * cb;
-      for (int i = warp; i < np; i += kWarps) {
-        float g, u;
-        mx_rows_dot(buf + (size_t)i * cb, gsc + (size_t)i * sb, buf + (size_t)(np + i) * cb,
-                    gsc + (size_t)(np + i) * sb, a.D, xf, g, u);
-        if (lane == 0) ll_store(hm + (size_t)j * a.Fe + f0 + i, swiglu(g, u), e);
-      }
-    }
+    const bool own = expert_owned(a, sel[j]);
+    float* red = r.red + (size_t)(r.nred & 1) * kWarps * kMaxChunkRows;
+    if (own)
+      mx_chunk_dot(reinterpret_cast<const uint8_t*>(r.base + (size_t)b * r.buf_bytes), 2 * np,
+                   a.D, cb, sb, xm, 1, 0, 1.f, true, red + warp * kMaxChunkRows);
     __syncwarp();
     if (lane == 0) mbar_arrive(r.empty + b);
+    if (own) {
+      r.nred++;
+      csync();
+      if (tid < np) {
+        float gs = 0.f, us = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; w++) {
+          gs += red[w * kMaxChunkRows + tid];
+          us += red[w * kMaxChunkRows + np + tid];
+        }
+        ll_store(hm + (size_t)j * a.Fe + f0 + tid, swiglu(gs, us), e);
+      }
+    }
     r.g++;
   }
-  csync();  // xf (the normalised x) is read no more
+  csync();  // the xm region (the normalised x) is read no more
   trace_mark(a, ph, MARK_CONSUMED);
   trace_put(a, ph, SUM_WAIT, t_wait);
 }
 
-// xf[j][f] = the selected experts' SwiGLU outputs (flagged vector hm,
-// epoch e) for the experts this rank owns.
-__device__ void stage_moe_h(const MegaArgs& a, int l, unsigned e, const int* sel, float* xf,
+// xm vectors j < topk = the selected experts' SwiGLU outputs (flagged
+// vector hm, epoch e), for the experts this rank owns.
+__device__ void stage_moe_h(const MegaArgs& a, int l, unsigned e, const int* sel, uint8_t* xm,
                             int ph) {
   constexpr int B = 16;
   for (int j = 0; j < a.topk; j++) {
     if (!expert_owned(a, sel[j])) continue;
     const u64* src = a.ll + a.llo.hm + ((size_t)l * a.topk + j) * a.Fe;
-    for (int base = threadIdx.x; base < a.Fe; base += B * kThreads) {
+    for (int base = threadIdx.x; base - (int)threadIdx.x < a.Fe; base += B * kThreads) {
       float v[B];
       ll_gather<B>(a, src, base, kThreads, a.Fe, e, v);
 #pragma unroll
       for (int u = 0; u < B; u++) {
+        // A warp's 32 lanes hold one 32-column block (Fe is a multiple of 32).
         const int k = base + u * kThreads;
-        if (k < a.Fe) xf[(size_t)j * a.Fe + k] = v[u];
+        if (k - (k & 31) < a.Fe) xm_put_block(xm, a.Fe, a.topk, j, k, v[u]);
       }
     }
   }
@@ -1150,10 +1276,10 @@ __device__ void stage_moe_h(const MegaArgs& a, int l, unsigned e, const int* sel
 }
 
 // Down rows of the selected experts: one chunk per (row group, expert j);
-// warp w takes rows w, w + 8, ... and adds w_j (down_j[row] . h_j) to the
-// row's sum in choice order; after the last expert, thread t finishes row
-// pair t (residual add, or the tensor-parallel push).
-__device__ void consume_mx_down(const MegaArgs& a, Ring& r, const float* xf, const int* sel,
+// the warps add w_j (down_j[row] . h_j) to their row sums in choice order;
+// after the last expert, thread t finishes row pair t (residual add, or the
+// tensor-parallel push).
+__device__ void consume_mx_down(const MegaArgs& a, Ring& r, const uint8_t* xm, const int* sel,
                                 const float* selw, const Out& o, float& bv, int& bi, int ph) {
   trace_mark(a, ph, MARK_STAGED);
   const Slice s = s_slices[W_EDOWN];
@@ -1170,32 +1296,28 @@ __device__ void consume_mx_down(const MegaArgs& a, Ring& r, const float* xf, con
     if (ci == 0) trace_mark(a, ph, MARK_READY);
     const Chunk ch = slice_chunk(s, phs, ci);
     const int nr = ch.r1 - ch.r0, j = ch.seg;
-    const bool own = expert_owned(a, sel[j]);
-    const float wj = selw[j];
-    const uint8_t* buf = reinterpret_cast<const uint8_t*>(r.base + (size_t)b * r.buf_bytes);
     float* red = r.red + (size_t)(r.nred & 1) * kWarps * kMaxChunkRows;
-    // Two rows per warp pass (shared activation loads, two chains).
-    for (int ri = 2 * warp; ri < nr; ri += 2 * kWarps) {
-      float d0 = 0.f, d1 = 0.f;
-      if (own) {
-        const bool two = ri + 1 < nr;
-        mx_rows_dot(buf + (size_t)ri * cb, buf + (size_t)nr * cb + (size_t)ri * sb,
-                    two ? buf + (size_t)(ri + 1) * cb : nullptr,
-                    buf + (size_t)nr * cb + (size_t)(ri + 1) * sb, a.Fe, xf + (size_t)j * a.Fe,
-                    d0, d1);
-      }
-      if (lane == 0) {
-        red[ri] = (ch.first_seg ? 0.f : red[ri]) + wj * d0;
-        if (ri + 1 < nr) red[ri + 1] = (ch.first_seg ? 0.f : red[ri + 1]) + wj * d1;
-      }
+    float* wred = red + warp * kMaxChunkRows;
+    if (expert_owned(a, sel[j])) {
+      mx_chunk_dot(reinterpret_cast<const uint8_t*>(r.base + (size_t)b * r.buf_bytes), nr, a.Fe,
+                   cb, sb, xm, a.topk, j, selw[j], ch.first_seg, wred);
+    } else if (ch.first_seg && lane == 0) {
+      for (int i = 0; i < nr; i++) wred[i] = 0.f;
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(r.empty + b);
     if (ch.last_seg) {
       r.nred++;
       csync();
-      if (tid < (nr >> 1))
-        pair_epilogue(a, o, W_EDOWN, (ch.r0 >> 1) + tid, red[2 * tid], red[2 * tid + 1], bv, bi);
+      if (tid < (nr >> 1)) {
+        float y0 = 0.f, y1 = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; w++) {
+          y0 += red[w * kMaxChunkRows + 2 * tid];
+          y1 += red[w * kMaxChunkRows + 2 * tid + 1];
+        }
+        pair_epilogue(a, o, W_EDOWN, (ch.r0 >> 1) + tid, y0, y1, bv, bi);
+      }
     }
     r.g++;
   }
@@ -1612,17 +1734,16 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   const int D32 = (a.D + 31) / 32 * 32;
   float* xraw = reinterpret_cast<float*>(dyn + (size_t)nbuf * buf_bytes);  // [D]
   uint16_t* gain_buf = reinterpret_cast<uint16_t*>(xraw + D32);              // [2][D]
-  // MoE: fp32 expert inputs (the normalised x, then the selected experts'
-  // SwiGLU outputs [topk][Fe]).
+  // MoE: the xm region (expert inputs as f16 parts: the normalised x, then
+  // the selected experts' SwiGLU outputs [topk][Fe]).
   float* xf = reinterpret_cast<float*>(gain_buf + 2 * D32);
+  uint8_t* xm = reinterpret_cast<uint8_t*>(xf);
   // Matvec input (bf16 parts) or attention scratch (floats).
-  float* xs = xf + (a.moe ? (max(a.D, a.topk * a.Fe) + 31) / 32 * 32 : 0);
+  float* xs = xf + (a.moe ? moe_xf_floats(a.D, a.topk, a.Fe) : 0);
   uint16_t* xq = reinterpret_cast<uint16_t*>(xs);
   __shared__ int s_csel[kMaxTopk];
   __shared__ float s_cselw[kMaxTopk];
   for (int i = threadIdx.x; i < a.L; i += kBlockThreads) s_layers[i] = a.layers[i];
-  for (int i = threadIdx.x; i < 256; i += kBlockThreads)
-    s_mx_lut[i] = make_float2(kMxE2M1[i & 0xF], kMxE2M1[i >> 4]);
   if (threadIdx.x == 0) {
     for (int i = 0; i < nbuf; i++) {
       mbar_init(&full_bar[i], 1);
@@ -1733,9 +1854,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
           tp_reduce_rows(a, xraw, part0, x_o, s_slices[W_O].rb, s_slices[W_O].re, e);
       }
       ph++;
-      // FFN input: RMSNorm of x_o (for MoE also kept as fp32 in xf)
+      // FFN input: RMSNorm of x_o (for MoE also as f16 parts in xm)
       trace_mark(a, ph, MARK_BEGIN);
-      stage_norm_ll(a, x_o, e, gs, 1, a.D, xq, parts, xraw, red, ph, a.moe ? xf : nullptr);
+      stage_norm_ll(a, x_o, e, gs, 1, a.D, xq, parts, xraw, red, ph, a.moe ? xm : nullptr);
       if (l + 1 < a.L)
         gains_fill(gs, 1, s_layers[l + 1].ffn_norm, a.D);
       else if (s + 1 < a.steps)
@@ -1750,12 +1871,12 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         ph++;
         // gate/up + SwiGLU of the selected experts
         trace_mark(a, ph, MARK_BEGIN);
-        consume_mx_gu(a, r, l, xf, s_csel, e, ph);
+        consume_mx_gu(a, r, l, xm, s_csel, e, ph);
         ph++;
         // down of the selected experts, weighted sum + residual
         trace_mark(a, ph, MARK_BEGIN);
-        stage_moe_h(a, l, e, s_csel, xf, ph);
-        consume_mx_down(a, r, xf, s_csel, s_cselw,
+        stage_moe_h(a, l, e, s_csel, xm, ph);
+        consume_mx_down(a, r, xm, s_csel, s_cselw,
                         Out{x_d, xraw, e, part_d + (size_t)a.rank * a.D}, bv, bi, ph);
         if (a.world > 1)
           tp_reduce_rows(a, xraw, part_d, x_d, s_slices[W_EDOWN].rb, s_slices[W_EDOWN].re, e);
@@ -1896,11 +2017,6 @@ size_t select_attn_floats(int HD, int G) {
 // (rounded to 32 floats), two bf16 gain vectors [D] (same rounding), then
 // the matvec input (`parts` bf16 arrays of K + 32 columns) or the attention
 // scratch.
-// fp32 expert inputs of a mixture of experts (none for a dense model): the
-// normalised x [D], then the selected experts' outputs [topk][Fe].
-int moe_xf_floats(int D, int topk, int Fe) {
-  return topk ? (std::max(D, topk * Fe) + 31) / 32 * 32 : 0;
-}
 
 size_t act_bytes(int D, int QD, int Fl, int HD, int G, int parts, int xf_floats = 0) {
   const size_t kmax = (size_t)std::max(D, std::max(QD, Fl));
