@@ -139,6 +139,8 @@ __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t* r) {
 
 // d += A (16x16 bf16, row-major fragments a0..a3) * B (16x8 bf16, b0/b1),
 // fp32 accumulators (rows g, g + 8; columns 2c, 2c + 1 of lane 4g + c).
+// (Register operands only, so not volatile: the compiler may interleave
+// the steps of independent fragments.)
 __device__ __forceinline__ void mma_bf16(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
@@ -286,14 +288,18 @@ constexpr int kMaxLayers = 96;
 __shared__ MegaLayer s_layers[kMaxLayers];
 
 // Weight phases per layer: dense QKV, O, GU, DOWN; mixture of experts QKV,
-// O, ROUTER, EGU, EDOWN. The LM head follows the last layer.
-__device__ __forceinline__ int phases_per_layer(const MegaArgs& a) { return a.moe ? 5 : 4; }
+// O, ROUTER, EGU, EDOWN. The LM head follows the last layer. MOE (a.moe) is
+// a template parameter of the kernel, so that the dense kernel carries no
+// expert code.
+template <bool MOE>
+__device__ __forceinline__ int phases_per_layer(const MegaArgs&) { return MOE ? 5 : 4; }
 
+template <bool MOE>
 __device__ __forceinline__ int phase_kind(const MegaArgs& a, int wp) {
-  const int P = phases_per_layer(a);
+  const int P = phases_per_layer<MOE>(a);
   if (wp == P * a.L) return W_LM;
   const int i = wp % P;
-  if (!a.moe || i < 2) return i;
+  if (!MOE || i < 2) return i;
   return i == 2 ? W_ROUTER : (i == 3 ? W_EGU : W_EDOWN);
 }
 
@@ -339,13 +345,9 @@ __device__ __forceinline__ float f16_to_f32(uint16_t h) {
 }
 
 // Stores v (element k of vector j of an xm region for K columns) as its two
-// f16 parts. Called by the 32 lanes of a warp together, for the 32 columns
-// of one block (lane 0 at the block's first column): the block scale is the
-// warp's largest magnitude.
-__device__ __forceinline__ void xm_put_block(uint8_t* xm, int K, int nvec, int j, int k, float v) {
-  float m = fabsf(v);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+// f16 parts, m being the largest magnitude of k's 32-column block.
+__device__ __forceinline__ void xm_store(uint8_t* xm, int K, int nvec, int j, int k, float v,
+                                         float m) {
   int sh = 0;
   if (m > 0.f) {
     const int ex = (int)((__float_as_uint(m) >> 23) & 0xFF) - 127;
@@ -362,17 +364,39 @@ __device__ __forceinline__ void xm_put_block(uint8_t* xm, int K, int nvec, int j
         __uint_as_float((uint32_t)(127 - sh) << 23);
 }
 
+// xm_store of v[u] at k = k0 + u * 256 (u < N) by the 32 lanes of a warp
+// together, each k one column of a 32-column block (lane 0 at the block's
+// first column; blocks at or past K are skipped). The N block maxima are
+// reduced side by side, so the shuffle latency is paid once per batch.
+template <int N>
+__device__ __forceinline__ void xm_put_batch(uint8_t* xm, int K, int nvec, int j, int k0,
+                                             const float* v) {
+  float m[N];
+#pragma unroll
+  for (int u = 0; u < N; u++) m[u] = fabsf(v[u]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int u = 0; u < N; u++) m[u] = fmaxf(m[u], __shfl_xor_sync(0xFFFFFFFFu, m[u], o));
+#pragma unroll
+  for (int u = 0; u < N; u++) {
+    const int k = k0 + u * 256;
+    if (k - (k & 31) < K) xm_store(xm, K, nvec, j, k, v[u], m[u]);
+  }
+}
+
 // Weight phase `wp` of a step.
+template <bool MOE>
 __device__ __forceinline__ Phase weight_phase(const MegaArgs& a, int wp) {
   Phase p;
-  p.kind = phase_kind(a, wp);
+  p.kind = phase_kind<MOE>(a, wp);
   if (p.kind == W_LM) {
     p.W = a.out_w;
     p.K = a.D;
     p.pairs = a.Vl / 2;
     return p;
   }
-  const MegaLayer& ly = s_layers[wp / phases_per_layer(a)];
+  const MegaLayer& ly = s_layers[wp / phases_per_layer<MOE>(a)];
   switch (p.kind) {
     case W_QKV:
       p.W = ly.wqkv;
@@ -519,10 +543,11 @@ struct Cursor {
 // shapes, so they are computed once per launch.
 __shared__ Slice s_slices[kKinds];
 
+template <bool MOE>
 __device__ void cursor_skip_empty(const MegaArgs& a, Cursor& c) {
-  const int last = phases_per_layer(a) * a.L;
+  const int last = phases_per_layer<MOE>(a) * a.L;
   while (c.step < a.steps) {
-    if (c.ci < s_slices[phase_kind(a, c.wp)].nchunks) return;
+    if (c.ci < s_slices[phase_kind<MOE>(a, c.wp)].nchunks) return;
     c.ci = 0;
     if (++c.wp > last) {
       c.wp = 0;
@@ -607,6 +632,7 @@ __device__ void produce_mx(const MegaArgs& a, const Phase& ph, const Slice& sl, 
   __syncwarp();
 }
 
+template <bool MOE>
 __device__ void produce(const MegaArgs& a, char* base, int buf_bytes, int nbuf, uint64_t* full,
                         uint64_t* empty) {
   const int lane = threadIdx.x & 31;
@@ -614,7 +640,7 @@ __device__ void produce(const MegaArgs& a, char* base, int buf_bytes, int nbuf, 
   unsigned g = 0;
   int psel_key = -1;  // (step, layer) of s_psel
   for (;;) {
-    cursor_skip_empty(a, c);
+    cursor_skip_empty<MOE>(a, c);
     if (c.step >= a.steps) break;
     const int b = (int)(g % nbuf);
     if (g >= (unsigned)nbuf) {
@@ -622,21 +648,23 @@ __device__ void produce(const MegaArgs& a, char* base, int buf_bytes, int nbuf, 
       __syncwarp();
     }
     if (*(volatile int*)a.err) break;
-    const Phase ph = weight_phase(a, c.wp);
+    const Phase ph = weight_phase<MOE>(a, c.wp);
     const Chunk ch = slice_chunk(s_slices[ph.kind], ph, c.ci);
     char* buf = base + (size_t)b * buf_bytes;
-    if (ph.kind == W_EGU || ph.kind == W_EDOWN) {
-      // The expert rows depend on this step's router output of the layer.
-      const int l = c.wp / phases_per_layer(a);
-      if (psel_key != c.step * a.L + l) {
-        expert_select(a, l, a.epoch + (unsigned)c.step, s_psel, nullptr);
-        psel_key = c.step * a.L + l;
-        if (*(volatile int*)a.err) break;  // the choice may be incomplete
+    if constexpr (MOE) {
+      if (ph.kind == W_EGU || ph.kind == W_EDOWN) {
+        // The expert rows depend on this step's router output of the layer.
+        const int l = c.wp / phases_per_layer<MOE>(a);
+        if (psel_key != c.step * a.L + l) {
+          expert_select(a, l, a.epoch + (unsigned)c.step, s_psel, nullptr);
+          psel_key = c.step * a.L + l;
+          if (*(volatile int*)a.err) break;  // the choice may be incomplete
+        }
+        produce_mx(a, ph, s_slices[ph.kind], ch, c.ci, l, buf, full + b);
+        c.ci++;
+        g++;
+        continue;
       }
-      produce_mx(a, ph, s_slices[ph.kind], ch, c.ci, l, buf, full + b);
-      c.ci++;
-      g++;
-      continue;
     }
     const int nr = ch.r1 - ch.r0, w = ch.k1 - ch.k0;
     const int stride = row_stride(w);
@@ -757,12 +785,25 @@ __device__ void stage_norm_ll(const MegaArgs& a, const u64* src, unsigned e, Gai
   const float inv = 1.0f / sqrtf(ss + a.eps);
   const uint16_t* g = gains_ready(a, gs, gi);
   trace_mark(a, ph, MARK_GAINS);
-  for (int k = tid; k < K; k += kThreads) {
-    const float v = (xraw[k] * inv) * bf16_to_f32(g[k]);
-    xq_put(xq, K, parts, k, v);
-    // MXFP4 expert input (K is then a multiple of 32: a warp's lanes hold
-    // one block)
-    if (xm) xm_put_block(xm, K, 1, 0, k, v);
+  if (xm) {
+    // Also the MXFP4 expert input (K is then a multiple of 32: a warp's
+    // lanes hold one block), in batches of four blocks.
+    for (int k0 = tid; k0 - tid < K; k0 += 4 * kThreads) {
+      float v[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int k = k0 + u * kThreads;
+        v[u] = 0.f;
+        if (k < K) {
+          v[u] = (xraw[k] * inv) * bf16_to_f32(g[k]);
+          xq_put(xq, K, parts, k, v[u]);
+        }
+      }
+      xm_put_batch<4>(xm, K, 1, 0, k0, v);
+    }
+  } else {
+    for (int k = tid; k < K; k += kThreads)
+      xq_put(xq, K, parts, k, (xraw[k] * inv) * bf16_to_f32(g[k]));
   }
   trace_mark(a, ph, MARK_SCALED);
   csync();
@@ -892,10 +933,11 @@ __device__ __forceinline__ void pair_epilogue(const MegaArgs& a, const Out& o, i
 // memory (added up over the column segments of a row group); after the last
 // segment the warps' sums meet and thread t finishes row pair t. For the LM
 // head, (bv, bi) track the thread's argmax.
+template <bool MOE>
 __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const uint16_t* xq, int parts,
                               const Out& o, float& bv, int& bi, int ph) {
   trace_mark(a, ph, MARK_STAGED);
-  const Phase phs = weight_phase(a, wp);
+  const Phase phs = weight_phase<MOE>(a, wp);
   const Slice s = s_slices[phs.kind];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, c = lane & 3;
@@ -1112,7 +1154,7 @@ __device__ __forceinline__ void e2m1x8_to_f16(uint32_t w, uint32_t* h) {
 // d += A (16x16 f16) * B (16x8 f16), fp32 accumulators; fragments as mma_bf16.
 __device__ __forceinline__ void mma_f16(float* d, uint32_t a0, uint32_t a1, uint32_t a2,
                                         uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
       "{%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -1263,12 +1305,11 @@ __device__ void stage_moe_h(const MegaArgs& a, int l, unsigned e, const int* sel
     for (int base = threadIdx.x; base - (int)threadIdx.x < a.Fe; base += B * kThreads) {
       float v[B];
       ll_gather<B>(a, src, base, kThreads, a.Fe, e, v);
+      // A warp's 32 lanes hold one 32-column block (Fe is a multiple of 32).
 #pragma unroll
-      for (int u = 0; u < B; u++) {
-        // A warp's 32 lanes hold one 32-column block (Fe is a multiple of 32).
-        const int k = base + u * kThreads;
-        if (k - (k & 31) < a.Fe) xm_put_block(xm, a.Fe, a.topk, j, k, v[u]);
-      }
+      for (int u = 0; u < B; u++)
+        if (base + u * kThreads >= a.Fe) v[u] = 0.f;
+      xm_put_batch<B>(xm, a.Fe, a.topk, j, base, v);
     }
   }
   trace_mark(a, ph, MARK_INPUTS);
@@ -1719,7 +1760,7 @@ __device__ void merge_item(const MegaArgs& a, int l, int kh, int pos, unsigned e
 // ---------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------
-template <int HD, int G>
+template <int HD, int G, bool MOE>
 __global__ void __launch_bounds__(kBlockThreads, 1)
     k_mega_decode(const __grid_constant__ MegaArgs a, int buf_bytes, int nbuf, int parts) {
   extern __shared__ __align__(128) char dyn[];
@@ -1739,7 +1780,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   float* xf = reinterpret_cast<float*>(gain_buf + 2 * D32);
   uint8_t* xm = reinterpret_cast<uint8_t*>(xf);
   // Matvec input (bf16 parts) or attention scratch (floats).
-  float* xs = xf + (a.moe ? moe_xf_floats(a.D, a.topk, a.Fe) : 0);
+  float* xs = xf + (MOE ? moe_xf_floats(a.D, a.topk, a.Fe) : 0);
   uint16_t* xq = reinterpret_cast<uint16_t*>(xs);
   __shared__ int s_csel[kMaxTopk];
   __shared__ float s_cselw[kMaxTopk];
@@ -1757,18 +1798,18 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   if (threadIdx.x < kKinds) {
     // Layer 0's phases stand for every layer (same shapes); kinds the model
     // does not have get no chunks.
-    const int k = threadIdx.x, P = phases_per_layer(a);
+    const int k = threadIdx.x, P = phases_per_layer<MOE>(a);
     int wp = -1;
     if (k == W_LM)
       wp = P * a.L;
     else if (k == W_QKV || k == W_O)
       wp = k;
-    else if (!a.moe && (k == W_GU || k == W_DOWN))
+    else if (!MOE && (k == W_GU || k == W_DOWN))
       wp = k;
-    else if (a.moe && k >= W_ROUTER)
+    else if (MOE && k >= W_ROUTER)
       wp = k - W_ROUTER + 2;
     if (wp >= 0) {
-      s_slices[k] = cta_slice(weight_phase(a, wp), buf_bytes, a.topk, a.Fe);
+      s_slices[k] = cta_slice(weight_phase<MOE>(a, wp), buf_bytes, a.topk, a.Fe);
     } else {
       Slice z = {0, 0, 2, 0, 1, 0};
       s_slices[k] = z;
@@ -1776,7 +1817,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   }
   __syncthreads();
   if (warp == kWarps) {
-    produce(a, dyn, buf_bytes, nbuf, full_bar, empty_bar);
+    produce<MOE>(a, dyn, buf_bytes, nbuf, full_bar, empty_bar);
     return;
   }
   Ring r;
@@ -1800,7 +1841,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   int token = __ldcg(a.tok);
   int step = __ldcg(a.step);
   const int QD = a.QHl * a.HD;
-  const int P = phases_per_layer(a);
+  const int P = phases_per_layer<MOE>(a);
   const int attn_items = a.KHl * a.nsplit;
   float bv = -INFINITY;
   int bi = 0x7FFFFFFF;
@@ -1828,7 +1869,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
       else
         stage_norm_ll(a, x_o - 2 * (size_t)a.D + a.D, e, gs, 0, a.D, xq, parts, xraw, red, ph);
       gains_fill(gs, 0, l + 1 < a.L ? s_layers[l + 1].attn_norm : a.out_norm, a.D);
-      consume_phase(a, r, P * l + 0, xq, parts,
+      consume_phase<MOE>(a, r, P * l + 0, xq, parts,
                     Out{a.ll + a.llo.qkv + (size_t)l * a.QKVl, nullptr, e}, bv, bi, ph);
       ph++;
       // ATTN
@@ -1848,7 +1889,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
       stage_plain_ll(a, a.ll + a.llo.att + (size_t)l * QD, e, QD, xq, parts, ph);
       {
         const size_t part0 = a.llo.xpart + (size_t)(l * 2 + 0) * a.world * a.D;
-        consume_phase(a, r, P * l + 1, xq, parts,
+        consume_phase<MOE>(a, r, P * l + 1, xq, parts,
                       Out{x_o, xraw, e, part0 + (size_t)a.rank * a.D}, bv, bi, ph);
         if (a.world > 1)
           tp_reduce_rows(a, xraw, part0, x_o, s_slices[W_O].rb, s_slices[W_O].re, e);
@@ -1856,15 +1897,15 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
       ph++;
       // FFN input: RMSNorm of x_o (for MoE also as f16 parts in xm)
       trace_mark(a, ph, MARK_BEGIN);
-      stage_norm_ll(a, x_o, e, gs, 1, a.D, xq, parts, xraw, red, ph, a.moe ? xm : nullptr);
+      stage_norm_ll(a, x_o, e, gs, 1, a.D, xq, parts, xraw, red, ph, MOE ? xm : nullptr);
       if (l + 1 < a.L)
         gains_fill(gs, 1, s_layers[l + 1].ffn_norm, a.D);
       else if (s + 1 < a.steps)
         gains_fill(gs, 1, s_layers[0].ffn_norm, a.D);
       const size_t part_d = a.llo.xpart + (size_t)(l * 2 + 1) * a.world * a.D;
-      if (a.moe) {
+      if constexpr (MOE) {
         // router logits, then every CTA picks the experts
-        consume_phase(a, r, P * l + 2, xq, parts,
+        consume_phase<MOE>(a, r, P * l + 2, xq, parts,
                       Out{a.ll + a.llo.rl + (size_t)l * a.E, nullptr, e}, bv, bi, ph);
         if (warp == 0) expert_select(a, l, e, s_csel, s_cselw);
         csync();
@@ -1883,13 +1924,13 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         ph++;
       } else {
         // gate/up + SwiGLU
-        consume_phase(a, r, P * l + 2, xq, parts,
+        consume_phase<MOE>(a, r, P * l + 2, xq, parts,
                       Out{a.ll + a.llo.h + (size_t)l * a.Fl, nullptr, e}, bv, bi, ph);
         ph++;
         // down + residual
         trace_mark(a, ph, MARK_BEGIN);
         stage_plain_ll(a, a.ll + a.llo.h + (size_t)l * a.Fl, e, a.Fl, xq, parts, ph);
-        consume_phase(a, r, P * l + 3, xq, parts,
+        consume_phase<MOE>(a, r, P * l + 3, xq, parts,
                       Out{x_d, xraw, e, part_d + (size_t)a.rank * a.D}, bv, bi, ph);
         if (a.world > 1)
           tp_reduce_rows(a, xraw, part_d, x_d, s_slices[W_DOWN].rb, s_slices[W_DOWN].re, e);
@@ -1903,7 +1944,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     if (s + 1 < a.steps) gains_fill(gs, 0, s_layers[0].attn_norm, a.D);
     bv = -INFINITY;
     bi = 0x7FFFFFFF;
-    consume_phase(a, r, P * a.L, xq, parts, Out{nullptr, nullptr, e}, bv, bi, ph);
+    consume_phase<MOE>(a, r, P * a.L, xq, parts, Out{nullptr, nullptr, e}, bv, bi, ph);
     // Warp argmax (ties: lower index), then the warps' in order.
     for (int o = 16; o > 0; o >>= 1) {
       const float v2 = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
@@ -1989,13 +2030,13 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
 }
 
 template <int HD, int G>
-void* kernel_ptr() {
-  return (void*)k_mega_decode<HD, G>;
+void* kernel_ptr(bool moe) {
+  return moe ? (void*)k_mega_decode<HD, G, true> : (void*)k_mega_decode<HD, G, false>;
 }
 
-void* select(int HD, int G) {
+void* select(int HD, int G, bool moe = false) {
 #define SG_SEL(h, g) \
-  if (HD == h && G == g) return kernel_ptr<h, g>();
+  if (HD == h && G == g) return kernel_ptr<h, g>(moe);
   SG_SEL(32, 1) SG_SEL(32, 2) SG_SEL(32, 4) SG_SEL(32, 8)
   SG_SEL(64, 1) SG_SEL(64, 2) SG_SEL(64, 4) SG_SEL(64, 8)
   SG_SEL(128, 1) SG_SEL(128, 2) SG_SEL(128, 4) SG_SEL(128, 8)
@@ -2033,8 +2074,10 @@ size_t smem_budget(int HD, int G) {
   const int hi = HD == 32 ? 0 : HD == 64 ? 1 : 2;
   const int gi = G == 1 ? 0 : G == 2 ? 1 : G == 4 ? 2 : 3;
   if (!cached[hi][gi]) {
-    cudaFuncAttributes fa;
-    SG_CUDA(cudaFuncGetAttributes(&fa, select(HD, G)));
+    cudaFuncAttributes fa, fm;
+    SG_CUDA(cudaFuncGetAttributes(&fa, select(HD, G, false)));
+    SG_CUDA(cudaFuncGetAttributes(&fm, select(HD, G, true)));
+    fa.sharedSizeBytes = std::max(fa.sharedSizeBytes, fm.sharedSizeBytes);
     int dev = 0, optin = 0;
     SG_CUDA(cudaGetDevice(&dev));
     SG_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
@@ -2135,16 +2178,21 @@ static int buffer_bytes(size_t smem, int D, int QD, int Fl, int HD, int G, int x
 void mega_configure(size_t smem) {
   for (int hd : {32, 64, 128})
     for (int g : {1, 2, 4, 8})
-      SG_CUDA(cudaFuncSetAttribute(select(hd, g), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)std::max(smem, (size_t)48 * 1024)));
+      for (bool moe : {false, true})
+        SG_CUDA(cudaFuncSetAttribute(select(hd, g, moe),
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)std::max(smem, (size_t)48 * 1024)));
 }
 
 int mega_grid(size_t smem, int HD, int G) {
   void* k = select(HD, G);
   if (!k || smem == 0) return 0;
-  int per_sm = 0;
-  SG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kBlockThreads, smem));
-  if (per_sm < 1) return 0;
+  for (bool moe : {false, true}) {
+    int per_sm = 0;
+    SG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, select(HD, G, moe),
+                                                          kBlockThreads, smem));
+    if (per_sm < 1) return 0;
+  }
   int dev, sms;
   SG_CUDA(cudaGetDevice(&dev));
   SG_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
@@ -2162,7 +2210,7 @@ void mega_split(int ctx, int KHl, int grid, int* nsplit, int* split_len) {
 }
 
 void mega_decode(const MegaArgs& a, int grid, size_t smem, cudaStream_t s) {
-  void* k = select(a.HD, a.G);
+  void* k = select(a.HD, a.G, a.moe != 0);
   if (!k) SG_DIE("megakernel: unsupported head_dim / group");
   if (a.nsplit > kMaxSplits) SG_DIE("megakernel: too many attention splits");
   if (a.L > kMaxLayers) SG_DIE("megakernel: too many layers");
