@@ -117,6 +117,23 @@ __device__ __forceinline__ void bulk_copy(void* dst, const void* src, unsigned b
       : "memory");
 }
 
+// The same for weight rows, which are read once per step: marked
+// evict-first in L2, so that the weight stream (GBs per step) does not push
+// out what the kernel reuses (its own instructions, the flagged vectors,
+// the K/V rows).
+__device__ __forceinline__ void bulk_copy_stream(void* dst, const void* src, unsigned bytes,
+                                                 uint64_t* bar) {
+  asm volatile(
+      "{\n"
+      " .reg .b64 pol;\n"
+      " createpolicy.fractional.L2::evict_first.b64 pol, 1.0;\n"
+      " cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], pol;\n"
+      "}" ::"r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
@@ -610,10 +627,10 @@ __device__ void produce_mx(const MegaArgs& a, const Phase& ph, const Slice& sl, 
       mbar_expect_tx(bar, own ? (unsigned)(2 * np * (cb + sb)) : 0u);
       if (own) {
         const size_t row = (size_t)(s_psel[j] - a.e_begin) * a.Fe + f0;
-        bulk_copy(buf, ly.gate_c + row * cb, (unsigned)(np * cb), bar);
-        bulk_copy(buf + (size_t)np * cb, ly.up_c + row * cb, (unsigned)(np * cb), bar);
-        bulk_copy(buf + (size_t)2 * np * cb, ly.gate_s + row * sb, (unsigned)(np * sb), bar);
-        bulk_copy(buf + (size_t)2 * np * cb + (size_t)np * sb, ly.up_s + row * sb,
+        bulk_copy_stream(buf, ly.gate_c + row * cb, (unsigned)(np * cb), bar);
+        bulk_copy_stream(buf + (size_t)np * cb, ly.up_c + row * cb, (unsigned)(np * cb), bar);
+        bulk_copy_stream(buf + (size_t)2 * np * cb, ly.gate_s + row * sb, (unsigned)(np * sb), bar);
+        bulk_copy_stream(buf + (size_t)2 * np * cb + (size_t)np * sb, ly.up_s + row * sb,
                   (unsigned)(np * sb), bar);
       }
     }
@@ -624,8 +641,8 @@ __device__ void produce_mx(const MegaArgs& a, const Phase& ph, const Slice& sl, 
       mbar_expect_tx(bar, own ? (unsigned)(nr * (cb + sb)) : 0u);
       if (own) {
         const size_t row = (size_t)(s_psel[j] - a.e_begin) * a.D + ch.r0;
-        bulk_copy(buf, ly.down_c + row * cb, (unsigned)(nr * cb), bar);
-        bulk_copy(buf + (size_t)nr * cb, ly.down_s + row * sb, (unsigned)(nr * sb), bar);
+        bulk_copy_stream(buf, ly.down_c + row * cb, (unsigned)(nr * cb), bar);
+        bulk_copy_stream(buf + (size_t)nr * cb, ly.down_s + row * sb, (unsigned)(nr * sb), bar);
       }
     }
   }
@@ -672,7 +689,7 @@ __device__ void produce(const MegaArgs& a, char* base, int buf_bytes, int nbuf, 
     __syncwarp();
     const uint16_t* src = ph.W + (size_t)ch.r0 * ph.K + ch.k0;
     for (int r = lane; r < nr; r += 32)
-      bulk_copy(buf + (size_t)r * stride, src + (size_t)r * ph.K, (unsigned)(w * 2), full + b);
+      bulk_copy_stream(buf + (size_t)r * stride, src + (size_t)r * ph.K, (unsigned)(w * 2), full + b);
     c.ci++;
     g++;
   }
