@@ -1102,8 +1102,8 @@ __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const uint16_t
 // Expert choice for layer l from its router logits (flagged vector rl,
 // epoch e), as the per-op router (kernels.cu moe_topk): topk rounds of the
 // warp argmax (ties -> lower index), then the softmax over the chosen
-// logits in choice order. One warp; lane 0 writes sel[topk] and, when w is
-// set, w[topk]; the warp is synchronised on return.
+// logits in choice order. One warp; lanes s < topk write sel[s] and, when
+// w is set, w[s]; the warp is synchronised on return.
 __device__ void expert_select(const MegaArgs& a, int l, unsigned e, int* sel, float* w) {
   const int lane = threadIdx.x & 31;
   float v[4];  // E <= 128
@@ -1111,8 +1111,11 @@ __device__ void expert_select(const MegaArgs& a, int l, unsigned e, int* sel, fl
 #pragma unroll
   for (int u = 0; u < 4; u++)
     if (lane + 32 * u >= a.E) v[u] = -INFINITY;
-  float chosen[kMaxTopk];
-  int ci[kMaxTopk];
+  // Round s's winner stays in lane s (registers only: arrays indexed by
+  // the runtime round would live in local memory, one L2 round trip per
+  // access).
+  float mine = -INFINITY;
+  int mine_i = 0;
   for (int s = 0; s < a.topk; s++) {
     float best = -INFINITY;
     int bi = 0x7FFFFFFF;
@@ -1132,23 +1135,23 @@ __device__ void expert_select(const MegaArgs& a, int l, unsigned e, int* sel, fl
         bi = i2;
       }
     }
-    chosen[s] = best;
-    ci[s] = bi;
+    if (lane == s) {
+      mine = best;
+      mine_i = bi;
+    }
 #pragma unroll
     for (int u = 0; u < 4; u++)
       if (lane + 32 * u == bi) v[u] = -INFINITY;
   }
-  if (lane == 0) {
-    const float mx = chosen[0];
-    float ex[kMaxTopk], sum = 0.f;
-    for (int s = 0; s < a.topk; s++) {
-      ex[s] = expf(chosen[s] - mx);
-      sum += ex[s];
-    }
-    for (int s = 0; s < a.topk; s++) {
-      sel[s] = ci[s];
-      if (w) w[s] = ex[s] / sum;
-    }
+  // Softmax over the chosen logits, the sum taken in choice order (every
+  // lane takes part in every shuffle).
+  const float mx = __shfl_sync(0xFFFFFFFFu, mine, 0);
+  const float ex = lane < a.topk ? expf(mine - mx) : 0.f;
+  float sum = 0.f;
+  for (int s = 0; s < a.topk; s++) sum += __shfl_sync(0xFFFFFFFFu, ex, s);
+  if (lane < a.topk) {
+    sel[lane] = mine_i;
+    if (w) w[lane] = ex / sum;
   }
   __syncwarp();
 }
@@ -1394,7 +1397,9 @@ __device__ void tp_reduce_rows(const MegaArgs& a, const float* xraw, size_t part
     float v[kTpMaxWorld];
     ll_gather<kTpMaxWorld, true>(a, a.ll + part0, r, a.D, a.world * a.D, e, v);
     float s = v[0];
-    for (int p = 1; p < a.world; p++) s += v[p];
+#pragma unroll
+    for (int p = 1; p < kTpMaxWorld; p++)
+      if (p < a.world) s += v[p];
     ll_store(dst + r, xraw[r] + s, e);
   }
 }
