@@ -1,4 +1,5 @@
-// Persistent decode megakernel for dense models (see mega.h).
+// Persistent decode megakernel (see mega.h), for dense models and, as a
+// compile-time variant (MOE), for mixtures of MXFP4 experts.
 //
 // One CTA per SM (cooperative launch, so all CTAs are co-resident), 8
 // warps. A decode step is a fixed sequence of phases; each phase splits its
@@ -10,6 +11,11 @@
 //              O       att -> Wo rows, residual add             -> x
 //              GU      x -> RMSNorm -> gate/up row pairs, SwiGLU -> h
 //              DOWN    h -> Wd rows, residual add               -> x
+//   (MOE: GU, DOWN are ROUTER  x -> RMSNorm -> router rows   -> logits,
+//              every CTA picks the top-k experts from the logits;
+//              EGU     gate/up rows of the chosen experts, SwiGLU -> h[k]
+//              EDOWN   down rows of the chosen experts, weighted in
+//                      choice order, residual add               -> x)
 //   LM head    x -> RMSNorm -> vocab rows (+ per-CTA argmax)     -> am
 //   argmax     every CTA reduces the per-CTA partials           -> token
 //
@@ -30,8 +36,10 @@
 // A ninth warp is the producer: it walks that list and, for each of the
 // ring buffers, waits until the consumers have released the buffer (empty
 // mbarrier), then copies the chunk's rows into it with one cp.async.bulk per
-// row (into its own CTA's buffer only), completion counted on the buffer's
-// full mbarrier. Rows sit kPad bytes further apart than in memory, so the
+// row (into its own CTA's buffer only; MXFP4 expert chunks: a few copies
+// of contiguous runs), completion counted on the buffer's full mbarrier.
+// The weight copies are marked evict-first in L2, so that the stream does
+// not push out the kernel's instructions, flagged vectors and K/V rows. Rows sit kPad bytes further apart than in memory, so the
 // eight rows of a tensor-core fragment fall into different banks. Weights
 // never depend on activations, so copies run ahead across phase and layer
 // boundaries while the consumers wait for their inputs. Attention CTAs
@@ -44,7 +52,10 @@
 // padded buffer) by B = the parts (columns 0..2 of 8) over 16 columns; the
 // fp32 accumulator columns are summed at the end. Each of the eight
 // consumer warps takes every eighth 32-column block of the chunk for all of
-// its rows, and the warps' partial sums meet in shared memory.
+// its rows, and the warps' partial sums meet in shared memory. MXFP4 rows
+// go through the same fragments: e2m1 codes converted to f16 in registers,
+// the activation as two f16 parts with a scale per 32-column block
+// (mx_chunk_dot).
 //
 // Every wait is bounded (2 s): a timeout sets *err, later waits return at
 // once, the kernel runs to its end and the host reports the error. The
