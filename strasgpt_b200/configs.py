@@ -102,6 +102,23 @@ C5 = ModelConfig("c5_mistral24b", "mistral", 5120, 32768, 40, 32, 8, 128,
 
 BENCH = {c.name: c for c in (C1, C2, C3, C4, C5)}
 
+# C5's width (D 5120, F 32768, 32/8 heads, theta 1e8, untied) and its full
+# 8192-token prompt on 4 layers: the long-context paths (8448-row KV
+# attention, multi-chunk prefill) at a CPU cost the reference finishes in
+# minutes, for a full-logits parity fixture.
+C5_L4 = C5.with_(name="c5_mistral24b_l4", layers=4, steps=64)
+
+PARITY = {c.name: c for c in (C5_L4,)}
+
+# C3's layer shapes on 2 layers with a 32768-row LM head and a 64-token
+# prompt: the small case (about 1.4 GB on the device) on which the decode
+# kernel is captured under ncu; its DRAM traffic over algorithmic bytes
+# carries over to C3, whose layers are identical.
+C3_S = C3.with_(name="c3s_llama8b_l2", layers=2, vocab=32768, prompt_len=64,
+                steps=8, bos_token_id=1, eos_token_id=2)
+
+PROFILE = {c.name: c for c in (C3_S,)}
+
 # Small shapes with the same structural features, for fast parity tests.
 T_LLAMA = ModelConfig("t_llama", "llama", 256, 512, 2, 8, 2, 32, 1024,
                       500000.0, 1e-5, tied=True, prompt_len=8, steps=8)
@@ -124,7 +141,7 @@ T_MOE = ModelConfig("t_moe", "strasgpt_moe", 256, 256, 2, 8, 2, 32, 1024,
 TINY = {c.name: c for c in (T_LLAMA, T_QWEN, T_UNTIED, T_GQA8, T_INTERLEAVED,
                             T_CHUNK, T_MOE)}
 
-ALL = {**BENCH, **TINY}
+ALL = {**BENCH, **PARITY, **PROFILE, **TINY}
 
 
 def get(name: str) -> ModelConfig:

@@ -115,7 +115,7 @@ template <int EPI>
 __device__ __forceinline__ void matvec_rows(int item, int rows, int& r0,
                                             int& r1, bool& has1) {
   if (EPI == EPI_SWIGLU) {
-    r0 = (item / SG_GU_GROUP) * (2 * SG_GU_GROUP) + item % SG_GU_GROUP;
+    r0 = gu_gate_row(item);
     r1 = r0 + SG_GU_GROUP;
     has1 = true;  // `rows` counts outputs; the up row always exists
   } else {

@@ -15,6 +15,12 @@
 
 namespace sg {
 
+// Row of the gate weights of SwiGLU output i in the interleaved gate/up
+// matrix; the matching up row is SG_GU_GROUP rows further.
+__host__ __device__ __forceinline__ int gu_gate_row(int i) {
+  return (i / SG_GU_GROUP) * (2 * SG_GU_GROUP) + i % SG_GU_GROUP;
+}
+
 enum Epilogue { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2 };
 
 // out[t][e] = bf16->f32(emb[tok[t]][e]) for t < T.

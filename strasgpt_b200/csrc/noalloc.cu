@@ -38,7 +38,7 @@ namespace {
 constexpr int kScratchFloats = STRASGPT_NOALLOC_SCRATCH_BYTES / 4;
 constexpr int kMaxSplits = 64;      // also the sums-of-squares slots
 constexpr int kRowsPerCta = 8;      // one warp per weight row
-constexpr int kTargetCtas = 148 * 8;
+constexpr int kCtasPerSm = 8;       // split-K target: this many CTAs per SM
 
 // The scratch itself. In host code this name is only a stand-in for the
 // symbol; its device address comes from cudaGetSymbolAddress.
@@ -103,8 +103,10 @@ __global__ void __launch_bounds__(256)
     for (int s = 0; s < nsplit; s++) v += part[(size_t)s * wrows + r];
     return v * scale;
   };
-  if (epi == STRASGPT_EPI_SWIGLU)
-    out[i] = sg::swiglu(total(2 * i), total(2 * i + 1));
+  if (epi == STRASGPT_EPI_SWIGLU) {
+    const int gate = sg::gu_gate_row(i);
+    out[i] = sg::swiglu(total(gate), total(gate + SG_GU_GROUP));
+  }
   else if (epi == STRASGPT_EPI_ADD)
     out[i] += total(i);
   else
@@ -113,15 +115,19 @@ __global__ void __launch_bounds__(256)
 
 std::mutex g_setup_mutex;
 float* g_scratch_on_device[64];
+int g_sms_on_device[64];
 
 // Device address of g_noalloc_scratch on the current device, resolved once
-// per device.
-float* scratch_on_current_device() {
+// per device, and that device's SM count (which sizes the split).
+float* scratch_on_current_device(int* sms) {
   int dev = 0;
   SG_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) SG_DIE("strasgpt_k_matvec_noalloc: device index above 63");
   std::lock_guard<std::mutex> lock(g_setup_mutex);
   if (!g_scratch_on_device[dev]) {
+    int n = 0;
+    SG_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+    g_sms_on_device[dev] = n > 0 ? n : 1;
     float* ptr = nullptr;
     const cudaError_t e = cudaGetSymbolAddress((void**)&ptr, g_noalloc_scratch);
     if (e != cudaSuccess || ptr == nullptr) {
@@ -132,6 +138,7 @@ float* scratch_on_current_device() {
     }
     g_scratch_on_device[dev] = ptr;
   }
+  *sms = g_sms_on_device[dev];
   return g_scratch_on_device[dev];
 }
 
@@ -153,6 +160,8 @@ extern "C" int strasgpt_k_matvec_noalloc(const float* x, const uint16_t* norm_w,
   if (!x || !w || !out) return reject("null buffer");
   if (!aligned16(x) || !aligned16(w) || (norm_w && !aligned16(norm_w)))
     return reject("x, w and norm_w must be 16-byte aligned");
+  if (epi == STRASGPT_EPI_SWIGLU && rows % SG_GU_GROUP != 0)
+    return reject("SwiGLU rows must be a multiple of the gate/up group");
   const long long wrows = epi == STRASGPT_EPI_SWIGLU ? 2LL * rows : (long long)rows;
   if (wrows + kMaxSplits > kScratchFloats) {
     char m[200];
@@ -162,8 +171,10 @@ extern "C" int strasgpt_k_matvec_noalloc(const float* x, const uint16_t* norm_w,
              wrows, STRASGPT_NOALLOC_SCRATCH_BYTES, kScratchFloats - kMaxSplits);
     return reject(m);
   }
+  int sms = 1;
+  float* scratch = scratch_on_current_device(&sms);
   const int row_blocks = (int)((wrows + kRowsPerCta - 1) / kRowsPerCta);
-  int nsplit = (kTargetCtas + row_blocks - 1) / row_blocks;
+  int nsplit = (sms * kCtasPerSm + row_blocks - 1) / row_blocks;
   nsplit = std::min(nsplit, kMaxSplits);
   nsplit = std::min(nsplit, (k + 255) / 256);
   nsplit = std::min(nsplit, (int)((kScratchFloats - kMaxSplits) / wrows));
@@ -172,7 +183,6 @@ extern "C" int strasgpt_k_matvec_noalloc(const float* x, const uint16_t* norm_w,
   ks = (ks + 7) & ~7;
   nsplit = (k + ks - 1) / ks;
 
-  float* scratch = scratch_on_current_device();
   cudaStream_t s = (cudaStream_t)stream;
   const dim3 grid(row_blocks, nsplit);
   const int rgrid = (rows + 255) / 256;

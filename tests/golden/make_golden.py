@@ -9,8 +9,10 @@ against:
   - small shapes (`t_*`): every step's full fp32 logits (<name>.npz);
   - benchmark shapes (`c*`): per step the top-16 (id, logit), the logit
     mean/std/max, the top-1 minus top-2 margin, and the dot of the logits
-    with 4 fixed random unit vectors (<name>.json) - enough to bound the
-    logit error without storing 0.5-0.8 MB per step.
+    with 4 fixed random unit vectors (<name>.json); plus the full fp32
+    logits of the prefill row and of FULL_ROWS evenly spaced decode steps
+    (<name>_logits.npz: `steps`, `logits` [n][V]), for the full-vocabulary
+    max-abs and cosine checks.
 Checker: the reference's own forward pass compiled from its sources
 (oracle.Reference) for dense models; this project's restatement
 (oracle.Restatement) for the MoE models the reference does not have.
@@ -36,6 +38,7 @@ import oracle  # noqa: E402
 
 CACHE = os.environ.get("STRASGPT_MODEL_CACHE", "/tmp/strasgpt_models")
 PROJECTIONS = 4
+FULL_ROWS = 8
 
 
 def file_sha256(path: str) -> str:
@@ -69,6 +72,13 @@ def step_summary(logits: np.ndarray, proj: np.ndarray) -> dict:
     }
 
 
+def full_rows(steps: int) -> list:
+    """Step 0 (the prefill row) and FULL_ROWS decode steps spread evenly
+    over 1..steps."""
+    picks = np.linspace(1, steps, min(FULL_ROWS, steps)).round().astype(int)
+    return [0] + sorted({int(s) for s in picks})
+
+
 def make(name: str) -> None:
     cfg = configs.get(name)
     d = synth.write_model(os.path.join(CACHE, f"{cfg.name}_s0"), cfg, seed=0)
@@ -95,6 +105,11 @@ def make(name: str) -> None:
     else:
         proj = projection_vectors(cfg.vocab)
         meta["steps"] = [step_summary(l, proj) for l in logits]
+        rows = full_rows(cfg.steps)
+        meta["full_rows"] = rows
+        np.savez_compressed(os.path.join(HERE, f"{name}_logits.npz"),
+                            steps=np.array(rows, dtype=np.int32),
+                            logits=np.stack([logits[s] for s in rows]).astype(np.float32))
         if gaps is not None:
             # Smallest top-k router margin over the layers (and, for the
             # prompt, its tokens) of each step.
