@@ -75,7 +75,8 @@ constexpr int kThreads = 256;               // consumer threads
 constexpr int kWarps = kThreads / 32;       // consumer warps
 constexpr int kBlockThreads = kThreads + 32;  // + the producer warp
 constexpr int kPosPerPass = kWarps * 8;  // cache rows per CTA pass
-constexpr int kMaxChunkRows = 64;        // rows per weight chunk (4 fragments)
+constexpr int kMaxChunkRows = 64;        // rows per MXFP4 weight chunk (4 fragments)
+constexpr int kMaxDenseRows = 32;        // rows per bf16 weight chunk (2 fragments)
 constexpr int kPad = 16;                 // extra bytes per row in a buffer
 constexpr int kMaxRing = 4;              // weight buffers per CTA (at most)
 constexpr int kMaxSplits = 64;
@@ -170,7 +171,7 @@ __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t* r) {
 // (Register operands only, so not volatile: the compiler may interleave
 // the steps of independent fragments.)
 __device__ __forceinline__ void mma_bf16(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
       "{%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -507,8 +508,9 @@ __device__ __forceinline__ Slice cta_slice(const Phase& ph, int buf_bytes, int t
   s.rb = 2 * (int)(np * blockIdx.x / gridDim.x);
   s.re = 2 * (int)(np * (blockIdx.x + 1) / gridDim.x);
   const int n = s.re - s.rb;
-  const int want = min(kMaxChunkRows, max(n, 2));
-  if (ph.kind == W_EGU || ph.kind == W_EDOWN) {
+  const bool mx = ph.kind == W_EGU || ph.kind == W_EDOWN;
+  const int want = min(mx ? kMaxChunkRows : kMaxDenseRows, max(n, 2));
+  if (mx) {
     // Whole MXFP4 rows; the down rows once per selected expert; gate/up
     // chunks end at expert boundaries.
     s.rows = max(2, min(want, (buf_bytes / mx_row_bytes(ph.K)) & ~1));
@@ -585,23 +587,23 @@ __device__ void cursor_skip_empty(const MegaArgs& a, Cursor& c) {
 }
 
 // Bounded wait on an mbarrier phase; with `stop_on_err` it also returns as
-// soon as the error flag is set. `nap` (ns) between polls keeps a waiting
-// producer from taking issue slots from the consumer warps beside it.
-__device__ void wait_bar(const MegaArgs& a, uint64_t* bar, unsigned parity,
-                         bool stop_on_err = true, unsigned nap = 0) {
-  if (mbar_try_wait(bar, parity)) return;
+// soon as the error flag is set. True when the phase completed. The error
+// flag (global memory, one L2 round trip) is read only while waiting.
+__device__ bool wait_bar(const MegaArgs& a, uint64_t* bar, unsigned parity,
+                         bool stop_on_err = true) {
+  if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = now_ns();
   unsigned spins = 0;
   while (!mbar_try_wait(bar, parity)) {
-    if (nap) __nanosleep(nap);
     if ((++spins & 63) == 0) {
-      if (stop_on_err && *(volatile int*)a.err) return;
+      if (stop_on_err && *(volatile int*)a.err) return false;
       if (now_ns() - t0 > kTimeoutNs) {
         atomicExch(a.err, 2);
-        return;
+        return false;
       }
     }
   }
+  return true;
 }
 
 // The producer warp: copies every chunk of the launch, in the consumers'
@@ -672,10 +674,12 @@ __device__ void produce(const MegaArgs& a, char* base, int buf_bytes, int nbuf, 
     if (c.step >= a.steps) break;
     const int b = (int)(g % nbuf);
     if (g >= (unsigned)nbuf) {
-      if (lane == 0) wait_bar(a, empty + b, (g / nbuf - 1) & 1, true, 128);
-      __syncwarp();
+      // Only a wait that ran out (or saw the error flag) stops the
+      // producer: no global load per chunk.
+      int ok = 1;
+      if (lane == 0) ok = wait_bar(a, empty + b, (g / nbuf - 1) & 1) ? 1 : 0;
+      if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) break;
     }
-    if (*(volatile int*)a.err) break;
     const Phase ph = weight_phase<MOE>(a, c.wp);
     const Chunk ch = slice_chunk(s_slices[ph.kind], ph, c.ci);
     char* buf = base + (size_t)b * buf_bytes;
@@ -830,8 +834,21 @@ __device__ void stage_norm_ll(const MegaArgs& a, const u64* src, unsigned e, Gai
       xm_put_batch<4>(xm, K, 1, 0, k0, v);
     }
   } else {
-    for (int k = tid; k < K; k += kThreads)
-      xq_put(xq, K, parts, k, (xraw[k] * inv) * bf16_to_f32(g[k]));
+    // Four elements per iteration, their loads first (independent chains).
+    for (int k0 = tid; k0 < K; k0 += 4 * kThreads) {
+      float xv[4], gv[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int k = k0 + u * kThreads;
+        xv[u] = k < K ? xraw[k] : 0.f;
+        gv[u] = k < K ? bf16_to_f32(g[k]) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int k = k0 + u * kThreads;
+        if (k < K) xq_put(xq, K, parts, k, (xv[u] * inv) * gv[u]);
+      }
+    }
   }
   trace_mark(a, ph, MARK_SCALED);
   csync();
@@ -998,48 +1015,38 @@ __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const uint16_t
     const bool has_x = g < (fold ? 2 * parts : parts);
     const uint4* xsrc = xq4 + (size_t)(g - xhalf * parts) * xps +
                         (size_t)(((ch.k0 >> 5) + xhalf * nkw) * 4 + c);
-    float acc[kMaxChunkRows / 16][2][4];
+    // Folded chunks: one accumulator pair.
+    float acc[1][2][4];
 #pragma unroll
-    for (int q = 0; q < kMaxChunkRows / 16; q++)
+    for (int h = 0; h < 2; h++)
 #pragma unroll
-      for (int h = 0; h < 2; h++)
-#pragma unroll
-        for (int i = 0; i < 4; i++) acc[q][h][i] = 0.f;
-    // Lane address for ldmatrix: row (lane % 8) + 8 ((lane / 8) % 2) of
-    // group q (rows past the chunk read its last row), 8 columns at
+      for (int i = 0; i < 4; i++) acc[0][h][i] = 0.f;
+    // Lane address for ldmatrix: row (lane % 8) + 8 ((lane / 8) % 2) of a
+    // 16-row group (rows past the chunk read its last row), 8 columns at
     // 8 (lane / 16) of the 16-column step.
     const uint32_t bbase = smem_addr(r.base + (size_t)b * r.buf_bytes) + (uint32_t)((lane >> 4) * 16);
     const int m = (lane & 7) + ((lane >> 3) & 1) * 8;  // fragment row of this lane's address
-    uint32_t lrow[kMaxChunkRows / 16];
+    uint32_t lrow[1] = {0u};
+    if (fold) lrow[0] = bbase + (uint32_t)(min(m & 7, nr - 1) * stride + (m >> 3) * nkw * 64);
     if (fold) {
-      lrow[0] = bbase + (uint32_t)(min(m & 7, nr - 1) * stride + (m >> 3) * nkw * 64);
-    } else {
-#pragma unroll
-      for (int q = 0; q < kMaxChunkRows / 16; q++)
-        lrow[q] = bbase + (uint32_t)(min(q * 16 + m, nr - 1) * stride);
-    }
-    for (int kb = warp; kb < nkw; kb += kWarps) {
-      uint4 xb = make_uint4(0u, 0u, 0u, 0u);
-      if (has_x) xb = xsrc[(size_t)kb * 4];
-#pragma unroll
-      for (int q = 0; q < kMaxChunkRows / 16; q++) {
-        if (q < ng) {
-          uint32_t m0[4], m1[4];
-          ldsm_x4(lrow[q] + (uint32_t)(kb * 64), m0);
-          ldsm_x4(lrow[q] + (uint32_t)(kb * 64 + 32), m1);
-          mma_bf16(acc[q][0], m0, xb.x, xb.y);
-          mma_bf16(acc[q][1], m1, xb.z, xb.w);
-        }
+      for (int kb = warp; kb < nkw; kb += kWarps) {
+        uint4 xb = make_uint4(0u, 0u, 0u, 0u);
+        if (has_x) xb = xsrc[(size_t)kb * 4];
+        uint32_t m0[4], m1[4];
+        ldsm_x4(lrow[0] + (uint32_t)(kb * 64), m0);
+        ldsm_x4(lrow[0] + (uint32_t)(kb * 64 + 32), m1);
+        mma_bf16(acc[0][0], m0, xb.x, xb.y);
+        mma_bf16(acc[0][1], m1, xb.z, xb.w);
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(r.empty + b);  // this warp is done with buffer b
     // Column p of the accumulators holds part p's products: lane 4g has
     // parts 0, 1 and lane 4g + 1 part 2 of rows g and g + 8. The warp's row
     // sums go to (or, for later column segments, add to) its red row.
     float* red = r.red + (size_t)(r.nred & 1) * kWarps * kMaxChunkRows;
     float* wred = red + warp * kMaxChunkRows;
     if (fold) {
+      if (lane == 0) mbar_arrive(r.empty + b);  // this warp is done with buffer b
       // Row g: columns 0..parts-1 of fragment row g (first half) plus
       // columns parts..2 parts-1 of fragment row g + 8 (second half).
       const float c0 = acc[0][0][0] + acc[0][1][0], c1 = acc[0][0][1] + acc[0][1][1];
@@ -1058,23 +1065,61 @@ __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const uint16_t
         (void)n1c1;
         wred[g] = v;
       }
-    }
+    } else {
+      // Both row groups of the chunk (at most 32 rows) per 32-column block:
+      // the block's four fragment loads issued before its four MMAs (four
+      // independent accumulator chains), so that the ldmatrix and MMA
+      // latencies overlap.
+      {
+        const bool two = ng > 1;  // ng <= 2: dense chunks have at most 32 rows
+        const uint32_t l0 = bbase + (uint32_t)(min(m, nr - 1) * stride);
+        const uint32_t l1 = bbase + (uint32_t)(min(16 + m, nr - 1) * stride);
+        float a4[2][2][4];
 #pragma unroll
-    for (int q = 0; q < kMaxChunkRows / 16; q++) {
-      if (fold) break;
-      if (q < ng) {
-        const float c0 = acc[q][0][0] + acc[q][1][0], c1 = acc[q][0][1] + acc[q][1][1];
-        const float c2 = acc[q][0][2] + acc[q][1][2], c3 = acc[q][0][3] + acc[q][1][3];
-        const float lo0 = __shfl_down_sync(0xFFFFFFFFu, c0, 1);
-        const float lo2 = __shfl_down_sync(0xFFFFFFFFu, c2, 1);
-        if (c == 0) {
-          const float v0 = (c0 + c1) + lo0, v8 = (c2 + c3) + lo2;
-          if (ch.first_seg) {
-            wred[q * 16 + g] = v0;
-            wred[q * 16 + g + 8] = v8;
-          } else {
-            wred[q * 16 + g] += v0;
-            wred[q * 16 + g + 8] += v8;
+        for (int q = 0; q < 2; q++)
+#pragma unroll
+          for (int h = 0; h < 2; h++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) a4[q][h][i] = 0.f;
+#pragma unroll 1
+        for (int kb = warp; kb < nkw; kb += kWarps) {
+          uint4 x0 = make_uint4(0u, 0u, 0u, 0u);
+          if (has_x) x0 = xsrc[(size_t)kb * 4];
+          uint32_t f[2][2][4];
+          const uint32_t o0 = (uint32_t)(kb * 64);
+          ldsm_x4(l0 + o0, f[0][0]);
+          ldsm_x4(l0 + o0 + 32, f[0][1]);
+          if (two) {
+            ldsm_x4(l1 + o0, f[1][0]);
+            ldsm_x4(l1 + o0 + 32, f[1][1]);
+          }
+          mma_bf16(a4[0][0], f[0][0], x0.x, x0.y);
+          mma_bf16(a4[0][1], f[0][1], x0.z, x0.w);
+          if (two) {
+            mma_bf16(a4[1][0], f[1][0], x0.x, x0.y);
+            mma_bf16(a4[1][1], f[1][1], x0.z, x0.w);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(r.empty + b);  // done with buffer b
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+          if (q == 1 && !two) break;
+          float cc[4];
+#pragma unroll
+          for (int i = 0; i < 4; i++) cc[i] = a4[q][0][i] + a4[q][1][i];
+          const float lo0 = __shfl_down_sync(0xFFFFFFFFu, cc[0], 1);
+          const float lo2 = __shfl_down_sync(0xFFFFFFFFu, cc[2], 1);
+          if (c == 0) {
+            const int rr = q * 16 + g;
+            const float v0 = (cc[0] + cc[1]) + lo0, v8 = (cc[2] + cc[3]) + lo2;
+            if (ch.first_seg) {
+              wred[rr] = v0;
+              wred[rr + 8] = v8;
+            } else {
+              wred[rr] += v0;
+              wred[rr + 8] += v8;
+            }
           }
         }
       }
@@ -1538,7 +1583,7 @@ constexpr int attn_floats() {
 // k and v come from the flagged qkv vector of layer l (epoch e). The split
 // holding `pos` appends this step's k and v to the cache. The split record
 // [m, l, acc[HD]] of each of the G query heads goes out as flagged words
-// (rec vector); merge_item combines the records of a kv head.
+// (rec vector); merge_item or merge_slice combines the records.
 template <int HD, int G>
 __device__ void attn_item(const MegaArgs& a, const MegaLayer& ly, int l, int kh, int sp,
                           int pos, unsigned e, float* sm, int ph) {
@@ -1679,24 +1724,34 @@ __device__ void attn_item(const MegaArgs& a, const MegaLayer& ly, int l, int kh,
     for (int v = 0; v < V; v++) wacc[((size_t)warp * G + g) * HD + lane * V + v] = acc[g][v];
   }
   csync();
+  // Per query head g and warp w the factor exp(m_w - M) (M the CTA's
+  // maximum), once per CTA (qs is free now), then the records.
+  float* cw = qs;  // [G][kWarps]
+  if (tid < G * kWarps) {
+    const int g = tid / kWarps, w = tid % kWarps;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w2 = 0; w2 < kWarps; w2++) M = fmaxf(M, wm[w2 * G + g]);
+    const float mw = wm[w * G + g];
+    cw[g * kWarps + w] = (mw == -INFINITY) ? 0.f : expf(mw - M);
+  }
+  csync();
   // The split record of each query head, as flagged words.
   u64* rec = a.ll + a.llo.rec + (((size_t)l * a.KHl + kh) * a.nsplit + sp) * G * (HD + 2);
   for (int ei = tid; ei < G * HD; ei += kThreads) {
     const int g = ei / HD, dd = ei % HD;
-    float M = -INFINITY;
-    for (int w = 0; w < kWarps; w++) M = fmaxf(M, wm[w * G + g]);
-    float L = 0.f, A = 0.f;
-    if (M != -INFINITY) {
-      for (int w = 0; w < kWarps; w++) {
-        const float mw = wm[w * G + g];
-        if (mw == -INFINITY) continue;
-        const float c = expf(mw - M);
-        L += wl[w * G + g] * c;
-        A += wacc[((size_t)w * G + g) * HD + dd] * c;
-      }
-    }
+    float A = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; w++)
+      A = fmaf(cw[g * kWarps + w], wacc[((size_t)w * G + g) * HD + dd], A);
     u64* R = rec + (size_t)g * (HD + 2);
     if (dd == 0) {
+      float M = -INFINITY, L = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; w++) {
+        M = fmaxf(M, wm[w * G + g]);
+        L = fmaf(cw[g * kWarps + w], wl[w * G + g], L);
+      }
       ll_store(R, M, e);
       ll_store(R + 1, L, e);
     }
@@ -1749,7 +1804,9 @@ __device__ __forceinline__ void ll_gather_rec(const MegaArgs& a, const u64* base
   }
 }
 
-// The attention output of kv head kh (its G query heads) at position pos:
+// The attention output of kv head kh (its G query heads) at position pos,
+// merged by one CTA (the layout when many CTAs have no attention item: one
+// of them per kv head merges, and the others do not poll):
 // att = sum_j c_j acc_j / sum_j c_j l_j over the splits holding positions
 // (c_j = exp(m_j - max m); splits of the kv head with positions <= pos).
 // Each thread merges one output element and waits for the words of up to
@@ -1788,6 +1845,70 @@ __device__ void merge_item(const MegaArgs& a, int l, int kh, int pos, unsigned e
     }
     ll_store(att + (size_t)(kh * G + g) * HD + dd, A / Ls, e);
   }
+}
+
+// The attention outputs att[e] for e in merge CTA mb's share of the QHl * HD
+// outputs (nmerge CTAs take equal slices): att = sum_j c_j acc_j /
+// sum_j c_j l_j over the splits j holding positions <= pos (c_j =
+// exp(m_j - max m)). S threads share an element, each folding every S-th
+// split with one round of loads (up to kMergeLoads splits per thread); the
+// S partial (m, l, acc) meet in shared memory (`sm`, 3 * kThreads floats),
+// where one thread per element finishes it.
+template <int HD, int G>
+__device__ void merge_slice(const MegaArgs& a, int l, int pos, unsigned e, float* sm, int mb,
+                            int nmerge) {
+  constexpr int kMergeLoads = 4;
+  const int QD = a.QHl * HD;
+  const int e0 = (int)((long long)QD * mb / nmerge);
+  const int e1 = (int)((long long)QD * (mb + 1) / nmerge);
+  const int n = e1 - e0;
+  if (n <= 0) return;
+  const int nact = min(a.nsplit, pos / a.split_len + 1);
+  const int S = max(1, min(kThreads / n, nact));
+  const int stride = G * (HD + 2);
+  const int tid = threadIdx.x;
+  const int el = tid / S, sub = tid % S;
+  float M = -INFINITY, Ls = 0.f, A = 0.f;
+  if (el < n) {
+    const int ei = e0 + el;
+    const int kh = ei / (G * HD), g = (ei / HD) % G, dd = ei % HD;
+    const u64* R0 = a.ll + a.llo.rec + ((size_t)l * a.KHl + kh) * a.nsplit * stride +
+                    (size_t)g * (HD + 2);
+    for (int j0 = sub; j0 < nact; j0 += S * kMergeLoads) {
+      float mj[kMergeLoads], lj[kMergeLoads], aj[kMergeLoads];
+      const int cnt = min(kMergeLoads, (nact - j0 + S - 1) / S);
+      ll_gather_rec<kMergeLoads>(a, R0 + (size_t)j0 * stride, S * stride, cnt, dd, e, mj, lj, aj);
+#pragma unroll
+      for (int u = 0; u < kMergeLoads; u++) {
+        if (u >= cnt || mj[u] == -INFINITY) continue;
+        const float Mn = fmaxf(M, mj[u]);
+        const float r = (M == -INFINITY) ? 0.f : expf(M - Mn);
+        const float c = expf(mj[u] - Mn);
+        Ls = fmaf(Ls, r, c * lj[u]);
+        A = fmaf(A, r, c * aj[u]);
+        M = Mn;
+      }
+    }
+  }
+  sm[tid] = M;
+  sm[kThreads + tid] = Ls;
+  sm[2 * kThreads + tid] = A;
+  csync();
+  if (tid < n) {
+    float Mt = -INFINITY;
+    for (int s2 = 0; s2 < S; s2++) Mt = fmaxf(Mt, sm[tid * S + s2]);
+    float Lt = 0.f, At = 0.f;
+    for (int s2 = 0; s2 < S; s2++) {
+      const float ms = sm[tid * S + s2];
+      if (ms == -INFINITY) continue;
+      const float c = expf(ms - Mt);
+      Lt = fmaf(c, sm[kThreads + tid * S + s2], Lt);
+      At = fmaf(c, sm[2 * kThreads + tid * S + s2], At);
+    }
+    u64* att = a.ll + a.llo.att + (size_t)l * QD;
+    ll_store(att + e0 + tid, At / Lt, e);
+  }
+  csync();  // sm is free again
 }
 
 // ---------------------------------------------------------------------------
@@ -1909,13 +2030,17 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
       trace_mark(a, ph, MARK_BEGIN);
       for (int it = blockIdx.x; it < attn_items; it += gridDim.x)
         attn_item<HD, G>(a, ly, l, it % a.KHl, it / a.KHl, pos, e, xs, ph);
-      // The merge of kv head kh runs on CTA (attn_items + kh) mod grid,
-      // idle during attention when the grid has room.
-      for (int kh = 0; kh < a.KHl; kh++)
-        if ((attn_items + kh) % (int)gridDim.x == (int)blockIdx.x) {
-          merge_item<HD, G>(a, l, kh, pos, e);
-          trace_mark(a, ph, MARK_READY);
-        }
+      // The split records: when at least KHl CTAs have no attention item,
+      // one such CTA per kv head merges them (few CTAs poll while the
+      // items run); otherwise every CTA merges an equal slice of the
+      // outputs once its own item is done.
+      if ((int)gridDim.x - attn_items >= a.KHl) {
+        for (int kh = 0; kh < a.KHl; kh++)
+          if (attn_items + kh == (int)blockIdx.x) merge_item<HD, G>(a, l, kh, pos, e);
+      } else {
+        merge_slice<HD, G>(a, l, pos, e, xs, (int)blockIdx.x, (int)gridDim.x);
+      }
+      trace_mark(a, ph, MARK_READY);
       ph++;
       // O + residual
       trace_mark(a, ph, MARK_BEGIN);
@@ -2089,12 +2214,13 @@ size_t select_attn_floats(int HD, int G) {
 
 // Activation region, rounded to 128 bytes: the residual copy xraw [D]
 // (rounded to 32 floats), two bf16 gain vectors [D] (same rounding), then
-// the matvec input (`parts` bf16 arrays of K + 32 columns) or the attention
-// scratch.
+// the matvec input (`parts` bf16 arrays of K + 32 columns), the attention
+// scratch or the attention merge's partials (3 floats per thread).
 
 size_t act_bytes(int D, int QD, int Fl, int HD, int G, int parts, int xf_floats = 0) {
   const size_t kmax = (size_t)std::max(D, std::max(QD, Fl));
   size_t bytes = std::max((size_t)parts * 2 * (kmax + 32), select_attn_floats(HD, G) * 4);
+  bytes = std::max(bytes, (size_t)3 * kThreads * 4);  // the attention merge's partials
   bytes += (size_t)(D + 31) / 32 * 32 * (4 + 2 * 2);  // xraw, two gain vectors
   bytes += (size_t)xf_floats * 4;
   return (bytes + 127) / 128 * 128;
