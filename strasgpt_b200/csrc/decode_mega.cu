@@ -2259,7 +2259,7 @@ int ring_count() {
 }
 
 // Three activation parts (fp32-faithful) when the weight ring keeps at
-// least 128 KB; two (x to about 2^-17, as in the tensor-core prefill)
+// least 112 KB; two (x to about 2^-17, as in the tensor-core prefill)
 // otherwise, so that large models keep enough weight bytes in flight.
 // STRASGPT_MEGA_PARTS=2 or 3 overrides the choice (when the ring still
 // fits).
@@ -2269,7 +2269,7 @@ int act_parts(int D, int QD, int Fl, int HD, int G, int xf) {
       act_bytes(D, QD, Fl, HD, G, atoi(v), xf) + (size_t)ring_count() * 16 * 1024 <=
           smem_budget(HD, G))
     return atoi(v);
-  return act_bytes(D, QD, Fl, HD, G, 3, xf) + (size_t)128 * 1024 <= smem_budget(HD, G) ? 3 : 2;
+  return act_bytes(D, QD, Fl, HD, G, 3, xf) + (size_t)112 * 1024 <= smem_budget(HD, G) ? 3 : 2;
 }
 
 // dst[r][0 .. src_bytes) = src[r][...], dst[r][src_bytes .. dst_bytes) = 0.
