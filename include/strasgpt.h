@@ -50,8 +50,18 @@ size_t transformer_cached_count(const transformer_t* transformer);
 // (world 1, 2, 4 or 8), on CUDA device `device`. Must be called before
 // transformer_from_safetensors(); without it the environment variables
 // STRASGPT_TP_RANK / STRASGPT_TP_SIZE / STRASGPT_DEVICE are read (default:
-// rank 0 of 1 on device 0). Returns 0, or -1 on an invalid placement.
+// rank 0 of 1 on device 0). world 0 clears an earlier placement (the
+// environment is read again). Returns 0, or -1 on an invalid placement.
 int strasgpt_set_placement(int rank, int world, int device);
+
+// Tensor parallelism in ONE process (no counterpart in the reference, whose
+// MPI split does no work): with STRASGPT_NGPU=N (2, 4 or 8) in the
+// environment and no placement set, transformer_from_safetensors() builds N
+// ranks on GPUs 0..N-1, connects them through direct peer access, and
+// returns one transformer_t that runs every later call on all ranks (one
+// host thread per rank) and answers with rank 0's results. The stock
+// strasgpt.c therefore runs tensor-parallel with no change but the
+// environment variable.
 
 // Tensor parallelism, one process per GPU of one node. Each rank's
 // transformer owns an exchange buffer in its GPU's memory; the ranks map

@@ -244,6 +244,27 @@ void tp_connect(TpComm* c, const void* handles) {
     c->peer[r] = static_cast<unsigned char*>(p);
   }
   c->connected = true;
+  c->ipc = true;
+}
+
+void tp_connect_local(TpComm* c, unsigned char* const* buffers, const int* devices) {
+  if (c->connected) SG_DIE("tensor-parallel peers already connected");
+  int me = 0;
+  SG_CUDA(cudaGetDevice(&me));
+  for (int r = 0; r < c->world; r++) {
+    c->peer[r] = buffers[r];
+    if (r == c->rank || devices[r] == me) continue;
+    int ok = 0;
+    SG_CUDA(cudaDeviceCanAccessPeer(&ok, me, devices[r]));
+    if (!ok) SG_DIE("single-process tensor parallelism: no peer access between the GPUs");
+    const cudaError_t e = cudaDeviceEnablePeerAccess(devices[r], 0);
+    if (e == cudaErrorPeerAccessAlreadyEnabled)
+      (void)cudaGetLastError();
+    else
+      SG_CUDA(e);
+  }
+  c->connected = true;
+  c->ipc = false;
 }
 
 void tp_free(TpComm* c, cudaStream_t s) {
@@ -251,8 +272,9 @@ void tp_free(TpComm* c, cudaStream_t s) {
     // No peer may still read this buffer once it is released.
     tp_barrier(*c, s);
     cudaStreamSynchronize(s);
-    for (int r = 0; r < c->world; r++)
-      if (r != c->rank && c->peer[r]) cudaIpcCloseMemHandle(c->peer[r]);
+    if (c->ipc)
+      for (int r = 0; r < c->world; r++)
+        if (r != c->rank && c->peer[r]) cudaIpcCloseMemHandle(c->peer[r]);
   }
   if (c->local) cudaFree(c->local);
   if (c->err) cudaFree(c->err);

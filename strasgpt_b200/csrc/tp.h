@@ -1,5 +1,6 @@
 // Tensor-parallel exchanges between the GPUs of one node over NVLink peer
-// memory (CUDA IPC), one process per GPU.
+// memory: one process per GPU (buffers shared through CUDA IPC), or all
+// ranks in one process (buffers used directly, peer access enabled).
 //
 // Every rank owns one exchange buffer (a single cudaMalloc, shared with the
 // other ranks through cudaIpcGetMemHandle / cudaIpcOpenMemHandle):
@@ -32,6 +33,7 @@ struct TpComm {
   unsigned char* peer[kTpMaxRanks] = {};  // every rank's buffer (own included)
   int* err = nullptr;                   // device int: non-zero after a timeout
   bool connected = false;
+  bool ipc = false;                     // peers mapped through CUDA IPC
 };
 
 // Bytes of the exchange buffer for `cap` floats per half and `extra` bytes
@@ -43,6 +45,11 @@ void tp_alloc(TpComm* c, int rank, int world, size_t cap, size_t extra = 0);
 void tp_handle(const TpComm& c, void* out64);
 // Maps the peers' buffers from world x 64-byte handles (rank order).
 void tp_connect(TpComm* c, const void* handles);
+// Connects ranks that live in this process: every rank's buffer
+// (buffers[r], allocated on devices[r]) is used directly; peer access from
+// this rank's device to every other device is enabled. Call with this
+// rank's device current.
+void tp_connect_local(TpComm* c, unsigned char* const* buffers, const int* devices);
 // Unmaps the peers (after a final barrier exchange) and frees the buffer.
 void tp_free(TpComm* c, cudaStream_t s);
 

@@ -33,6 +33,7 @@
 
 #include <cmath>
 #include <string>
+#include <thread>
 #include <vector>
 
 extern "C" {
@@ -84,6 +85,11 @@ struct transformer_weights {
   std::vector<Layer> layer;
   std::vector<void*> allocs;
   size_t device_bytes = 0;
+  // Single-process tensor parallelism (STRASGPT_NGPU=N): the transformer the
+  // caller holds is a group of N ranks, one per GPU, each a full
+  // transformer_t on its device; the C ABI runs every call on all ranks,
+  // one host thread per rank, and answers with rank 0's results.
+  std::vector<transformer_t*> ranks;
 };
 
 struct transformer_state {
@@ -556,8 +562,8 @@ void alloc_state(const W_t* w, const transformer_configuration_t* c, S_t* s) {
   SG_CUDA(cudaMemset(s->gen, 0, ((size_t)s->ctx + 1) * 4));
   sg::attn_decode_split(s->ctx, w->KHl, &s->nsplit, &s->split_len);
   // Megakernel decode (dense and mixture-of-experts models), when a CTA fits
-  // on every SM (under tensor parallelism for the greedy loop; predict keeps
-  // the per-op path, which gathers the full logits).
+  // on every SM (under tensor parallelism too: the LM-head slices are then
+  // gathered after the kernel when predict needs full logits).
   const bool moe_ok = !w->moe || (w->E % 2 == 0 && w->E <= 128 && w->topk >= 1 &&
                                   w->topk <= 8 && w->F % 32 == 0 && w->D % 32 == 0);
   const int mega_Fl = w->moe ? 0 : w->Fl;
@@ -851,7 +857,7 @@ struct Runner {
     a.pair_bound = (int)c->rope_pair_bound;
     a.pair_offset = (int)c->rope_pair_offset;
     a.pair_stride = (int)c->rope_pair_stride;
-    a.logits = s->logits;
+    a.logits = lm_out();
     a.kc = s->kc; a.vc = s->vc;
     a.nsplit = s->mega_nsplit; a.split_len = s->mega_split_len;
     a.ll = s->mega_ll; a.llo = s->mega_llo; a.epoch = s->mega_epoch;
@@ -1090,8 +1096,11 @@ void predict_impl(transformer_t* t, size_t T, const int* tok, size_t n,
     set_pos(s, (int)s->cached_count);
     const size_t lo = std::max(c0, lstart);
     if (Tc == 1) {
-      if (s->use_mega && w->world == 1) {
+      if (s->use_mega) {
+        // Under tensor parallelism each rank's LM-head rows land in its
+        // slice; the gather puts every rank's slice into s->logits.
         r.mega(1, true);
+        r.lm_gather(1);
       } else {
         if (!s->graph_logits) s->graph_logits = capture(r, false);
         SG_CUDA(cudaGraphLaunch(s->graph_logits, s->stream));
@@ -1119,6 +1128,20 @@ void predict_impl(transformer_t* t, size_t T, const int* tok, size_t n,
   if (T > 1) check_device_errors(s);
 }
 
+// Runs fn(rank, transformer) for every rank of a single-process group, rank
+// 0 on the calling thread and each other rank on a thread of its own (the
+// ranks' kernels wait for one another, so they must run concurrently).
+template <typename Fn>
+void on_ranks(W_t* g, Fn&& fn) {
+  std::vector<std::thread> th;
+  for (size_t r = 1; r < g->ranks.size(); r++)
+    th.emplace_back([&fn, g, r] { fn((int)r, g->ranks[r]); });
+  fn(0, g->ranks[0]);
+  for (auto& x : th) x.join();
+}
+
+bool is_group(transformer_t* t) { return t && !weights_of(t)->ranks.empty(); }
+
 }  // namespace
 
 // ===========================================================================
@@ -1127,6 +1150,10 @@ void predict_impl(transformer_t* t, size_t T, const int* tok, size_t n,
 extern "C" {
 
 int strasgpt_set_placement(int rank, int world, int device) {
+  if (world == 0) {
+    g_rank = g_world = g_device = -1;
+    return 0;
+  }
   if (world != 1 && world != 2 && world != 4 && world != 8) return -1;
   if (rank < 0 || rank >= world || device < 0) return -1;
   g_rank = rank;
@@ -1155,8 +1182,46 @@ int strasgpt_tp_connect(transformer_t* t, const void* handles) {
   return 0;
 }
 
+// STRASGPT_NGPU=N (2, 4 or 8, without strasgpt_set_placement): N ranks of
+// a tensor-parallel group on GPUs 0..N-1 of this process, connected through
+// direct peer access; the caller gets one transformer_t that runs them all.
+static transformer_t* group_from_safetensors(struct safetensors* st, int n) {
+  if (n != 2 && n != 4 && n != 8) SG_DIE("STRASGPT_NGPU must be 1, 2, 4 or 8");
+  int ndev = 0;
+  SG_CUDA(cudaGetDeviceCount(&ndev));
+  if (ndev < n) SG_DIE("STRASGPT_NGPU is larger than the number of visible GPUs");
+  W_t* g = new W_t();
+  for (int r = 0; r < n; r++) {
+    g_rank = r;
+    g_world = n;
+    g_device = r;
+    g->ranks.push_back(transformer_from_safetensors(st));
+  }
+  g_rank = g_world = g_device = -1;
+  std::vector<unsigned char*> bufs(n);
+  std::vector<int> devs(n);
+  for (int r = 0; r < n; r++) {
+    bufs[r] = state_of(g->ranks[r])->tp.local;
+    devs[r] = weights_of(g->ranks[r])->device;
+  }
+  for (int r = 0; r < n; r++) {
+    SG_CUDA(cudaSetDevice(devs[r]));
+    sg::tp_connect_local(&state_of(g->ranks[r])->tp, bufs.data(), devs.data());
+  }
+  SG_CUDA(cudaSetDevice(devs[0]));
+  transformer_t* t = (transformer_t*)calloc(1, sizeof(*t));
+  if (!t) SG_DIE("failed to malloc for transformer_t");
+  // The configuration and state the caller may read are rank 0's.
+  t->config = g->ranks[0]->config;
+  t->weights = (transformer_weights_t*)g;
+  t->state = g->ranks[0]->state;
+  return t;
+}
+
 transformer_t* transformer_from_safetensors(struct safetensors* st) {
   if (!st) SG_DIE("NULL safetensors");
+  if (g_world < 0 && env_int("STRASGPT_NGPU", 1) > 1)
+    return group_from_safetensors(st, env_int("STRASGPT_NGPU", 1));
   transformer_t* t = (transformer_t*)calloc(1, sizeof(*t));
   transformer_configuration_t* c = (transformer_configuration_t*)calloc(1, sizeof(*c));
   if (!t || !c) SG_DIE("failed to malloc for transformer_t");
@@ -1248,6 +1313,14 @@ transformer_t* transformer_from_safetensors(struct safetensors* st) {
 
 void transformer_free(transformer_t* t) {
   if (!t) return;
+  if (is_group(t)) {
+    // Every rank's final barrier exchange needs the others running.
+    W_t* g = weights_of(t);
+    on_ranks(g, [](int, transformer_t* r) { transformer_free(r); });
+    delete g;
+    free(t);
+    return;
+  }
   W_t* w = weights_of(t);
   S_t* s = state_of(t);
   if (w) SG_CUDA(cudaSetDevice(w->device));
@@ -1278,6 +1351,13 @@ void transformer_free(transformer_t* t) {
 void transformer_print(FILE* f, const transformer_t* t) {
   if (!t) {
     fprintf(f, "transformer: NULL\n");
+    return;
+  }
+  if (is_group(const_cast<transformer_t*>(t))) {
+    const W_t* g = (const W_t*)t->weights;
+    fprintf(f, "Tensor-parallel group of %zu GPUs in this process (STRASGPT_NGPU):\n",
+            g->ranks.size());
+    for (transformer_t* r : g->ranks) transformer_print(f, r);
     return;
   }
   const transformer_configuration_t* c = t->config;
@@ -1325,7 +1405,18 @@ void transformer_predict(transformer_t* t, size_t token_count, int* token,
     if (token_count + s->cached_count > t->config->context_len)
       SG_DIE("context length exhausted");
     if (logits_count > token_count) logits_count = token_count;
-    predict_impl(t, token_count, token, logits_count, logits);
+    if (is_group(t)) {
+      // Every rank ends with the full logits; rank 0's go to the caller.
+      W_t* g = weights_of(t);
+      const size_t n = logits_count * t->config->vocabulary_len;
+      std::vector<std::vector<float>> spare(g->ranks.size());
+      for (size_t r = 1; r < spare.size(); r++) spare[r].resize(n);
+      on_ranks(g, [&](int r, transformer_t* tr) {
+        predict_impl(tr, token_count, token, logits_count, r == 0 ? logits : spare[r].data());
+      });
+    } else {
+      predict_impl(t, token_count, token, logits_count, logits);
+    }
   }
 }
 
@@ -1333,6 +1424,25 @@ int transformer_generate_greedy(transformer_t* t, size_t P, const int* prompt,
                                 size_t S, int* out_tokens,
                                 strasgpt_timing_t* timing) {
   if (!t || !prompt || P == 0 || !out_tokens) SG_DIE("invalid arguments");
+  if (is_group(t)) {
+    W_t* g = weights_of(t);
+    std::vector<std::vector<int>> toks(g->ranks.size());
+    std::vector<strasgpt_timing_t> tms(g->ranks.size());
+    for (size_t r = 1; r < toks.size(); r++) toks[r].resize(S + 1);
+    on_ranks(g, [&](int r, transformer_t* tr) {
+      transformer_generate_greedy(tr, P, prompt, S, r == 0 ? out_tokens : toks[r].data(),
+                                  &tms[r]);
+    });
+    if (timing) {
+      // Device times: the slowest rank.
+      *timing = tms[0];
+      for (const auto& x : tms) {
+        timing->prefill_ms = std::max(timing->prefill_ms, x.prefill_ms);
+        timing->decode_ms = std::max(timing->decode_ms, x.decode_ms);
+      }
+    }
+    return 0;
+  }
   W_t* w = weights_of(t);
   S_t* st = state_of(t);
   require_connected(w, st);
@@ -1392,7 +1502,10 @@ int transformer_generate_greedy(transformer_t* t, size_t P, const int* prompt,
 }
 
 void transformer_reset(transformer_t* t) {
-  if (t) state_of(t)->cached_count = 0;
+  if (is_group(t))
+    for (transformer_t* r : weights_of(t)->ranks) transformer_reset(r);
+  else if (t)
+    state_of(t)->cached_count = 0;
 }
 
 size_t transformer_cached_count(const transformer_t* t) {
@@ -1402,6 +1515,14 @@ size_t transformer_cached_count(const transformer_t* t) {
 int strasgpt_profile_decode(transformer_t* t, int first_token, size_t steps,
                             strasgpt_kernel_profile_t* prof) {
   if (!t || !prof) SG_DIE("invalid arguments");
+  if (is_group(t)) {
+    W_t* g = weights_of(t);
+    std::vector<strasgpt_kernel_profile_t> spare(g->ranks.size());
+    on_ranks(g, [&](int r, transformer_t* tr) {
+      strasgpt_profile_decode(tr, first_token, steps, r == 0 ? prof : &spare[r]);
+    });
+    return 0;
+  }
   W_t* w = weights_of(t);
   S_t* st = state_of(t);
   require_connected(w, st);

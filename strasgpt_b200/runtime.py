@@ -129,18 +129,27 @@ class Transformer:
     """A model resident on one GPU (or one tensor-parallel shard of it)."""
 
     def __init__(self, model_dir: str, rank: int = 0, world: int = 1,
-                 device: int = 0, group=None):
+                 device: int = 0, group=None, ngpu: int = 1):
         """With world > 1 this is rank `rank`'s tensor-parallel shard; the
         ranks' exchange handles are all-gathered over the torch.distributed
-        process group `group` (any backend, e.g. gloo) and connected."""
+        process group `group` (any backend, e.g. gloo) and connected.
+        With ngpu > 1 (and world 1) the library builds a tensor-parallel
+        group of `ngpu` GPUs inside this process (STRASGPT_NGPU)."""
         L = lib()
-        if L.strasgpt_set_placement(rank, world, device) != 0:
+        if ngpu > 1:
+            if world != 1:
+                raise ValueError("ngpu > 1 is a single-process group: world must be 1")
+            L.strasgpt_set_placement(0, 0, 0)
+            os.environ["STRASGPT_NGPU"] = str(ngpu)
+        elif L.strasgpt_set_placement(rank, world, device) != 0:
             raise ValueError(f"invalid placement rank={rank} world={world}")
         st = L.parser_parse_safetensors(model_dir.encode())
         try:
             self._t = L.transformer_from_safetensors(st)
         finally:
             L.safetensors_free(st)
+            if ngpu > 1:
+                os.environ.pop("STRASGPT_NGPU", None)
         cfg = self._t.contents.config.contents
         self.vocab = int(cfg.vocabulary_len)
         self.context_len = int(cfg.context_len)

@@ -20,8 +20,8 @@ GPU = os.path.join(ROOT, "oracle", "_ref", "strasgpt_gpu")
 PROMPT = "Once upon a time, in a land far away"
 
 
-def _generate(binary, mdir, steps):
-    env = dict(os.environ, OMP_NUM_THREADS="4")
+def _generate(binary, mdir, steps, **extra_env):
+    env = dict(os.environ, OMP_NUM_THREADS="4", **extra_env)
     r = subprocess.run([binary, "-m", mdir, "-n", str(steps), "-p", PROMPT, "--temp", "0",
                         "-t", "4"], capture_output=True, text=True, timeout=300, env=env)
     assert r.returncode == 0, f"{os.path.basename(binary)} failed: {r.stderr[-2000:]}"
@@ -37,5 +37,21 @@ def test_reference_cli_on_the_gpu_library(cuda, name):
     steps = 16
     want = _generate(CPU, mdir, steps)
     got = _generate(GPU, mdir, steps)
+    assert want.strip(), "empty reference output"
+    assert got == want
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["t_llama", "t_gqa8"])
+def test_reference_cli_tensor_parallel_in_one_process(cuda, name):
+    """The unmodified strasgpt.c on 2 GPUs: STRASGPT_NGPU=2 makes
+    transformer_from_safetensors build a 2-rank group in the process."""
+    if not (os.path.exists(CPU) and os.path.exists(GPU)):
+        pytest.skip("reference CLI binaries not built (oracle/Makefile)")
+    if cuda.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    mdir = model_dir(configs.get(name))
+    want = _generate(CPU, mdir, 16)
+    got = _generate(GPU, mdir, 16, STRASGPT_NGPU="2")
     assert want.strip(), "empty reference output"
     assert got == want

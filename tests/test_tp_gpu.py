@@ -83,3 +83,31 @@ def test_tp2_matches_golden(cuda, tmp_path):
         assert err <= MAX_ABS and cos >= MIN_COS, f"{name}: max-abs {err:.3e} cos {cos:.7f}"
         assert [int(np.argmax(l)) for l in got] == meta["tokens"], name
         assert list(r0["tokens"]) == meta["tokens"] and list(r1["tokens"]) == meta["tokens"], name
+
+
+@pytest.mark.gpu
+def test_single_process_group_matches_golden(cuda):
+    """STRASGPT_NGPU=2: both ranks in this process (one host thread per
+    rank, direct peer access); the same parity bar as above."""
+    torch = cuda
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from strasgpt_b200 import Transformer
+    for name in NAMES:
+        cfg = configs.get(name)
+        meta = json.load(open(os.path.join(GOLDEN, f"{name}.json")))
+        want = np.load(os.path.join(GOLDEN, f"{name}.npz"))["logits"].astype(np.float64)
+        m = Transformer(model_dir(cfg), ngpu=2)
+        prompt = synth.prompt_tokens(cfg)
+        rows = [m.predict(prompt, 1)[0]]
+        for _ in range(cfg.steps):
+            rows.append(m.predict([int(np.argmax(rows[-1]))], 1)[0])
+        m.reset()
+        toks, _ = m.generate_greedy(prompt, cfg.steps)
+        m.free()
+        got = np.stack(rows).astype(np.float64)
+        err = np.abs(got - want).max()
+        cos = min(float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b))) for a, b in zip(got, want))
+        assert err <= MAX_ABS and cos >= MIN_COS, f"{name}: max-abs {err:.3e} cos {cos:.7f}"
+        assert [int(np.argmax(l)) for l in got] == meta["tokens"], name
+        assert list(toks) == meta["tokens"], name
