@@ -56,6 +56,15 @@ int strasgpt_k_attn_prefill(const float* q, const float* k_cache,
 int strasgpt_k_rmsnorm_rows(const float* x, int t, int d, const uint16_t* w,
                             float eps, float* y, void* stream);
 
+// The error path of the device-side waits, for tests (no counterpart in the
+// reference): runs the tensor-parallel barrier kernel of a 2-rank exchange
+// on the current GPU whose second rank is a buffer that nothing writes
+// (peer_posted 0: the wait can only run out) or whose post is already in
+// place (peer_posted 1), with a wait limit of timeout_ms. Returns 1 when
+// the wait ran out and the kernel returned with its error flag set, 0 when
+// it completed, -1 on a bad argument. The GPU stays usable either way.
+int strasgpt_k_tp_wait_check(int timeout_ms, int peer_posted, void* stream);
+
 // Size of the fixed device scratch of strasgpt_k_matvec_noalloc, held by
 // every GPU that loads the library until the process exits.
 #define STRASGPT_NOALLOC_SCRATCH_BYTES (4 << 20)

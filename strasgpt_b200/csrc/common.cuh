@@ -26,6 +26,15 @@
 
 namespace sg {
 
+// Bound (ns of %globaltimer) of the device-side waits on other CTAs or
+// GPUs: STRASGPT_WAIT_LIMIT_MS when set (tests make waits run out quickly
+// with it), else `default_ms`.
+inline unsigned long long wait_limit_ns(unsigned long long default_ms) {
+  const char* v = getenv("STRASGPT_WAIT_LIMIT_MS");
+  const long long ms = (v && *v) ? atoll(v) : 0;
+  return (ms > 0 ? (unsigned long long)ms : default_ms) * 1000000ull;
+}
+
 // bf16 stored as raw uint16_t everywhere: widening is a 16-bit shift
 // (the reference's util_bf16_to_f32, include/util.h:33-39).
 __device__ __forceinline__ float bf16_lo(uint32_t w) {

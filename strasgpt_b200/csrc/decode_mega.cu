@@ -57,10 +57,10 @@
 // the activation as two f16 parts with a scale per 32-column block
 // (mx_chunk_dot).
 //
-// Every wait is bounded (2 s): a timeout sets *err, later waits return at
-// once, the kernel runs to its end and the host reports the error. The
-// producer waits (bounded) for the completion of its last copies before it
-// exits.
+// Every wait is bounded (MegaArgs::wait_ns, 2 s by default): a timeout sets
+// *err, later waits return at once, the kernel runs to its end and the host
+// reports the error. The producer waits (bounded) for the completion of its
+// last copies before it exits.
 //
 // Math per element is the same as the multi-kernel path (kernels.cu) and
 // the reference (source/transformer.c:1186-1602).
@@ -71,8 +71,11 @@
 namespace sg {
 namespace {
 
-constexpr int kThreads = 256;               // consumer threads
-constexpr int kWarps = kThreads / 32;       // consumer warps
+#ifndef SG_MEGA_WARPS
+#define SG_MEGA_WARPS 8
+#endif
+constexpr int kWarps = SG_MEGA_WARPS;       // consumer warps
+constexpr int kThreads = 32 * kWarps;       // consumer threads
 constexpr int kBlockThreads = kThreads + 32;  // + the producer warp
 constexpr int kPosPerPass = kWarps * 8;  // cache rows per CTA pass
 constexpr int kMaxChunkRows = 64;        // rows per MXFP4 weight chunk (4 fragments)
@@ -81,7 +84,6 @@ constexpr int kPad = 16;                 // extra bytes per row in a buffer
 constexpr int kMaxRing = 4;              // weight buffers per CTA (at most)
 constexpr int kMaxSplits = 64;
 constexpr int kTpMaxWorld = 8;
-constexpr unsigned long long kTimeoutNs = 2000000000ULL;
 
 // ---------------------------------------------------------------------------
 // PTX helpers
@@ -217,7 +219,7 @@ __device__ __forceinline__ bool spin_on(const MegaArgs& a, Spin& s) {
   if (*(volatile int*)a.err) return false;
   const unsigned long long t = now_ns();
   if (s.t0 == 0) s.t0 = t;
-  if (t - s.t0 > kTimeoutNs) {
+  if (t - s.t0 > a.wait_ns) {
     atomicExch(a.err, 1);
     return false;
   }
@@ -393,7 +395,7 @@ __device__ __forceinline__ void xm_store(uint8_t* xm, int K, int nvec, int j, in
         __uint_as_float((uint32_t)(127 - sh) << 23);
 }
 
-// xm_store of v[u] at k = k0 + u * 256 (u < N) by the 32 lanes of a warp
+// xm_store of v[u] at k = k0 + u * kThreads (u < N) by the 32 lanes of a warp
 // together, each k one column of a 32-column block (lane 0 at the block's
 // first column; blocks at or past K are skipped). The N block maxima are
 // reduced side by side, so the shuffle latency is paid once per batch.
@@ -409,7 +411,7 @@ __device__ __forceinline__ void xm_put_batch(uint8_t* xm, int K, int nvec, int j
     for (int u = 0; u < N; u++) m[u] = fmaxf(m[u], __shfl_xor_sync(0xFFFFFFFFu, m[u], o));
 #pragma unroll
   for (int u = 0; u < N; u++) {
-    const int k = k0 + u * 256;
+    const int k = k0 + u * kThreads;
     if (k - (k & 31) < K) xm_store(xm, K, nvec, j, k, v[u], m[u]);
   }
 }
@@ -597,7 +599,7 @@ __device__ bool wait_bar(const MegaArgs& a, uint64_t* bar, unsigned parity,
   while (!mbar_try_wait(bar, parity)) {
     if ((++spins & 63) == 0) {
       if (stop_on_err && *(volatile int*)a.err) return false;
-      if (now_ns() - t0 > kTimeoutNs) {
+      if (now_ns() - t0 > a.wait_ns) {
         atomicExch(a.err, 2);
         return false;
       }
@@ -762,7 +764,7 @@ __device__ __forceinline__ float cta_sum(float v, float* red) {
 // Largest K an RMSNorm staging handles (K = embedding_dim), read in rounds
 // of kNormBatch flagged words per thread.
 constexpr int kNormBatch = 16;
-constexpr int kNormMaxK = 32 * kThreads;
+constexpr int kNormMaxK = 8192;
 
 // RMSNorm gains in shared memory: two bf16 vectors of D, refilled by bulk
 // copies (consumer thread 0) one phase or more before they are needed, so
@@ -791,7 +793,7 @@ __device__ __forceinline__ const uint16_t* gains_ready(const MegaArgs& a, Gains&
 
 // xq = rmsnorm(x) * gains from the flagged vector src (epoch e); the raw
 // values also go to xraw[K] (and the normalised ones to the xm region, as
-// vector 0, when set). Thread t owns k = t + u * 256. The loops are kept short: this code
+// vector 0, when set). Thread t owns k = t + u * kThreads. The loops are kept short: this code
 // runs once per phase, from a cold instruction cache.
 __device__ void stage_norm_ll(const MegaArgs& a, const u64* src, unsigned e, Gains& gs, int gi,
                               int K, uint16_t* xq, int parts, float* xraw, float* red, int ph,
@@ -1615,12 +1617,12 @@ __device__ void attn_item(const MegaArgs& a, const MegaLayer& ly, int l, int kh,
       for (int i = 0; i < QF; i++) kv[i] = __ldcg(kr + qd + 4 * i);
     }
   }
-  if (warp < G) {
+  for (int gq = warp; gq < G; gq += kWarps) {
     HeadFactors<HD> f;
     load_head_factors<HD>(a, ly.q_norm, pos, f);
     float v[V];
-    ll_gather<V>(a, qkv + (size_t)(kh * G + warp) * HD, lane, 32, HD, e, v);
-    head_norm_rope<HD>(a, v, ly.q_norm != nullptr, f, wacc + (size_t)warp * HD, qs + warp * HD);
+    ll_gather<V>(a, qkv + (size_t)(kh * G + gq) * HD, lane, 32, HD, e, v);
+    head_norm_rope<HD>(a, v, ly.q_norm != nullptr, f, wacc + (size_t)gq * HD, qs + gq * HD);
   }
   if (warp == kWarps - 1 && pos >= s_begin && pos < s_begin + a.split_len) {
     HeadFactors<HD> f;
@@ -1857,7 +1859,7 @@ __device__ void merge_item(const MegaArgs& a, int l, int kh, int pos, unsigned e
 template <int HD, int G>
 __device__ void merge_slice(const MegaArgs& a, int l, int pos, unsigned e, float* sm, int mb,
                             int nmerge) {
-  constexpr int kMergeLoads = 4;
+  constexpr int kMergeLoads = 6;
   const int QD = a.QHl * HD;
   const int e0 = (int)((long long)QD * mb / nmerge);
   const int e1 = (int)((long long)QD * (mb + 1) / nmerge);

@@ -2,6 +2,7 @@
 #include "common.cuh"
 #include "gemm_tc.h"
 #include "kernels.h"
+#include "tp.h"
 
 extern "C" {
 #include "strasgpt_kernels.h"
@@ -93,6 +94,11 @@ int strasgpt_k_rmsnorm_rows(const float* x, int t, int d, const uint16_t* w,
   sg::rmsnorm_rows(x, t, d, w, eps, y, (cudaStream_t)stream);
   SG_CUDA(cudaGetLastError());
   return 0;
+}
+
+int strasgpt_k_tp_wait_check(int timeout_ms, int peer_posted, void* stream) {
+  if (timeout_ms <= 0 || timeout_ms > 60000) return -1;
+  return sg::tp_wait_check(timeout_ms, peer_posted != 0, (cudaStream_t)stream);
 }
 
 }  // extern "C"

@@ -77,6 +77,7 @@ struct MegaArgs {
   int* gen;                 // generated tokens
   int gen_len;              // capacity of gen: writes at step >= gen_len are dropped
   int* err;                 // set non-zero when a wait times out
+  unsigned long long wait_ns;  // bound of every wait (ns)
   // Mixture of experts (moe != 0): E experts, topk chosen per token, expert
   // FFN width Fe, this rank owning experts [e_begin, e_end).
   int moe, E, topk, Fe, e_begin, e_end;

@@ -1,6 +1,7 @@
 // Tensor-parallel exchanges over NVLink peer memory (protocol in tp.h).
 //
-// Waits are bounded (kTpTimeoutNs of %globaltimer): on timeout a kernel sets
+// Waits are bounded (TpComm::timeout_ns of %globaltimer, 60 s unless
+// STRASGPT_WAIT_LIMIT_MS sets another limit): on timeout a kernel sets
 // the rank's error flag, skips the data movement and returns; the host
 // checks the flag after the step and stops with an error message. Every CTA
 // posts the epoch itself (idempotent stores), so no CTA waits on another CTA
@@ -14,13 +15,13 @@ namespace sg {
 namespace {
 
 constexpr size_t kHeader = 256;  // flags, epoch, ticket
-constexpr unsigned long long kTpTimeoutNs = 60ull * 1000000000ull;
 
 struct TpArgs {
   unsigned char* peer[kTpMaxRanks];
   int rank, world;
   size_t cap;
   int* err;
+  unsigned long long timeout_ns;
 };
 
 __device__ __forceinline__ unsigned* flags_of(unsigned char* b) { return (unsigned*)b; }
@@ -71,7 +72,7 @@ __device__ bool post_and_wait(const TpArgs& a, unsigned e) {
         if (*(volatile int*)a.err) return false;
         const unsigned long long t = now_ns();
         if (t0 == 0) t0 = t;
-        if (t - t0 > kTpTimeoutNs) {
+        if (t - t0 > a.timeout_ns) {
           atomicExch(a.err, 1);
           return false;
         }
@@ -186,6 +187,7 @@ TpArgs args_of(const TpComm& c) {
   a.world = c.world;
   a.cap = c.cap;
   a.err = c.err;
+  a.timeout_ns = c.timeout_ns;
   return a;
 }
 
@@ -213,6 +215,7 @@ void tp_alloc(TpComm* c, int rank, int world, size_t cap, size_t extra) {
     SG_DIE("invalid tensor-parallel placement");
   c->rank = rank;
   c->world = world;
+  c->timeout_ns = wait_limit_ns(60000);
   c->cap = (cap + 63) & ~(size_t)63;
   c->extra_off = kHeader + 2 * c->cap * sizeof(float);
   const size_t bytes = tp_buffer_bytes(c->cap, extra);
@@ -298,6 +301,35 @@ void tp_gather_rows(TpComm& c, const float* src, int rows, int cols, float* dst,
 
 void tp_barrier(TpComm& c, cudaStream_t s) {
   launch(k_tp_barrier, dim3(1), dim3(32), 0, s, args_of(c));
+}
+
+int tp_wait_check(int timeout_ms, bool peer_posted, cudaStream_t s) {
+  int dev = 0;
+  SG_CUDA(cudaGetDevice(&dev));
+  TpComm c;
+  tp_alloc(&c, 0, 2, 64);
+  c.timeout_ns = (unsigned long long)timeout_ms * 1000000ull;
+  unsigned char* other = nullptr;  // rank 1's buffer: nothing runs rank 1
+  const size_t bytes = tp_buffer_bytes(c.cap, 0);
+  SG_CUDA(cudaMalloc(&other, bytes));
+  SG_CUDA(cudaMemset(other, 0, bytes));
+  unsigned char* bufs[2] = {c.local, other};
+  const int devs[2] = {dev, dev};
+  tp_connect_local(&c, bufs, devs);
+  if (peer_posted) {
+    // Rank 1's post of the first exchange epoch, as if it had run.
+    const unsigned one = 1;
+    SG_CUDA(cudaMemcpy(c.local + sizeof(unsigned), &one, sizeof(one), cudaMemcpyHostToDevice));
+  }
+  tp_barrier(c, s);
+  SG_CUDA(cudaStreamSynchronize(s));
+  int err = 0;
+  SG_CUDA(cudaMemcpy(&err, c.err, sizeof(int), cudaMemcpyDeviceToHost));
+  // No final barrier: rank 1 does not exist.
+  SG_CUDA(cudaFree(other));
+  SG_CUDA(cudaFree(c.local));
+  SG_CUDA(cudaFree(c.err));
+  return err != 0 ? 1 : 0;
 }
 
 }  // namespace sg

@@ -34,6 +34,7 @@ struct TpComm {
   int* err = nullptr;                   // device int: non-zero after a timeout
   bool connected = false;
   bool ipc = false;                     // peers mapped through CUDA IPC
+  unsigned long long timeout_ns = 0;    // bound of every wait on a peer
 };
 
 // Bytes of the exchange buffer for `cap` floats per half and `extra` bytes
@@ -61,5 +62,11 @@ void tp_gather_rows(TpComm& c, const float* src, int rows, int cols, float* dst,
                     cudaStream_t s);
 // Exchange without data: returns once every rank has reached it.
 void tp_barrier(TpComm& c, cudaStream_t s);
+
+// The bounded wait of an exchange, alone: a 2-rank barrier on this GPU
+// whose rank 1 is a buffer nothing runs (peer_posted: its post already in
+// place). Returns 1 when the wait ran out (the kernel returned with the
+// error flag set), 0 when it completed.
+int tp_wait_check(int timeout_ms, bool peer_posted, cudaStream_t s);
 
 }  // namespace sg

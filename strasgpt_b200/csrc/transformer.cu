@@ -872,6 +872,7 @@ struct Runner {
     a.tok = s->tok; a.pos = s->pos; a.step = s->step; a.gen = s->gen;
     a.gen_len = s->ctx + 1;
     a.err = s->err;
+    a.wait_ns = sg::wait_limit_ns(2000);
     a.steps = steps; a.write_logits = write_logits ? 1 : 0;
     a.trace = s->trace; a.trace_phases = s->trace_phases;
     if (s->trace)
