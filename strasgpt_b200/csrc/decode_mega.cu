@@ -161,24 +161,28 @@ __device__ __forceinline__ void csync() {
 // i / 8 and receives, from each matrix, the pair (row i / 4, cols 2 (i % 4)).
 // For matrices (rows 0-7, cols 0-7), (rows 8-15, cols 0-7), (rows 0-7,
 // cols 8-15), (rows 8-15, cols 8-15) of a 16x16 tile these are the A
-// fragments of m16n8k16.
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t* r) {
+// fragments of m16n8k16. The registers come back by value: an array whose
+// address is taken can end up in local memory, which with the shared-memory
+// carveout at its maximum is served by L2.
+__device__ __forceinline__ uint4 ldsm4(uint32_t addr) {
+  uint4 r;
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                : "r"(addr));
+  return r;
 }
 
-// d += A (16x16 bf16, row-major fragments a0..a3) * B (16x8 bf16, b0/b1),
+// d += A (16x16 bf16, row-major fragments a.x..a.w) * B (16x8 bf16, b0/b1),
 // fp32 accumulators (rows g, g + 8; columns 2c, 2c + 1 of lane 4g + c).
 // (Register operands only, so not volatile: the compiler may interleave
 // the steps of independent fragments.)
-__device__ __forceinline__ void mma_bf16(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
-  asm(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+__device__ __forceinline__ void mma4(float4& d, uint4 a, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
       "{%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+      : "+f"(d.x), "+f"(d.y), "+f"(d.z), "+f"(d.w)
+      : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
 }
+
 
 // ---------------------------------------------------------------------------
 // Flagged vectors
@@ -910,15 +914,19 @@ __device__ void stage_embedding(const MegaArgs& a, int token, Gains& gs, int gi,
 // ---------------------------------------------------------------------------
 // Consuming one weight phase
 // ---------------------------------------------------------------------------
+// The ring lives at fixed shared-memory places (the buffers at the start of
+// the dynamic region, a.buf_bytes apart; the barriers and the per-warp row
+// sums in file-scope arrays) and its geometry in the kernel arguments, so
+// that the chunk loops keep only two counters in registers.
+extern __shared__ __align__(128) char s_dyn[];
+__shared__ __align__(8) uint64_t s_full[kMaxRing];   // the chunk in buffer b has landed
+__shared__ __align__(8) uint64_t s_empty[kMaxRing];  // the consumer warps are done with it
+__shared__ __align__(16) float s_mvred[2 * kWarps * kMaxChunkRows];  // per-warp row sums
+__shared__ unsigned long long s_tsum[4];  // trace: wait, dot, reduce sums; last mark
+
 struct Ring {
-  char* base;      // buffer b starts at base + b * buf_bytes
-  uint64_t* full;  // [nbuf]: the chunk in buffer b has landed
-  uint64_t* empty; // [nbuf]: the consumer warps are done with buffer b
-  int nbuf;
-  int buf_bytes;
   unsigned g;      // chunks consumed so far
-  unsigned nred;   // cross-warp reductions so far (selects the red half)
-  float* red;      // [2][kWarps][kMaxChunkRows] per-warp partial row sums
+  unsigned nred;   // cross-warp reductions so far (selects the row-sum half)
 };
 
 // Where a phase's outputs go.
@@ -991,15 +999,20 @@ __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const uint16_t
   const int xps = xq_stride(phs.K) / 8;  // uint4 per activation part
   const uint4* xq4 = reinterpret_cast<const uint4*>(xq);
   const bool tr = a.trace != nullptr;
-  unsigned long long t_wait = 0, t_dot = 0, t_red = 0, t0 = 0;
+  // Trace sums (thread 0 only) in shared memory: no registers held across
+  // the chunk loop when tracing is off.
+  const bool tr0 = tr && tid == 0;
+  if (tr0) s_tsum[0] = s_tsum[1] = s_tsum[2] = 0;
   for (int ci = 0; ci < s.nchunks; ci++) {
-    const int b = (int)(r.g % r.nbuf);
-    if (tr) t0 = now_ns();
-    wait_bar(a, r.full + b, (r.g / r.nbuf) & 1);
+    const int b = (int)(r.g % a.nbuf);
+    if (tr0) s_tsum[3] = now_ns();
+    wait_bar(a, s_full + b, (r.g / a.nbuf) & 1);
     if (tr) {
       const unsigned long long t1 = now_ns();
-      t_wait += t1 - t0;
-      t0 = t1;
+      if (tr0) {
+        s_tsum[0] += t1 - s_tsum[3];
+        s_tsum[3] = t1;
+      }
     }
     if (ci == 0) trace_mark(a, ph, MARK_READY);
     const Chunk ch = slice_chunk(s, phs, ci);
@@ -1017,42 +1030,37 @@ __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const uint16_t
     const bool has_x = g < (fold ? 2 * parts : parts);
     const uint4* xsrc = xq4 + (size_t)(g - xhalf * parts) * xps +
                         (size_t)(((ch.k0 >> 5) + xhalf * nkw) * 4 + c);
-    // Folded chunks: one accumulator pair.
-    float acc[1][2][4];
-#pragma unroll
-    for (int h = 0; h < 2; h++)
-#pragma unroll
-      for (int i = 0; i < 4; i++) acc[0][h][i] = 0.f;
+    // Folded chunks: one accumulator pair (named, by value).
+    float4 facc0 = make_float4(0.f, 0.f, 0.f, 0.f), facc1 = facc0;
     // Lane address for ldmatrix: row (lane % 8) + 8 ((lane / 8) % 2) of a
     // 16-row group (rows past the chunk read its last row), 8 columns at
     // 8 (lane / 16) of the 16-column step.
-    const uint32_t bbase = smem_addr(r.base + (size_t)b * r.buf_bytes) + (uint32_t)((lane >> 4) * 16);
+    const uint32_t bbase = smem_addr(s_dyn + (size_t)b * a.buf_bytes) + (uint32_t)((lane >> 4) * 16);
     const int m = (lane & 7) + ((lane >> 3) & 1) * 8;  // fragment row of this lane's address
-    uint32_t lrow[1] = {0u};
-    if (fold) lrow[0] = bbase + (uint32_t)(min(m & 7, nr - 1) * stride + (m >> 3) * nkw * 64);
+    const uint32_t lrow0 =
+        fold ? bbase + (uint32_t)(min(m & 7, nr - 1) * stride + (m >> 3) * nkw * 64) : 0u;
     if (fold) {
       for (int kb = warp; kb < nkw; kb += kWarps) {
         uint4 xb = make_uint4(0u, 0u, 0u, 0u);
         if (has_x) xb = xsrc[(size_t)kb * 4];
-        uint32_t m0[4], m1[4];
-        ldsm_x4(lrow[0] + (uint32_t)(kb * 64), m0);
-        ldsm_x4(lrow[0] + (uint32_t)(kb * 64 + 32), m1);
-        mma_bf16(acc[0][0], m0, xb.x, xb.y);
-        mma_bf16(acc[0][1], m1, xb.z, xb.w);
+        const uint4 m0 = ldsm4(lrow0 + (uint32_t)(kb * 64));
+        const uint4 m1 = ldsm4(lrow0 + (uint32_t)(kb * 64 + 32));
+        mma4(facc0, m0, xb.x, xb.y);
+        mma4(facc1, m1, xb.z, xb.w);
       }
     }
     __syncwarp();
     // Column p of the accumulators holds part p's products: lane 4g has
     // parts 0, 1 and lane 4g + 1 part 2 of rows g and g + 8. The warp's row
     // sums go to (or, for later column segments, add to) its red row.
-    float* red = r.red + (size_t)(r.nred & 1) * kWarps * kMaxChunkRows;
+    float* red = s_mvred + (size_t)(r.nred & 1) * kWarps * kMaxChunkRows;
     float* wred = red + warp * kMaxChunkRows;
     if (fold) {
-      if (lane == 0) mbar_arrive(r.empty + b);  // this warp is done with buffer b
+      if (lane == 0) mbar_arrive(s_empty + b);  // this warp is done with buffer b
       // Row g: columns 0..parts-1 of fragment row g (first half) plus
       // columns parts..2 parts-1 of fragment row g + 8 (second half).
-      const float c0 = acc[0][0][0] + acc[0][1][0], c1 = acc[0][0][1] + acc[0][1][1];
-      const float c2 = acc[0][0][2] + acc[0][1][2], c3 = acc[0][0][3] + acc[0][1][3];
+      const float c0 = facc0.x + facc1.x, c1 = facc0.y + facc1.y;
+      const float c2 = facc0.z + facc1.z, c3 = facc0.w + facc1.w;
       const float n1c0 = __shfl_down_sync(0xFFFFFFFFu, c0, 1);
       const float n1c1 = __shfl_down_sync(0xFFFFFFFFu, c1, 1);
       const float n1c3 = __shfl_down_sync(0xFFFFFFFFu, c3, 1);
@@ -1069,47 +1077,36 @@ __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const uint16_t
       }
     } else {
       // Both row groups of the chunk (at most 32 rows) per 32-column block:
-      // the block's four fragment loads issued before its four MMAs (four
-      // independent accumulator chains), so that the ldmatrix and MMA
-      // latencies overlap.
+      // the block's four fragment loads issued before its four MMAs (two
+      // accumulator chains), so that the ldmatrix and MMA latencies overlap.
       {
         const bool two = ng > 1;  // ng <= 2: dense chunks have at most 32 rows
         const uint32_t l0 = bbase + (uint32_t)(min(m, nr - 1) * stride);
         const uint32_t l1 = bbase + (uint32_t)(min(16 + m, nr - 1) * stride);
-        float a4[2][2][4];
-#pragma unroll
-        for (int q = 0; q < 2; q++)
-#pragma unroll
-          for (int h = 0; h < 2; h++)
-#pragma unroll
-            for (int i = 0; i < 4; i++) a4[q][h][i] = 0.f;
+        // One accumulator per row group (both k16 steps of a block add into
+        // it), fragments as values; both groups always (with one group, the
+        // second reads the chunk's last row again and is discarded), so the
+        // loop has no branches and no arrays.
+        float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
 #pragma unroll 1
         for (int kb = warp; kb < nkw; kb += kWarps) {
           uint4 x0 = make_uint4(0u, 0u, 0u, 0u);
           if (has_x) x0 = xsrc[(size_t)kb * 4];
-          uint32_t f[2][2][4];
           const uint32_t o0 = (uint32_t)(kb * 64);
-          ldsm_x4(l0 + o0, f[0][0]);
-          ldsm_x4(l0 + o0 + 32, f[0][1]);
-          if (two) {
-            ldsm_x4(l1 + o0, f[1][0]);
-            ldsm_x4(l1 + o0 + 32, f[1][1]);
-          }
-          mma_bf16(a4[0][0], f[0][0], x0.x, x0.y);
-          mma_bf16(a4[0][1], f[0][1], x0.z, x0.w);
-          if (two) {
-            mma_bf16(a4[1][0], f[1][0], x0.x, x0.y);
-            mma_bf16(a4[1][1], f[1][1], x0.z, x0.w);
-          }
+          const uint4 f00 = ldsm4(l0 + o0), f01 = ldsm4(l0 + o0 + 32);
+          const uint4 f10 = ldsm4(l1 + o0), f11 = ldsm4(l1 + o0 + 32);
+          mma4(acc0, f00, x0.x, x0.y);
+          mma4(acc1, f10, x0.x, x0.y);
+          mma4(acc0, f01, x0.z, x0.w);
+          mma4(acc1, f11, x0.z, x0.w);
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(r.empty + b);  // done with buffer b
+        if (lane == 0) mbar_arrive(s_empty + b);  // done with buffer b
 #pragma unroll
         for (int q = 0; q < 2; q++) {
           if (q == 1 && !two) break;
-          float cc[4];
-#pragma unroll
-          for (int i = 0; i < 4; i++) cc[i] = a4[q][0][i] + a4[q][1][i];
+          const float4 aq = q ? acc1 : acc0;
+          const float cc[4] = {aq.x, aq.y, aq.z, aq.w};
           const float lo0 = __shfl_down_sync(0xFFFFFFFFu, cc[0], 1);
           const float lo2 = __shfl_down_sync(0xFFFFFFFFu, cc[2], 1);
           if (c == 0) {
@@ -1128,8 +1125,10 @@ __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const uint16_t
     }
     if (tr) {
       const unsigned long long t1 = now_ns();
-      t_dot += t1 - t0;
-      t0 = t1;
+      if (tr0) {
+        s_tsum[1] += t1 - s_tsum[3];
+        s_tsum[3] = t1;
+      }
     }
     if (ch.last_seg) {
       r.nred++;
@@ -1143,15 +1142,17 @@ __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const uint16_t
         }
         pair_epilogue(a, o, phs.kind, (ch.r0 >> 1) + tid, y0, y1, bv, bi);
       }
-      if (tr) t_red += now_ns() - t0;
+      if (tr0) s_tsum[2] += now_ns() - s_tsum[3];
     }
     r.g++;
   }
   trace_mark(a, ph, MARK_CONSUMED);
-  trace_put(a, ph, SUM_WAIT, t_wait);
-  trace_put(a, ph, SUM_COMPUTE, t_dot + t_red);
-  trace_put(a, ph, SUM_DOT, t_dot);
-  trace_put(a, ph, SUM_REDUCE, t_red);
+  if (tr0) {
+    trace_put(a, ph, SUM_WAIT, s_tsum[0]);
+    trace_put(a, ph, SUM_COMPUTE, s_tsum[1] + s_tsum[2]);
+    trace_put(a, ph, SUM_DOT, s_tsum[1]);
+    trace_put(a, ph, SUM_REDUCE, s_tsum[2]);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -1216,7 +1217,8 @@ __device__ void expert_select(const MegaArgs& a, int l, unsigned e, int* sel, fl
 
 // Four e2m1 pairs (the bytes of w, low byte first) as f16x2 words, the low
 // nibble of a byte in the low half (exact: every e2m1 value is an f16).
-__device__ __forceinline__ void e2m1x8_to_f16(uint32_t w, uint32_t* h) {
+__device__ __forceinline__ uint4 e2m1x8_to_f16v(uint32_t w) {
+  uint4 h;
   asm("{\n"
       " .reg .b8 b0, b1, b2, b3;\n"
       " mov.b32 {b0, b1, b2, b3}, %4;\n"
@@ -1225,17 +1227,17 @@ __device__ __forceinline__ void e2m1x8_to_f16(uint32_t w, uint32_t* h) {
       " cvt.rn.f16x2.e2m1x2 %2, b2;\n"
       " cvt.rn.f16x2.e2m1x2 %3, b3;\n"
       "}"
-      : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+      : "=r"(h.x), "=r"(h.y), "=r"(h.z), "=r"(h.w)
       : "r"(w));
+  return h;
 }
-
-// d += A (16x16 f16) * B (16x8 f16), fp32 accumulators; fragments as mma_bf16.
-__device__ __forceinline__ void mma_f16(float* d, uint32_t a0, uint32_t a1, uint32_t a2,
-                                        uint32_t a3, uint32_t b0, uint32_t b1) {
+// d += A (16x16 f16) * B (16x8 f16), fp32 accumulators; fragments as mma4.
+__device__ __forceinline__ void mma_f16v(float4& d, uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
   asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
       "{%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "+f"(d.x), "+f"(d.y), "+f"(d.z), "+f"(d.w)
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
@@ -1264,61 +1266,63 @@ __device__ __forceinline__ void mx_chunk_dot(const uint8_t* buf, int nr, int K, 
   // (rows past the chunk read its last row), block + lane / 16.
   const uint32_t bbase = smem_addr(buf) + (uint32_t)((lane >> 4) * 16);
   const int m = (lane & 7) + ((lane >> 3) & 1) * 8;
-  float acc[kMaxChunkRows / 16][4];
-#pragma unroll
-  for (int q = 0; q < kMaxChunkRows / 16; q++)
-#pragma unroll
-    for (int i = 0; i < 4; i++) acc[q][i] = 0.f;
+  // Named float4 accumulators and by-value fragments: arrays written under
+  // runtime conditions end up in local memory (served by L2 here).
+  float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0, acc2 = acc0, acc3 = acc0;
+  // One 16-row group q of block pair kp: codes by ldmatrix, e2m1 -> f16 in
+  // registers, two MMA pairs, scaled into the group's accumulator.
+  auto group = [&](int q, int kp, int b0, bool two, uint4 x0, uint4 x1, float xs0, float xs1,
+                   float4& acc) {
+    const uint4 w = ldsm4(bbase + (uint32_t)(min(q * 16 + m, nr - 1) * cb + kp * 32));
+    const uint32_t sg =
+        *reinterpret_cast<const uint16_t*>(scl + min(q * 16 + g, nr - 1) * sb + b0);
+    const uint32_t s8 =
+        *reinterpret_cast<const uint16_t*>(scl + min(q * 16 + g + 8, nr - 1) * sb + b0);
+    uint4 hg = e2m1x8_to_f16v(w.x), h8 = e2m1x8_to_f16v(w.y);
+    float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+    mma_f16v(t, hg.x, h8.x, hg.y, h8.y, x0.x, x0.y);
+    mma_f16v(t, hg.z, h8.z, hg.w, h8.w, x0.z, x0.w);
+    float fg = mx_scale(sg & 0xFF) * xs0, f8 = mx_scale(s8 & 0xFF) * xs0;
+    acc.x = fmaf(t.x, fg, acc.x);
+    acc.y = fmaf(t.y, fg, acc.y);
+    acc.z = fmaf(t.z, f8, acc.z);
+    acc.w = fmaf(t.w, f8, acc.w);
+    if (two) {
+      float4 u = make_float4(0.f, 0.f, 0.f, 0.f);
+      hg = e2m1x8_to_f16v(w.z);
+      h8 = e2m1x8_to_f16v(w.w);
+      mma_f16v(u, hg.x, h8.x, hg.y, h8.y, x1.x, x1.y);
+      mma_f16v(u, hg.z, h8.z, hg.w, h8.w, x1.z, x1.w);
+      fg = mx_scale(sg >> 8) * xs1;
+      f8 = mx_scale(s8 >> 8) * xs1;
+      acc.x = fmaf(u.x, fg, acc.x);
+      acc.y = fmaf(u.y, fg, acc.y);
+      acc.z = fmaf(u.z, f8, acc.z);
+      acc.w = fmaf(u.w, f8, acc.w);
+    }
+  };
   for (int kp = warp; kp < npair; kp += kWarps) {
     const int b0 = 2 * kp;
     const bool two = b0 + 1 < nb;
     const uint4 x0 = *reinterpret_cast<const uint4*>(xp + (size_t)b0 * 64);
     const uint4 x1 = two ? *reinterpret_cast<const uint4*>(xp + (size_t)(b0 + 1) * 64) : x0;
     const float xs0 = xsi[b0], xs1 = two ? xsi[b0 + 1] : 0.f;
-#pragma unroll
-    for (int q = 0; q < kMaxChunkRows / 16; q++) {
-      if (q < ng) {
-        uint32_t w[4];
-        ldsm_x4(bbase + (uint32_t)(min(q * 16 + m, nr - 1) * cb + kp * 32), w);
-        const uint32_t sg =
-            *reinterpret_cast<const uint16_t*>(scl + min(q * 16 + g, nr - 1) * sb + b0);
-        const uint32_t s8 =
-            *reinterpret_cast<const uint16_t*>(scl + min(q * 16 + g + 8, nr - 1) * sb + b0);
-        uint32_t hg[4], h8[4];
-        float t[4] = {0.f, 0.f, 0.f, 0.f};
-        e2m1x8_to_f16(w[0], hg);
-        e2m1x8_to_f16(w[1], h8);
-        mma_f16(t, hg[0], h8[0], hg[1], h8[1], x0.x, x0.y);
-        mma_f16(t, hg[2], h8[2], hg[3], h8[3], x0.z, x0.w);
-        float fg = mx_scale(sg & 0xFF) * xs0, f8 = mx_scale(s8 & 0xFF) * xs0;
-        acc[q][0] = fmaf(t[0], fg, acc[q][0]);
-        acc[q][1] = fmaf(t[1], fg, acc[q][1]);
-        acc[q][2] = fmaf(t[2], f8, acc[q][2]);
-        acc[q][3] = fmaf(t[3], f8, acc[q][3]);
-        if (two) {
-          float u[4] = {0.f, 0.f, 0.f, 0.f};
-          e2m1x8_to_f16(w[2], hg);
-          e2m1x8_to_f16(w[3], h8);
-          mma_f16(u, hg[0], h8[0], hg[1], h8[1], x1.x, x1.y);
-          mma_f16(u, hg[2], h8[2], hg[3], h8[3], x1.z, x1.w);
-          fg = mx_scale(sg >> 8) * xs1;
-          f8 = mx_scale(s8 >> 8) * xs1;
-          acc[q][0] = fmaf(u[0], fg, acc[q][0]);
-          acc[q][1] = fmaf(u[1], fg, acc[q][1]);
-          acc[q][2] = fmaf(u[2], f8, acc[q][2]);
-          acc[q][3] = fmaf(u[3], f8, acc[q][3]);
-        }
-      }
-    }
+    group(0, kp, b0, two, x0, x1, xs0, xs1, acc0);
+    if (ng > 1) group(1, kp, b0, two, x0, x1, xs0, xs1, acc1);
+    if (ng > 2) group(2, kp, b0, two, x0, x1, xs0, xs1, acc2);
+    if (ng > 3) group(3, kp, b0, two, x0, x1, xs0, xs1, acc3);
   }
   // Lane 4g: columns 0 and 1 (parts hi and mid) of rows g and g + 8.
   if (c == 0) {
-#pragma unroll
-    for (int q = 0; q < kMaxChunkRows / 16; q++) {
+    auto put = [&](int q, float4 a4) {
       const int r0 = q * 16 + g, r8 = r0 + 8;
-      if (r0 < nr) wred[r0] = (first ? 0.f : wred[r0]) + wgt * (acc[q][0] + acc[q][1]);
-      if (r8 < nr) wred[r8] = (first ? 0.f : wred[r8]) + wgt * (acc[q][2] + acc[q][3]);
-    }
+      if (r0 < nr) wred[r0] = (first ? 0.f : wred[r0]) + wgt * (a4.x + a4.y);
+      if (r8 < nr) wred[r8] = (first ? 0.f : wred[r8]) + wgt * (a4.z + a4.w);
+    };
+    put(0, acc0);
+    put(1, acc1);
+    put(2, acc2);
+    put(3, acc3);
   }
 }
 
@@ -1337,21 +1341,21 @@ __device__ void consume_mx_gu(const MegaArgs& a, Ring& r, int l, const uint8_t* 
   const bool tr = a.trace != nullptr;
   unsigned long long t_wait = 0, t0 = 0;
   for (int ci = 0; ci < s.nchunks; ci++) {
-    const int b = (int)(r.g % r.nbuf);
+    const int b = (int)(r.g % a.nbuf);
     if (tr) t0 = now_ns();
-    wait_bar(a, r.full + b, (r.g / r.nbuf) & 1);
+    wait_bar(a, s_full + b, (r.g / a.nbuf) & 1);
     if (tr) t_wait += now_ns() - t0;
     if (ci == 0) trace_mark(a, ph, MARK_READY);
     int p0, np;
     egu_chunk(s.rb / 2, s.re / 2, s.rows / 2, a.Fe, ci, p0, np);
     const int j = p0 / a.Fe, f0 = p0 % a.Fe;
     const bool own = expert_owned(a, sel[j]);
-    float* red = r.red + (size_t)(r.nred & 1) * kWarps * kMaxChunkRows;
+    float* red = s_mvred + (size_t)(r.nred & 1) * kWarps * kMaxChunkRows;
     if (own)
-      mx_chunk_dot(reinterpret_cast<const uint8_t*>(r.base + (size_t)b * r.buf_bytes), 2 * np,
+      mx_chunk_dot(reinterpret_cast<const uint8_t*>(s_dyn + (size_t)b * a.buf_bytes), 2 * np,
                    a.D, cb, sb, xm, 1, 0, 1.f, true, red + warp * kMaxChunkRows);
     __syncwarp();
-    if (lane == 0) mbar_arrive(r.empty + b);
+    if (lane == 0) mbar_arrive(s_empty + b);
     if (own) {
       r.nred++;
       csync();
@@ -1408,23 +1412,23 @@ __device__ void consume_mx_down(const MegaArgs& a, Ring& r, const uint8_t* xm, c
   const bool tr = a.trace != nullptr;
   unsigned long long t_wait = 0, t0 = 0;
   for (int ci = 0; ci < s.nchunks; ci++) {
-    const int b = (int)(r.g % r.nbuf);
+    const int b = (int)(r.g % a.nbuf);
     if (tr) t0 = now_ns();
-    wait_bar(a, r.full + b, (r.g / r.nbuf) & 1);
+    wait_bar(a, s_full + b, (r.g / a.nbuf) & 1);
     if (tr) t_wait += now_ns() - t0;
     if (ci == 0) trace_mark(a, ph, MARK_READY);
     const Chunk ch = slice_chunk(s, phs, ci);
     const int nr = ch.r1 - ch.r0, j = ch.seg;
-    float* red = r.red + (size_t)(r.nred & 1) * kWarps * kMaxChunkRows;
+    float* red = s_mvred + (size_t)(r.nred & 1) * kWarps * kMaxChunkRows;
     float* wred = red + warp * kMaxChunkRows;
     if (expert_owned(a, sel[j])) {
-      mx_chunk_dot(reinterpret_cast<const uint8_t*>(r.base + (size_t)b * r.buf_bytes), nr, a.Fe,
+      mx_chunk_dot(reinterpret_cast<const uint8_t*>(s_dyn + (size_t)b * a.buf_bytes), nr, a.Fe,
                    cb, sb, xm, a.topk, j, selw[j], ch.first_seg, wred);
     } else if (ch.first_seg && lane == 0) {
       for (int i = 0; i < nr; i++) wred[i] = 0.f;
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(r.empty + b);
+    if (lane == 0) mbar_arrive(s_empty + b);
     if (ch.last_seg) {
       r.nred++;
       csync();
@@ -1918,15 +1922,13 @@ __device__ void merge_slice(const MegaArgs& a, int l, int pos, unsigned e, float
 // ---------------------------------------------------------------------------
 template <int HD, int G, bool MOE>
 __global__ void __launch_bounds__(kBlockThreads, 1)
-    k_mega_decode(const __grid_constant__ MegaArgs a, int buf_bytes, int nbuf, int parts) {
-  extern __shared__ __align__(128) char dyn[];
+    k_mega_decode(const __grid_constant__ MegaArgs a) {
+  char* dyn = s_dyn;
+  const int buf_bytes = a.buf_bytes, nbuf = a.nbuf, parts = a.parts;
   __shared__ float red[32];
   __shared__ float cbest_v[kWarps];
   __shared__ int cbest_i[kWarps];
-  __shared__ __align__(8) uint64_t full_bar[kMaxRing];
-  __shared__ __align__(8) uint64_t empty_bar[kMaxRing];
   __shared__ __align__(8) uint64_t gain_bar[2];
-  __shared__ __align__(16) float mv_red[2 * kWarps * kMaxChunkRows];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int D32 = (a.D + 31) / 32 * 32;
   float* xraw = reinterpret_cast<float*>(dyn + (size_t)nbuf * buf_bytes);  // [D]
@@ -1943,8 +1945,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   for (int i = threadIdx.x; i < a.L; i += kBlockThreads) s_layers[i] = a.layers[i];
   if (threadIdx.x == 0) {
     for (int i = 0; i < nbuf; i++) {
-      mbar_init(&full_bar[i], 1);
-      mbar_init(&empty_bar[i], kWarps);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], kWarps);
     }
     mbar_init(&gain_bar[0], 1);
     mbar_init(&gain_bar[1], 1);
@@ -1973,18 +1975,12 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   }
   __syncthreads();
   if (warp == kWarps) {
-    produce<MOE>(a, dyn, buf_bytes, nbuf, full_bar, empty_bar);
+    produce<MOE>(a, dyn, buf_bytes, nbuf, s_full, s_empty);
     return;
   }
   Ring r;
-  r.base = dyn;
-  r.full = full_bar;
-  r.empty = empty_bar;
-  r.nbuf = nbuf;
-  r.buf_bytes = buf_bytes;
   r.g = 0;
   r.nred = 0;
-  r.red = mv_red;
   Gains gs;
   gs.buf[0] = gain_buf;
   gs.buf[1] = gain_buf + D32;
@@ -2394,7 +2390,11 @@ void mega_decode(const MegaArgs& a, int grid, size_t smem, cudaStream_t s) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int nbuf = ring_count();
-  void* args[] = {(void*)&a, (void*)&buf, (void*)&nbuf, (void*)&parts};
+  MegaArgs ak = a;
+  ak.buf_bytes = buf;
+  ak.nbuf = nbuf;
+  ak.parts = parts;
+  void* args[] = {(void*)&ak};
   SG_CUDA(cudaLaunchKernelExC(&cfg, k, args));
 }
 

@@ -78,6 +78,9 @@ struct MegaArgs {
   int gen_len;              // capacity of gen: writes at step >= gen_len are dropped
   int* err;                 // set non-zero when a wait times out
   unsigned long long wait_ns;  // bound of every wait (ns)
+  // Set by mega_decode: the ring's buffers (nbuf of buf_bytes) and the
+  // activation's bf16 parts.
+  int nbuf, buf_bytes, parts;
   // Mixture of experts (moe != 0): E experts, topk chosen per token, expert
   // FFN width Fe, this rank owning experts [e_begin, e_end).
   int moe, E, topk, Fe, e_begin, e_end;
