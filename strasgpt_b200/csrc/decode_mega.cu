@@ -1003,6 +1003,11 @@ __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const uint16_t
   // the chunk loop when tracing is off.
   const bool tr0 = tr && tid == 0;
   if (tr0) s_tsum[0] = s_tsum[1] = s_tsum[2] = 0;
+  // The chunk's row group and column segment, advanced per chunk (the order
+  // of slice_chunk, without its divisions), and the warp's row sums of the
+  // current row group, kept in registers across its column segments.
+  int grp = 0, segi = 0;
+  float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
   for (int ci = 0; ci < s.nchunks; ci++) {
     const int b = (int)(r.g % a.nbuf);
     if (tr0) s_tsum[3] = now_ns();
@@ -1015,7 +1020,18 @@ __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const uint16_t
       }
     }
     if (ci == 0) trace_mark(a, ph, MARK_READY);
-    const Chunk ch = slice_chunk(s, phs, ci);
+    Chunk ch;
+    ch.r0 = s.rb + grp * s.rows;
+    ch.r1 = min(ch.r0 + s.rows, s.re);
+    ch.seg = segi;
+    ch.k0 = segi * s.kseg;
+    ch.k1 = min(ch.k0 + s.kseg, phs.K);
+    ch.first_seg = segi == 0;
+    ch.last_seg = segi == s.spp - 1;
+    if (++segi == s.spp) {
+      segi = 0;
+      grp++;
+    }
     const int nr = ch.r1 - ch.r0;
     const int stride = row_stride(ch.k1 - ch.k0);
     const int nkb = (ch.k1 - ch.k0) >> 5;
@@ -1052,7 +1068,7 @@ __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const uint16_t
     __syncwarp();
     // Column p of the accumulators holds part p's products: lane 4g has
     // parts 0, 1 and lane 4g + 1 part 2 of rows g and g + 8. The warp's row
-    // sums go to (or, for later column segments, add to) its red row.
+    // sums go to its red row.
     float* red = s_mvred + (size_t)(r.nred & 1) * kWarps * kMaxChunkRows;
     float* wred = red + warp * kMaxChunkRows;
     if (fold) {
@@ -1083,11 +1099,12 @@ __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const uint16_t
         const bool two = ng > 1;  // ng <= 2: dense chunks have at most 32 rows
         const uint32_t l0 = bbase + (uint32_t)(min(m, nr - 1) * stride);
         const uint32_t l1 = bbase + (uint32_t)(min(16 + m, nr - 1) * stride);
-        // One accumulator per row group (both k16 steps of a block add into
-        // it), fragments as values; both groups always (with one group, the
+        // One accumulator per 16-row group (both k16 steps of a block add
+        // into it, and so do the later column segments of the chunk's rows),
+        // fragments as values; both groups always (with one group, the
         // second reads the chunk's last row again and is discarded), so the
         // loop has no branches and no arrays.
-        float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
+        if (ch.first_seg) acc0 = acc1 = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 1
         for (int kb = warp; kb < nkw; kb += kWarps) {
           uint4 x0 = make_uint4(0u, 0u, 0u, 0u);
@@ -1102,23 +1119,17 @@ __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const uint16_t
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(s_empty + b);  // done with buffer b
+        // After the row group's last column segment: the warp's row sums.
 #pragma unroll
         for (int q = 0; q < 2; q++) {
-          if (q == 1 && !two) break;
+          if (!ch.last_seg || (q == 1 && !two)) break;
           const float4 aq = q ? acc1 : acc0;
-          const float cc[4] = {aq.x, aq.y, aq.z, aq.w};
-          const float lo0 = __shfl_down_sync(0xFFFFFFFFu, cc[0], 1);
-          const float lo2 = __shfl_down_sync(0xFFFFFFFFu, cc[2], 1);
+          const float lo0 = __shfl_down_sync(0xFFFFFFFFu, aq.x, 1);
+          const float lo2 = __shfl_down_sync(0xFFFFFFFFu, aq.z, 1);
           if (c == 0) {
             const int rr = q * 16 + g;
-            const float v0 = (cc[0] + cc[1]) + lo0, v8 = (cc[2] + cc[3]) + lo2;
-            if (ch.first_seg) {
-              wred[rr] = v0;
-              wred[rr + 8] = v8;
-            } else {
-              wred[rr] += v0;
-              wred[rr + 8] += v8;
-            }
+            wred[rr] = (aq.x + aq.y) + lo0;
+            wred[rr + 8] = (aq.z + aq.w) + lo2;
           }
         }
       }
