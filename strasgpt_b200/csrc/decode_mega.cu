@@ -927,7 +927,18 @@ __shared__ unsigned long long s_tsum[4];  // trace: wait, dot, reduce sums; last
 struct Ring {
   unsigned g;      // chunks consumed so far
   unsigned nred;   // cross-warp reductions so far (selects the row-sum half)
+  int b;           // buffer of chunk g (g mod nbuf)
+  unsigned par;    // phase parity of that buffer's barriers ((g / nbuf) & 1)
 };
+
+// The next chunk of the ring (without a division per chunk).
+__device__ __forceinline__ void ring_next(Ring& r, const MegaArgs& a) {
+  r.g++;
+  if (++r.b == a.nbuf) {
+    r.b = 0;
+    r.par ^= 1u;
+  }
+}
 
 // Where a phase's outputs go.
 struct Out {
@@ -988,12 +999,12 @@ __device__ __forceinline__ void pair_epilogue(const MegaArgs& a, const Out& o, i
 // memory (added up over the column segments of a row group); after the last
 // segment the warps' sums meet and thread t finishes row pair t. For the LM
 // head, (bv, bi) track the thread's argmax.
-template <bool MOE>
+template <bool MOE, int KIND>
 __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const uint16_t* xq, int parts,
                               const Out& o, float& bv, int& bi, int ph) {
   trace_mark(a, ph, MARK_STAGED);
   const Phase phs = weight_phase<MOE>(a, wp);
-  const Slice s = s_slices[phs.kind];
+  const Slice s = s_slices[KIND];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, c = lane & 3;
   const int xps = xq_stride(phs.K) / 8;  // uint4 per activation part
@@ -1009,9 +1020,9 @@ __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const uint16_t
   int grp = 0, segi = 0;
   float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
   for (int ci = 0; ci < s.nchunks; ci++) {
-    const int b = (int)(r.g % a.nbuf);
+    const int b = r.b;
     if (tr0) s_tsum[3] = now_ns();
-    wait_bar(a, s_full + b, (r.g / a.nbuf) & 1);
+    wait_bar(a, s_full + b, r.par);
     if (tr) {
       const unsigned long long t1 = now_ns();
       if (tr0) {
@@ -1151,11 +1162,11 @@ __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const uint16_t
           y0 += red[w * kMaxChunkRows + 2 * tid];
           y1 += red[w * kMaxChunkRows + 2 * tid + 1];
         }
-        pair_epilogue(a, o, phs.kind, (ch.r0 >> 1) + tid, y0, y1, bv, bi);
+        pair_epilogue(a, o, KIND, (ch.r0 >> 1) + tid, y0, y1, bv, bi);
       }
       if (tr0) s_tsum[2] += now_ns() - s_tsum[3];
     }
-    r.g++;
+    ring_next(r, a);
   }
   trace_mark(a, ph, MARK_CONSUMED);
   if (tr0) {
@@ -1352,9 +1363,9 @@ __device__ void consume_mx_gu(const MegaArgs& a, Ring& r, int l, const uint8_t* 
   const bool tr = a.trace != nullptr;
   unsigned long long t_wait = 0, t0 = 0;
   for (int ci = 0; ci < s.nchunks; ci++) {
-    const int b = (int)(r.g % a.nbuf);
+    const int b = r.b;
     if (tr) t0 = now_ns();
-    wait_bar(a, s_full + b, (r.g / a.nbuf) & 1);
+    wait_bar(a, s_full + b, r.par);
     if (tr) t_wait += now_ns() - t0;
     if (ci == 0) trace_mark(a, ph, MARK_READY);
     int p0, np;
@@ -1380,7 +1391,7 @@ __device__ void consume_mx_gu(const MegaArgs& a, Ring& r, int l, const uint8_t* 
         ll_store(hm + (size_t)j * a.Fe + f0 + tid, swiglu(gs, us), e);
       }
     }
-    r.g++;
+    ring_next(r, a);
   }
   csync();  // the xm region (the normalised x) is read no more
   trace_mark(a, ph, MARK_CONSUMED);
@@ -1423,9 +1434,9 @@ __device__ void consume_mx_down(const MegaArgs& a, Ring& r, const uint8_t* xm, c
   const bool tr = a.trace != nullptr;
   unsigned long long t_wait = 0, t0 = 0;
   for (int ci = 0; ci < s.nchunks; ci++) {
-    const int b = (int)(r.g % a.nbuf);
+    const int b = r.b;
     if (tr) t0 = now_ns();
-    wait_bar(a, s_full + b, (r.g / a.nbuf) & 1);
+    wait_bar(a, s_full + b, r.par);
     if (tr) t_wait += now_ns() - t0;
     if (ci == 0) trace_mark(a, ph, MARK_READY);
     const Chunk ch = slice_chunk(s, phs, ci);
@@ -1453,7 +1464,7 @@ __device__ void consume_mx_down(const MegaArgs& a, Ring& r, const uint8_t* xm, c
         pair_epilogue(a, o, W_EDOWN, (ch.r0 >> 1) + tid, y0, y1, bv, bi);
       }
     }
-    r.g++;
+    ring_next(r, a);
   }
   trace_mark(a, ph, MARK_CONSUMED);
   trace_put(a, ph, SUM_WAIT, t_wait);
@@ -1992,6 +2003,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   Ring r;
   r.g = 0;
   r.nred = 0;
+  r.b = 0;
+  r.par = 0;
   Gains gs;
   gs.buf[0] = gain_buf;
   gs.buf[1] = gain_buf + D32;
@@ -2032,7 +2045,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
       else
         stage_norm_ll(a, x_o - 2 * (size_t)a.D + a.D, e, gs, 0, a.D, xq, parts, xraw, red, ph);
       gains_fill(gs, 0, l + 1 < a.L ? s_layers[l + 1].attn_norm : a.out_norm, a.D);
-      consume_phase<MOE>(a, r, P * l + 0, xq, parts,
+      consume_phase<MOE, W_QKV>(a, r, P * l + 0, xq, parts,
                     Out{a.ll + a.llo.qkv + (size_t)l * a.QKVl, nullptr, e}, bv, bi, ph);
       ph++;
       // ATTN
@@ -2056,7 +2069,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
       stage_plain_ll(a, a.ll + a.llo.att + (size_t)l * QD, e, QD, xq, parts, ph);
       {
         const size_t part0 = a.llo.xpart + (size_t)(l * 2 + 0) * a.world * a.D;
-        consume_phase<MOE>(a, r, P * l + 1, xq, parts,
+        consume_phase<MOE, W_O>(a, r, P * l + 1, xq, parts,
                       Out{x_o, xraw, e, part0 + (size_t)a.rank * a.D}, bv, bi, ph);
         if (a.world > 1)
           tp_reduce_rows(a, xraw, part0, x_o, s_slices[W_O].rb, s_slices[W_O].re, e);
@@ -2072,7 +2085,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
       const size_t part_d = a.llo.xpart + (size_t)(l * 2 + 1) * a.world * a.D;
       if constexpr (MOE) {
         // router logits, then every CTA picks the experts
-        consume_phase<MOE>(a, r, P * l + 2, xq, parts,
+        consume_phase<MOE, W_ROUTER>(a, r, P * l + 2, xq, parts,
                       Out{a.ll + a.llo.rl + (size_t)l * a.E, nullptr, e}, bv, bi, ph);
         if (warp == 0) expert_select(a, l, e, s_csel, s_cselw);
         csync();
@@ -2091,13 +2104,13 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         ph++;
       } else {
         // gate/up + SwiGLU
-        consume_phase<MOE>(a, r, P * l + 2, xq, parts,
+        consume_phase<MOE, W_GU>(a, r, P * l + 2, xq, parts,
                       Out{a.ll + a.llo.h + (size_t)l * a.Fl, nullptr, e}, bv, bi, ph);
         ph++;
         // down + residual
         trace_mark(a, ph, MARK_BEGIN);
         stage_plain_ll(a, a.ll + a.llo.h + (size_t)l * a.Fl, e, a.Fl, xq, parts, ph);
-        consume_phase<MOE>(a, r, P * l + 3, xq, parts,
+        consume_phase<MOE, W_DOWN>(a, r, P * l + 3, xq, parts,
                       Out{x_d, xraw, e, part_d + (size_t)a.rank * a.D}, bv, bi, ph);
         if (a.world > 1)
           tp_reduce_rows(a, xraw, part_d, x_d, s_slices[W_DOWN].rb, s_slices[W_DOWN].re, e);
@@ -2111,7 +2124,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     if (s + 1 < a.steps) gains_fill(gs, 0, s_layers[0].attn_norm, a.D);
     bv = -INFINITY;
     bi = 0x7FFFFFFF;
-    consume_phase<MOE>(a, r, P * a.L, xq, parts, Out{nullptr, nullptr, e}, bv, bi, ph);
+    consume_phase<MOE, W_LM>(a, r, P * a.L, xq, parts, Out{nullptr, nullptr, e}, bv, bi, ph);
     // Warp argmax (ties: lower index), then the warps' in order.
     for (int o = 16; o > 0; o >>= 1) {
       const float v2 = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
