@@ -320,7 +320,12 @@ struct Phase {
 // Per-layer weight pointers, copied to shared memory at kernel start so that
 // no global load sits on the phase-to-phase critical path.
 constexpr int kMaxLayers = 96;
-__shared__ MegaLayer s_layers[kMaxLayers];
+// It sits at the end of the dynamic region (a.layers_off), sized by the
+// model's layer count.
+extern __shared__ __align__(128) char s_dyn[];
+__device__ __forceinline__ MegaLayer* layer_table(const MegaArgs& a) {
+  return reinterpret_cast<MegaLayer*>(s_dyn + a.layers_off);
+}
 
 // Weight phases per layer: dense QKV, O, GU, DOWN; mixture of experts QKV,
 // O, ROUTER, EGU, EDOWN. The LM head follows the last layer. MOE (a.moe) is
@@ -431,7 +436,7 @@ __device__ __forceinline__ Phase weight_phase(const MegaArgs& a, int wp) {
     p.pairs = a.Vl / 2;
     return p;
   }
-  const MegaLayer& ly = s_layers[wp / phases_per_layer<MOE>(a)];
+  const MegaLayer& ly = layer_table(a)[wp / phases_per_layer<MOE>(a)];
   switch (p.kind) {
     case W_QKV:
       p.W = ly.wqkv;
@@ -636,7 +641,7 @@ __device__ void produce_mx(const MegaArgs& a, const Phase& ph, const Slice& sl, 
                            int ci, int l, char* buf, uint64_t* bar) {
   const int lane = threadIdx.x & 31;
   const int cb = ph.K / 2, sb = mx_scale_bytes(ph.K);
-  const MegaLayer& ly = s_layers[l];
+  const MegaLayer& ly = layer_table(a)[l];
   if (ph.kind == W_EGU) {
     int p0, np;
     egu_chunk(sl.rb / 2, sl.re / 2, sl.rows / 2, a.Fe, ci, p0, np);
@@ -770,36 +775,38 @@ __device__ __forceinline__ float cta_sum(float v, float* red) {
 constexpr int kNormBatch = 16;
 constexpr int kNormMaxK = 8192;
 
-// RMSNorm gains in shared memory: two bf16 vectors of D, refilled by bulk
-// copies (consumer thread 0) one phase or more before they are needed, so
-// that no gain load sits on a phase's critical path. Buffer 0 holds the
-// attention norm of the coming QKV phase (or the final norm), buffer 1 the
-// FFN norm. Every consumer thread counts the fills; thread 0 issues them.
+// RMSNorm gains in shared memory: one bf16 vector of D, refilled by a bulk
+// copy (consumer thread 0) as soon as a norm staging is done with it, with
+// the gains of the next norm (after the attention norm the FFN norm, after
+// the FFN norm the next layer's attention norm or the final norm), two
+// phases or more before they are needed, so that no gain load sits on a
+// phase's critical path. Every consumer thread counts the fills; thread 0
+// issues them.
 struct Gains {
-  uint16_t* buf[2];
-  uint64_t* bar;   // [2] in shared memory
-  unsigned n[2];   // fills issued so far
+  uint16_t* buf;
+  uint64_t* bar;   // in shared memory
+  unsigned n;      // fills issued so far
 };
 
-__device__ __forceinline__ void gains_fill(Gains& gs, int i, const uint16_t* src, int D) {
+__device__ __forceinline__ void gains_fill(Gains& gs, const uint16_t* src, int D) {
   if (threadIdx.x == 0) {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    mbar_expect_tx(gs.bar + i, (unsigned)D * 2u);
-    bulk_copy(gs.buf[i], src, (unsigned)D * 2u, gs.bar + i);
+    mbar_expect_tx(gs.bar, (unsigned)D * 2u);
+    bulk_copy(gs.buf, src, (unsigned)D * 2u, gs.bar);
   }
-  gs.n[i]++;
+  gs.n++;
 }
 
-__device__ __forceinline__ const uint16_t* gains_ready(const MegaArgs& a, Gains& gs, int i) {
-  wait_bar(a, gs.bar + i, (gs.n[i] - 1) & 1);
-  return gs.buf[i];
+__device__ __forceinline__ const uint16_t* gains_ready(const MegaArgs& a, Gains& gs) {
+  wait_bar(a, gs.bar, (gs.n - 1) & 1);
+  return gs.buf;
 }
 
 // xq = rmsnorm(x) * gains from the flagged vector src (epoch e); the raw
 // values also go to xraw[K] (and the normalised ones to the xm region, as
 // vector 0, when set). Thread t owns k = t + u * kThreads. The loops are kept short: this code
 // runs once per phase, from a cold instruction cache.
-__device__ void stage_norm_ll(const MegaArgs& a, const u64* src, unsigned e, Gains& gs, int gi,
+__device__ void stage_norm_ll(const MegaArgs& a, const u64* src, unsigned e, Gains& gs,
                               int K, uint16_t* xq, int parts, float* xraw, float* red, int ph,
                               uint8_t* xm = nullptr) {
   const int tid = threadIdx.x;
@@ -821,7 +828,7 @@ __device__ void stage_norm_ll(const MegaArgs& a, const u64* src, unsigned e, Gai
   trace_mark(a, ph, MARK_NORMED);
   ss /= (float)K;
   const float inv = 1.0f / sqrtf(ss + a.eps);
-  const uint16_t* g = gains_ready(a, gs, gi);
+  const uint16_t* g = gains_ready(a, gs);
   trace_mark(a, ph, MARK_GAINS);
   if (xm) {
     // Also the MXFP4 expert input (K is then a multiple of 32: a warp's
@@ -880,8 +887,8 @@ __device__ void stage_plain_ll(const MegaArgs& a, const u64* src, unsigned e, in
 }
 
 // Layer-0 input: the embedding row of `token` (xraw) and its RMSNorm (xq)
-// with the gains of buffer gi.
-__device__ void stage_embedding(const MegaArgs& a, int token, Gains& gs, int gi, uint16_t* xq,
+// with the gains in shared memory.
+__device__ void stage_embedding(const MegaArgs& a, int token, Gains& gs, uint16_t* xq,
                                 int parts, float* xraw, float* red) {
   const int tid = threadIdx.x, K = a.D;
   const uint16_t* row = a.emb + (size_t)token * K;
@@ -905,7 +912,7 @@ __device__ void stage_embedding(const MegaArgs& a, int token, Gains& gs, int gi,
   ss = cta_sum(ss, red);
   ss /= (float)K;
   const float inv = 1.0f / sqrtf(ss + a.eps);
-  const uint16_t* g = gains_ready(a, gs, gi);
+  const uint16_t* g = gains_ready(a, gs);
   for (int k = tid; k < K; k += kThreads)
     xq_put(xq, K, parts, k, (xraw[k] * inv) * bf16_to_f32(g[k]));
   csync();
@@ -918,7 +925,6 @@ __device__ void stage_embedding(const MegaArgs& a, int token, Gains& gs, int gi,
 // the dynamic region, a.buf_bytes apart; the barriers and the per-warp row
 // sums in file-scope arrays) and its geometry in the kernel arguments, so
 // that the chunk loops keep only two counters in registers.
-extern __shared__ __align__(128) char s_dyn[];
 __shared__ __align__(8) uint64_t s_full[kMaxRing];   // the chunk in buffer b has landed
 __shared__ __align__(8) uint64_t s_empty[kMaxRing];  // the consumer warps are done with it
 __shared__ __align__(16) float s_mvred[2 * kWarps * kMaxChunkRows];  // per-warp row sums
@@ -1596,7 +1602,7 @@ __device__ void prefetch_kv(const MegaArgs& a, int l, int pos) {
 // CTAs read them on the phase's critical path.
 __device__ void prefetch_gains(const MegaArgs& a, int l) {
   if (threadIdx.x != 32 || l >= a.L) return;
-  const MegaLayer& ly = s_layers[l];
+  const MegaLayer& ly = layer_table(a)[l];
   if (ly.q_norm) prefetch_l2(ly.q_norm, (uint32_t)a.HD * 2);
   if (ly.k_norm) prefetch_l2(ly.k_norm, (uint32_t)a.HD * 2);
 }
@@ -1950,28 +1956,27 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   __shared__ float red[32];
   __shared__ float cbest_v[kWarps];
   __shared__ int cbest_i[kWarps];
-  __shared__ __align__(8) uint64_t gain_bar[2];
+  __shared__ __align__(8) uint64_t gain_bar[1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int D32 = (a.D + 31) / 32 * 32;
   float* xraw = reinterpret_cast<float*>(dyn + (size_t)nbuf * buf_bytes);  // [D]
-  uint16_t* gain_buf = reinterpret_cast<uint16_t*>(xraw + D32);              // [2][D]
+  uint16_t* gain_buf = reinterpret_cast<uint16_t*>(xraw + D32);              // [D]
   // MoE: the xm region (expert inputs as f16 parts: the normalised x, then
   // the selected experts' SwiGLU outputs [topk][Fe]).
-  float* xf = reinterpret_cast<float*>(gain_buf + 2 * D32);
+  float* xf = reinterpret_cast<float*>(gain_buf + D32);
   uint8_t* xm = reinterpret_cast<uint8_t*>(xf);
   // Matvec input (bf16 parts) or attention scratch (floats).
   float* xs = xf + (MOE ? moe_xf_floats(a.D, a.topk, a.Fe) : 0);
   uint16_t* xq = reinterpret_cast<uint16_t*>(xs);
   __shared__ int s_csel[kMaxTopk];
   __shared__ float s_cselw[kMaxTopk];
-  for (int i = threadIdx.x; i < a.L; i += kBlockThreads) s_layers[i] = a.layers[i];
+  for (int i = threadIdx.x; i < a.L; i += kBlockThreads) layer_table(a)[i] = a.layers[i];
   if (threadIdx.x == 0) {
     for (int i = 0; i < nbuf; i++) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], kWarps);
     }
     mbar_init(&gain_bar[0], 1);
-    mbar_init(&gain_bar[1], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -2006,12 +2011,10 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   r.b = 0;
   r.par = 0;
   Gains gs;
-  gs.buf[0] = gain_buf;
-  gs.buf[1] = gain_buf + D32;
+  gs.buf = gain_buf;
   gs.bar = gain_bar;
-  gs.n[0] = gs.n[1] = 0;
-  gains_fill(gs, 0, s_layers[0].attn_norm, a.D);
-  gains_fill(gs, 1, s_layers[0].ffn_norm, a.D);
+  gs.n = 0;
+  gains_fill(gs, layer_table(a)[0].attn_norm, a.D);
   int ph = 0;  // phase counter (trace only)
   int pos = __ldcg(a.pos);
   int token = __ldcg(a.tok);
@@ -2028,7 +2031,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   for (int s = 0; s < a.steps; s++) {
     const unsigned e = a.epoch + (unsigned)s;
     for (int l = 0; l < a.L; l++) {
-      const MegaLayer& ly = s_layers[l];
+      const MegaLayer& ly = layer_table(a)[l];
       u64* x_o = a.ll + a.llo.x + (size_t)l * 2 * a.D;  // after o_proj
       u64* x_d = x_o + a.D;                              // after down
       // QKV
@@ -2041,10 +2044,10 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         prefetch_kv<HD>(a, 0, pos + 1);
       prefetch_gains(a, l + 1);
       if (l == 0)
-        stage_embedding(a, token, gs, 0, xq, parts, xraw, red);
+        stage_embedding(a, token, gs, xq, parts, xraw, red);
       else
-        stage_norm_ll(a, x_o - 2 * (size_t)a.D + a.D, e, gs, 0, a.D, xq, parts, xraw, red, ph);
-      gains_fill(gs, 0, l + 1 < a.L ? s_layers[l + 1].attn_norm : a.out_norm, a.D);
+        stage_norm_ll(a, x_o - 2 * (size_t)a.D + a.D, e, gs, a.D, xq, parts, xraw, red, ph);
+      gains_fill(gs, ly.ffn_norm, a.D);
       consume_phase<MOE, W_QKV>(a, r, P * l + 0, xq, parts,
                     Out{a.ll + a.llo.qkv + (size_t)l * a.QKVl, nullptr, e}, bv, bi, ph);
       ph++;
@@ -2077,11 +2080,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
       ph++;
       // FFN input: RMSNorm of x_o (for MoE also as f16 parts in xm)
       trace_mark(a, ph, MARK_BEGIN);
-      stage_norm_ll(a, x_o, e, gs, 1, a.D, xq, parts, xraw, red, ph, MOE ? xm : nullptr);
-      if (l + 1 < a.L)
-        gains_fill(gs, 1, s_layers[l + 1].ffn_norm, a.D);
-      else if (s + 1 < a.steps)
-        gains_fill(gs, 1, s_layers[0].ffn_norm, a.D);
+      stage_norm_ll(a, x_o, e, gs, a.D, xq, parts, xraw, red, ph, MOE ? xm : nullptr);
+      gains_fill(gs, l + 1 < a.L ? layer_table(a)[l + 1].attn_norm : a.out_norm, a.D);
       const size_t part_d = a.llo.xpart + (size_t)(l * 2 + 1) * a.world * a.D;
       if constexpr (MOE) {
         // router logits, then every CTA picks the experts
@@ -2119,9 +2119,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     }
     // LM head with per-CTA argmax
     trace_mark(a, ph, MARK_BEGIN);
-    stage_norm_ll(a, a.ll + a.llo.x + (size_t)(a.L - 1) * 2 * a.D + a.D, e, gs, 0, a.D, xq, parts,
+    stage_norm_ll(a, a.ll + a.llo.x + (size_t)(a.L - 1) * 2 * a.D + a.D, e, gs, a.D, xq, parts,
                   xraw, red, ph);
-    if (s + 1 < a.steps) gains_fill(gs, 0, s_layers[0].attn_norm, a.D);
+    if (s + 1 < a.steps) gains_fill(gs, layer_table(a)[0].attn_norm, a.D);
     bv = -INFINITY;
     bi = 0x7FFFFFFF;
     consume_phase<MOE, W_LM>(a, r, P * a.L, xq, parts, Out{nullptr, nullptr, e}, bv, bi, ph);
@@ -2235,17 +2235,23 @@ size_t select_attn_floats(int HD, int G) {
 }
 
 // Activation region, rounded to 128 bytes: the residual copy xraw [D]
-// (rounded to 32 floats), two bf16 gain vectors [D] (same rounding), then
+// (rounded to 32 floats), one bf16 gain vector [D] (same rounding), then
 // the matvec input (`parts` bf16 arrays of K + 32 columns), the attention
 // scratch or the attention merge's partials (3 floats per thread).
 
-size_t act_bytes(int D, int QD, int Fl, int HD, int G, int parts, int xf_floats = 0) {
+size_t act_core_bytes(int D, int QD, int Fl, int HD, int G, int parts, int xf_floats) {
   const size_t kmax = (size_t)std::max(D, std::max(QD, Fl));
   size_t bytes = std::max((size_t)parts * 2 * (kmax + 32), select_attn_floats(HD, G) * 4);
   bytes = std::max(bytes, (size_t)3 * kThreads * 4);  // the attention merge's partials
-  bytes += (size_t)(D + 31) / 32 * 32 * (4 + 2 * 2);  // xraw, two gain vectors
+  bytes += (size_t)(D + 31) / 32 * 32 * (4 + 2);  // xraw, the gain vector
   bytes += (size_t)xf_floats * 4;
   return (bytes + 127) / 128 * 128;
+}
+
+// ... then the layer table (L entries).
+size_t act_bytes(int D, int QD, int Fl, int HD, int G, int parts, int xf_floats, int L) {
+  return act_core_bytes(D, QD, Fl, HD, G, parts, xf_floats) +
+         ((size_t)L * sizeof(MegaLayer) + 127) / 128 * 128;
 }
 
 // Dynamic shared memory a CTA may take: the device's opt-in limit less the
@@ -2285,13 +2291,14 @@ int ring_count() {
 // otherwise, so that large models keep enough weight bytes in flight.
 // STRASGPT_MEGA_PARTS=2 or 3 overrides the choice (when the ring still
 // fits).
-int act_parts(int D, int QD, int Fl, int HD, int G, int xf) {
+int act_parts(int D, int QD, int Fl, int HD, int G, int xf, int L) {
   const char* v = getenv("STRASGPT_MEGA_PARTS");
   if (v && (atoi(v) == 2 || atoi(v) == 3) &&
-      act_bytes(D, QD, Fl, HD, G, atoi(v), xf) + (size_t)ring_count() * 16 * 1024 <=
+      act_bytes(D, QD, Fl, HD, G, atoi(v), xf, L) + (size_t)ring_count() * 16 * 1024 <=
           smem_budget(HD, G))
     return atoi(v);
-  return act_bytes(D, QD, Fl, HD, G, 3, xf) + (size_t)112 * 1024 <= smem_budget(HD, G) ? 3 : 2;
+  return act_bytes(D, QD, Fl, HD, G, 3, xf, L) + (size_t)112 * 1024 <= smem_budget(HD, G) ? 3
+                                                                                           : 2;
 }
 
 // dst[r][0 .. src_bytes) = src[r][...], dst[r][src_bytes .. dst_bytes) = 0.
@@ -2338,12 +2345,12 @@ MegaFlagged mega_flagged_layout(int D, int QKVl, int QD, int Fl, int L, int grid
 
 // Ring buffers take what the activations leave of the budget. Every row
 // length (D, QD, Fl) must be a multiple of 32 columns.
-size_t mega_smem_bytes(int D, int QD, int Fl, int HD, int G, int topk, int Fe) {
+size_t mega_smem_bytes(int D, int QD, int Fl, int HD, int G, int L, int topk, int Fe) {
   if (!select(HD, G)) return 0;
-  if (D > kNormMaxK) return 0;
+  if (D > kNormMaxK || L > kMaxLayers) return 0;
   if (D % 32 || QD % 32 || Fl % 32 || Fe % 32) return 0;
   const int xf = moe_xf_floats(D, topk, Fe);
-  const size_t act = act_bytes(D, QD, Fl, HD, G, act_parts(D, QD, Fl, HD, G, xf), xf);
+  const size_t act = act_bytes(D, QD, Fl, HD, G, act_parts(D, QD, Fl, HD, G, xf, L), xf, L);
   const size_t budget = smem_budget(HD, G);
   const int nbuf = ring_count();
   if (act + (size_t)nbuf * 16 * 1024 > budget) return 0;
@@ -2351,8 +2358,8 @@ size_t mega_smem_bytes(int D, int QD, int Fl, int HD, int G, int topk, int Fe) {
   return (size_t)nbuf * buf + act;
 }
 
-static int buffer_bytes(size_t smem, int D, int QD, int Fl, int HD, int G, int xf) {
-  return (int)((smem - act_bytes(D, QD, Fl, HD, G, act_parts(D, QD, Fl, HD, G, xf), xf)) /
+static int buffer_bytes(size_t smem, int D, int QD, int Fl, int HD, int G, int xf, int L) {
+  return (int)((smem - act_bytes(D, QD, Fl, HD, G, act_parts(D, QD, Fl, HD, G, xf, L), xf, L)) /
                ring_count());
 }
 
@@ -2396,13 +2403,13 @@ void mega_decode(const MegaArgs& a, int grid, size_t smem, cudaStream_t s) {
   if (a.nsplit > kMaxSplits) SG_DIE("megakernel: too many attention splits");
   if (a.L > kMaxLayers) SG_DIE("megakernel: too many layers");
   const int xf = moe_xf_floats(a.D, a.moe ? a.topk : 0, a.Fe);
-  int buf = buffer_bytes(smem, a.D, a.QHl * a.HD, a.Fl, a.HD, a.G, xf);
+  int buf = buffer_bytes(smem, a.D, a.QHl * a.HD, a.Fl, a.HD, a.G, xf, a.L);
   if (buf < 16 * 1024 || buf % 1024) SG_DIE("megakernel: weight buffers too small");
   if (a.moe && (a.topk < 1 || a.topk > kMaxTopk || a.E > 128 || a.E % 2))
     SG_DIE("megakernel: unsupported expert count / top-k");
   if (a.moe && 2 * mx_row_bytes(std::max(a.D, a.Fe)) > buf)
     SG_DIE("megakernel: weight buffers too small for two expert rows");
-  int parts = act_parts(a.D, a.QHl * a.HD, a.Fl, a.HD, a.G, xf);
+  int parts = act_parts(a.D, a.QHl * a.HD, a.Fl, a.HD, a.G, xf, a.L);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kBlockThreads);
@@ -2417,6 +2424,8 @@ void mega_decode(const MegaArgs& a, int grid, size_t smem, cudaStream_t s) {
   MegaArgs ak = a;
   ak.buf_bytes = buf;
   ak.nbuf = nbuf;
+  ak.layers_off = (long long)nbuf * buf +
+                  (long long)act_core_bytes(a.D, a.QHl * a.HD, a.Fl, a.HD, a.G, parts, xf);
   ak.parts = parts;
   void* args[] = {(void*)&ak};
   SG_CUDA(cudaLaunchKernelExC(&cfg, k, args));

@@ -81,6 +81,7 @@ struct MegaArgs {
   // Set by mega_decode: the ring's buffers (nbuf of buf_bytes) and the
   // activation's bf16 parts.
   int nbuf, buf_bytes, parts;
+  long long layers_off;  // byte offset of the layer table in dynamic smem
   // Mixture of experts (moe != 0): E experts, topk chosen per token, expert
   // FFN width Fe, this rank owning experts [e_begin, e_end).
   int moe, E, topk, Fe, e_begin, e_end;
@@ -102,7 +103,7 @@ constexpr int kMegaTraceWidth = 13;
 
 // Dynamic shared memory the megakernel needs for these dimensions (for a
 // mixture of experts, Fl = 0, topk and Fe set; dense: topk = Fe = 0).
-size_t mega_smem_bytes(int D, int QD, int Fl, int HD, int G, int topk = 0, int Fe = 0);
+size_t mega_smem_bytes(int D, int QD, int Fl, int HD, int G, int L, int topk = 0, int Fe = 0);
 // Largest grid that is co-resident (one CTA per SM); 0 if not launchable.
 int mega_grid(size_t smem, int HD, int G);
 // Decode split used by the megakernel (split_len a multiple of 64).

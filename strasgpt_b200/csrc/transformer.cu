@@ -570,7 +570,7 @@ void alloc_state(const W_t* w, const transformer_configuration_t* c, S_t* s) {
   s->use_mega = moe_ok && (w->Vl % 2 == 0) && w->L <= 96 && w->world <= 8 && w->D <= 8192 &&
                 env_int("STRASGPT_MEGA", 1) != 0;
   if (s->use_mega) {
-    s->mega_smem = sg::mega_smem_bytes(w->D, w->QHl * w->HD, mega_Fl, w->HD, w->G,
+    s->mega_smem = sg::mega_smem_bytes(w->D, w->QHl * w->HD, mega_Fl, w->HD, w->G, w->L,
                                        w->moe ? w->topk : 0, w->moe ? w->F : 0);
     if (s->mega_smem == 0) s->use_mega = false;
   }
