@@ -79,7 +79,7 @@ constexpr int kThreads = 32 * kWarps;       // consumer threads
 constexpr int kBlockThreads = kThreads + 32;  // + the producer warp
 constexpr int kPosPerPass = kWarps * 8;  // cache rows per CTA pass
 constexpr int kMaxChunkRows = 64;        // rows per MXFP4 weight chunk (4 fragments)
-constexpr int kMaxDenseRows = 32;        // rows per bf16 weight chunk (2 fragments)
+constexpr int kMaxDenseRows = 48;        // rows per bf16 weight chunk (3 fragments)
 constexpr int kPad = 16;                 // extra bytes per row in a buffer
 constexpr int kMaxRing = 4;              // weight buffers per CTA (at most)
 constexpr int kMaxSplits = 64;
@@ -1024,7 +1024,7 @@ __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const uint16_t
   // of slice_chunk, without its divisions), and the warp's row sums of the
   // current row group, kept in registers across its column segments.
   int grp = 0, segi = 0;
-  float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
+  float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0, acc2 = acc0;
   for (int ci = 0; ci < s.nchunks; ci++) {
     const int b = r.b;
     if (tr0) s_tsum[3] = now_ns();
@@ -1109,19 +1109,22 @@ __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const uint16_t
         wred[g] = v;
       }
     } else {
-      // Both row groups of the chunk (at most 32 rows) per 32-column block:
-      // the block's four fragment loads issued before its four MMAs (two
-      // accumulator chains), so that the ldmatrix and MMA latencies overlap.
+      // The chunk's 16-row groups (at most three: 48 rows) per 32-column
+      // block: each block's fragment loads issued before its MMAs (one
+      // accumulator chain per group), so that the ldmatrix and MMA latencies
+      // overlap.
       {
-        const bool two = ng > 1;  // ng <= 2: dense chunks have at most 32 rows
+        const bool two = ng > 1;    // ng <= 3: dense chunks have at most 48 rows
+        const bool three = ng > 2;  // (a third group mostly for a slice's last rows)
         const uint32_t l0 = bbase + (uint32_t)(min(m, nr - 1) * stride);
         const uint32_t l1 = bbase + (uint32_t)(min(16 + m, nr - 1) * stride);
+        const uint32_t l2 = bbase + (uint32_t)(min(32 + m, nr - 1) * stride);
         // One accumulator per 16-row group (both k16 steps of a block add
         // into it, and so do the later column segments of the chunk's rows),
-        // fragments as values; both groups always (with one group, the
-        // second reads the chunk's last row again and is discarded), so the
-        // loop has no branches and no arrays.
-        if (ch.first_seg) acc0 = acc1 = make_float4(0.f, 0.f, 0.f, 0.f);
+        // fragments as values; the first two groups always (with one group,
+        // the second reads the chunk's last row again and is discarded), so
+        // the common loop has no branches and no arrays.
+        if (ch.first_seg) acc0 = acc1 = acc2 = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 1
         for (int kb = warp; kb < nkw; kb += kWarps) {
           uint4 x0 = make_uint4(0u, 0u, 0u, 0u);
@@ -1133,14 +1136,19 @@ __device__ void consume_phase(const MegaArgs& a, Ring& r, int wp, const uint16_t
           mma4(acc1, f10, x0.x, x0.y);
           mma4(acc0, f01, x0.z, x0.w);
           mma4(acc1, f11, x0.z, x0.w);
+          if (three) {
+            const uint4 f20 = ldsm4(l2 + o0), f21 = ldsm4(l2 + o0 + 32);
+            mma4(acc2, f20, x0.x, x0.y);
+            mma4(acc2, f21, x0.z, x0.w);
+          }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(s_empty + b);  // done with buffer b
         // After the row group's last column segment: the warp's row sums.
 #pragma unroll
-        for (int q = 0; q < 2; q++) {
-          if (!ch.last_seg || (q == 1 && !two)) break;
-          const float4 aq = q ? acc1 : acc0;
+        for (int q = 0; q < 3; q++) {
+          if (!ch.last_seg || (q == 1 && !two) || (q == 2 && !three)) break;
+          const float4 aq = q == 2 ? acc2 : (q ? acc1 : acc0);
           const float lo0 = __shfl_down_sync(0xFFFFFFFFu, aq.x, 1);
           const float lo2 = __shfl_down_sync(0xFFFFFFFFu, aq.z, 1);
           if (c == 0) {
