@@ -102,6 +102,9 @@ class Clocks:
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            # nvidia-smi takes a moment to start sampling; the GPU work that
+            # follows must fall inside its window.
+            time.sleep(1.0)
         except OSError:
             self.proc = None
 
