@@ -116,8 +116,12 @@ PARITY = {c.name: c for c in (C5_L4,)}
 # carries over to C3, whose layers are identical.
 C3_S = C3.with_(name="c3s_llama8b_l2", layers=2, vocab=32768, prompt_len=64,
                 steps=8, bos_token_id=1, eos_token_id=2)
+# The same 2-layer model with C3's 2048-token prompt: the prefill kernels
+# (projections, attention) at C3's shapes, captured under ncu with a few GB
+# on the device.
+C3_P = C3_S.with_(name="c3p_llama8b_l2", prompt_len=2048, steps=4)
 
-PROFILE = {c.name: c for c in (C3_S,)}
+PROFILE = {c.name: c for c in (C3_S, C3_P)}
 
 # Small shapes with the same structural features, for fast parity tests.
 T_LLAMA = ModelConfig("t_llama", "llama", 256, 512, 2, 8, 2, 32, 1024,
