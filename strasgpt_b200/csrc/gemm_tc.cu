@@ -190,8 +190,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ uint32_t tmem_slot;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t sbase = (saddr(smem_raw) + 1023u) & ~1023u;
-  const int r0 = blockIdx.x * BM;  // weight rows
-  const int t0 = blockIdx.y * BN;  // tokens
+  // Token tiles vary fastest: the CTAs resident at a time share a few
+  // weight tiles (each read from HBM about once) and every token tile (the
+  // activations stay in L2); weight tiles varying fastest re-read all
+  // weights once per wave of token tiles.
+  const int t0 = blockIdx.x * BN;  // tokens
+  const int r0 = blockIdx.y * BM;  // weight rows
   const int nk = (p.K + BK - 1) / BK;  // the K tail reads zeros from TMA
 
   if (threadIdx.x == 0) {
@@ -278,20 +282,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(BN + c0), vl);
 #pragma unroll
         for (int j = 0; j < 32; j++) v[j] += vl[j];
+        if (p.epi == EPI_SWIGLU) {
 #pragma unroll
-        for (int j = 0; j < 32; j++) {
-          const int t = t0 + c0 + j;
-          if (p.epi == EPI_SWIGLU) {
+          for (int j = 0; j < 32; j++) {
+            const int t = t0 + c0 + j;
             const float up = __shfl_down_sync(0xFFFFFFFFu, v[j], 1);
             if (t < p.T && (r & 1) == 0 && r + 1 < p.N)
               p.C[(size_t)t * p.ldc + (r >> 1)] = swiglu(v[j], up);
-          } else if (t < p.T && r < p.N) {
-            float* c = p.C + (size_t)t * p.ldc + r;
-            if (p.epi == EPI_STORE)
-              *c = v[j];
-            else
-              *c += v[j];
           }
+        } else {
+          float* cb = p.C + (size_t)(t0 + c0) * p.ldc + r;
+          const int nt = min(32, p.T - (t0 + c0));
+          if (p.epi == EPI_ADD) {
+            // The residual rows: all 32 loads issued before any store (one
+            // read-modify-write at a time left each load's latency exposed).
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+              vl[j] = (j < nt && r < p.N) ? cb[(size_t)j * p.ldc] : 0.f;
+#pragma unroll
+            for (int j = 0; j < 32; j++) v[j] += vl[j];
+          }
+#pragma unroll
+          for (int j = 0; j < 32; j++)
+            if (j < nt && r < p.N) cb[(size_t)j * p.ldc] = v[j];
         }
       }
     }
@@ -376,7 +389,9 @@ constexpr int kWidths[3] = {32, 64, 128};
 
 template <int BN>
 void launch_bn(const TcMap& w, const TcAct& a, int wi, const TcParams& p, cudaStream_t s) {
-  dim3 grid((w.rows + BM - 1) / BM, (p.T + BN - 1) / BN);
+  const int row_tiles = (w.rows + BM - 1) / BM;
+  if (row_tiles > 65535) SG_DIE("tensor-core GEMM: too many weight rows");
+  dim3 grid((p.T + BN - 1) / BN, row_tiles);
   launch(k_gemm_tc<BN>, grid, dim3(kThreads), (size_t)Cfg<BN>::kSmemBytes, s,
          *reinterpret_cast<const CUtensorMap*>(w.bytes),
          *reinterpret_cast<const CUtensorMap*>(a.hi[wi].bytes),
