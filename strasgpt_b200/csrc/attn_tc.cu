@@ -14,7 +14,7 @@
 //   online softmax on the S accumulators (rows g and g + 8 of a lane);
 //   O += P V    P re-packed from the S accumulators into A fragments, V as
 //               the B operand (ldmatrix.trans of [key][hd] tiles).
-// K/V tiles of 64 keys are read from the fp32 cache, split and stored in
+// K/V tiles of kKeysTc keys are read from the fp32 cache, split and stored in
 // shared memory with rows padded by 16 bytes (conflict-free ldmatrix).
 #include "common.cuh"
 #include "kernels.h"
@@ -25,7 +25,9 @@ namespace sg {
 namespace {
 
 constexpr int kRowsTc = 64;  // rows per CTA
-constexpr int kKeysTc = 64;  // keys per tile
+constexpr int kKeysTc = 32;  // keys per tile (two CTAs fit on an SM)
+constexpr int kKT8 = kKeysTc / 8;    // n8 tiles of S
+constexpr int kKT16 = kKeysTc / 16;  // k16 steps of P.V
 
 template <int HD>
 struct TcAttn {
@@ -195,44 +197,44 @@ __global__ void __launch_bounds__(128) k_attn_prefill_tc(AttnPrefillArgs a) {
     // The next tile's rows stream in while this one is multiplied.
     if (k0 + kKeysTc < kend) fetch(k0 + kKeysTc);
 
-    // S = Q K^T: 16 rows x 64 keys per warp (8 n8 tiles).
-    float s[8][4];
+    // S = Q K^T: 16 rows x kKeysTc keys per warp (kKT8 n8 tiles).
+    float s[kKT8][4];
 #pragma unroll
-    for (int n = 0; n < 8; n++) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+    for (int n = 0; n < kKT8; n++) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
     // Per k16 step: every fragment first, then the three products of all
-    // eight tiles in turn (eight independent accumulation chains).
+    // tiles in turn (kKT8 independent accumulation chains).
 #pragma unroll
     for (int ks = 0; ks < KS; ks++) {
-      uint32_t ah[4], al[4], bh[4][4], bl[4][4];
+      uint32_t ah[4], al[4], bh[kKT16][4], bl[kKT16][4];
       ldsm4(saddr(Qh + qoff + ks * 16), ah);
       ldsm4(saddr(Ql + qoff + ks * 16), al);
 #pragma unroll
-      for (int n = 0; n < 4; n++) {
+      for (int n = 0; n < kKT16; n++) {
         ldsm4(saddr(Kh + koff + n * 16 * LD + ks * 16), bh[n]);
         ldsm4(saddr(Kl + koff + n * 16 * LD + ks * 16), bl[n]);
       }
 #pragma unroll
-      for (int n = 0; n < 4; n++) {
+      for (int n = 0; n < kKT16; n++) {
         mma(s[2 * n], ah, bh[n][0], bh[n][1]);
         mma(s[2 * n + 1], ah, bh[n][2], bh[n][3]);
       }
 #pragma unroll
-      for (int n = 0; n < 4; n++) {
+      for (int n = 0; n < kKT16; n++) {
         mma(s[2 * n], ah, bl[n][0], bl[n][1]);
         mma(s[2 * n + 1], ah, bl[n][2], bl[n][3]);
       }
 #pragma unroll
-      for (int n = 0; n < 4; n++) {
+      for (int n = 0; n < kKT16; n++) {
         mma(s[2 * n], al, bh[n][0], bh[n][1]);
         mma(s[2 * n + 1], al, bh[n][2], bh[n][3]);
       }
     }
 
     // Scale, causal mask, online softmax (rows A and B of this lane; the
-    // four lanes of a row hold its 64 keys).
+    // four lanes of a row hold its kKeysTc keys).
     float mxA = -INFINITY, mxB = -INFINITY;
 #pragma unroll
-    for (int n = 0; n < 8; n++) {
+    for (int n = 0; n < kKT8; n++) {
       const int key = k0 + n * 8 + 2 * c;
       s[n][0] = (key <= posA) ? s[n][0] / div : -INFINITY;
       s[n][1] = (key + 1 <= posA) ? s[n][1] / div : -INFINITY;
@@ -261,7 +263,7 @@ __global__ void __launch_bounds__(128) k_attn_prefill_tc(AttnPrefillArgs a) {
       o[n][3] *= cB;
     }
 #pragma unroll
-    for (int n = 0; n < 8; n++) {
+    for (int n = 0; n < kKT8; n++) {
       s[n][0] = (s[n][0] == -INFINITY) ? 0.f : expf(s[n][0] - nA);
       s[n][1] = (s[n][1] == -INFINITY) ? 0.f : expf(s[n][1] - nA);
       s[n][2] = (s[n][2] == -INFINITY) ? 0.f : expf(s[n][2] - nB);
@@ -272,7 +274,7 @@ __global__ void __launch_bounds__(128) k_attn_prefill_tc(AttnPrefillArgs a) {
 
     // O += P V: k16 step j = keys 16 j .. 16 j + 15 (S tiles 2j, 2j + 1).
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
+    for (int j = 0; j < kKT16; j++) {
       uint32_t ph[4], pl[4];
       split_pair(s[2 * j][0], s[2 * j][1], ph[0], pl[0]);
       split_pair(s[2 * j][2], s[2 * j][3], ph[1], pl[1]);
