@@ -38,7 +38,10 @@ namespace {
 constexpr int BM = 128;  // weight rows per tile
 constexpr int BK = 64;   // K per stage
 constexpr int kWTileBytes = BM * BK * 2;  // 16 KB
-constexpr int kSmemBudget = 200 * 1024;
+// Two CTAs per SM (each with its own 2-4 stages and 2*BN TMEM columns,
+// 512 in all for BN = 128): one CTA's epilogue and set-up overlap the
+// other's main loop.
+constexpr int kSmemBudget = 112 * 1024;
 constexpr int kThreads = 192;
 constexpr unsigned long long kTimeoutNs = 2000000000ULL;
 
