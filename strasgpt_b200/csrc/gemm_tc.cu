@@ -423,16 +423,32 @@ void tc_split(const float* x, int ldx, int T, int K, uint16_t* hi, uint16_t* lo,
   launch(k_split_hi_lo, dim3(blocks), dim3(256), 0, s, x, ldx, T, K, hi, lo);
 }
 
+// Resident CTAs of the current device: two per SM (kSmemBudget), the SM
+// count read once per device.
+int resident_ctas() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 2 * 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cached[dev] = 2 * n;
+  }
+  return cached[dev];
+}
+
 int tc_width(int rows, int T) {
   // Streaming-bound model: time ~ waves x bytes per stage; ties go to the
   // wider tile.
   const int rt = (rows + BM - 1) / BM;
+  const long per_wave = resident_ctas();
   int best = 0;
   long best_cost = 0;
   for (int i = 2; i >= 0; i--) {
     const int bn = kWidths[i];
     const long ctas = (long)rt * ((T + bn - 1) / bn);
-    const long waves = (ctas + 147) / 148;
+    const long waves = (ctas + per_wave - 1) / per_wave;
     const long cost = waves * (kWTileBytes + 2L * bn * BK * 2);
     if (best == 0 || cost < best_cost) {
       best = bn;
